@@ -1,0 +1,174 @@
+/*
+ * p2p_attn.h -- C ABI of the B200 (sm_100a) attention library for the LFM2.5-VL engine.
+ *
+ * The library replaces the three attention shaders of the reference engine and the buffer
+ * plumbing around them:
+ *   QK_PREP      src/scripts/lfm-engine/kernels.js:216-266   -> p2p_qk_prep
+ *   ATTN         src/scripts/lfm-engine/kernels.js:268-319   -> p2p_attn (prefill and decode)
+ *   QK_PREP+ATTN at M=1 for every attention layer of a step  -> p2p_decode_step
+ *   ATTN over many independent sequences (ragged KV cache)   -> p2p_attn_decode_ragged
+ *   VISION_ATTN  src/scripts/lfm-engine/vision-kernels.js:176-258 -> p2p_attn_bidir
+ *   ropeTable    src/scripts/lfm-engine/engine.js:60-71      -> p2p_rope_table
+ *   meta buffer  src/scripts/lfm-engine/engine.js:144,388,422 -> p2p_meta / p2p_meta_write
+ *   KV cache     src/scripts/lfm-engine/engine.js:152-165 (alloc), :274-304 (growth)
+ *                                                            -> p2p_kv_*
+ *
+ * Layouts are the reference's (row-major, f16 unless dtype says otherwise):
+ *   qkv row      [Hq*D | Hkv*D | Hkv*D]      (kernels.js:219, engine.js:202-204)
+ *   q / out      [M][ld] with head h at column h*D           (kernels.js:263, :317)
+ *   K/V cache    [cap][Hkv][D] token-major, one K and one V buffer per layer (kernels.js:219)
+ *   norm weights [q_norm(D) | k_norm(D)]     (engine.js:205-212)
+ *   rope         [max_ctx][D] = [cos(D/2) | sin(D/2)] per position (engine.js:60-71)
+ *   meta         uint32[4] = [pos0, M, step, 0] in device memory (engine.js:144, :388)
+ *   vision q/k/v [B][S][ld] with head h at column h*D         (vision-kernels.js:198)
+ *
+ * Conventions: every call is asynchronous on the given CUDA stream (passed as void*; NULL
+ * means the context's own stream).  A context is not thread-safe; use one per host thread.
+ * Calls return a p2p_status and never abort; p2p_last_error() describes the last failure.
+ * head_dim must be 64 (the reference's only head size); num_heads % num_kv_heads == 0 and
+ * num_heads / num_kv_heads in {1, 2, 4, 8}.
+ */
+#ifndef P2P_ATTN_H
+#define P2P_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define P2P_ATTN_ABI_VERSION 1
+
+typedef enum p2p_status {
+  P2P_OK = 0,
+  P2P_ERR_INVALID_ARG = 1, /* bad shape, null pointer, misaligned buffer, bad dtype */
+  P2P_ERR_OOM = 2,         /* device allocation failed (engine.js:280-286 error scope) */
+  P2P_ERR_KV_FULL = 3,     /* KV cache cannot hold the request (engine.js:418-421 'kv_full') */
+  P2P_ERR_CUDA = 4,        /* a CUDA runtime call failed */
+  P2P_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up */
+  P2P_ERR_NCCL = 6,        /* a collective failed */
+  P2P_ERR_UNSUPPORTED = 7  /* valid request this build does not implement (e.g. head_dim != 64) */
+} p2p_status;
+
+typedef enum p2p_dtype { P2P_F16 = 0, P2P_F32 = 1 } p2p_dtype;
+
+/* Uniform parameters of one attention layer (the WGSL constants and overrides:
+ * kernels.js:268 (16/8/64, 0.125), vision-kernels.js:182-185 (S, NUM_HEADS, HEAD_DIM, SCALE)). */
+typedef struct p2p_attn_params {
+  int32_t num_heads;    /* Hq  (reference decoder 16, LFM2.5-1.2B 32, vision 12) */
+  int32_t num_kv_heads; /* Hkv (reference 8; vision: equal to num_heads) */
+  int32_t head_dim;     /* D = 64 */
+  float scale;          /* multiplies f32(q); 0 selects 1/sqrt(D) = 0.125 */
+  float eps;            /* q/k RMSNorm epsilon (kernels.js:252: 1e-5); 0 selects 1e-5 */
+  int32_t dtype;        /* p2p_dtype of q/k/v/out/cache/rope; P2P_F32 only for decode */
+} p2p_attn_params;
+
+typedef struct p2p_ctx p2p_ctx;
+typedef struct p2p_kv p2p_kv;
+
+int p2p_abi_version(void);
+const char* p2p_status_string(p2p_status s);
+
+/* Context: owns a CUDA stream, the split-KV workspace and the meta buffer on `device`. */
+p2p_status p2p_ctx_create(int device, p2p_ctx** out);
+p2p_status p2p_ctx_destroy(p2p_ctx* ctx);
+const char* p2p_last_error(const p2p_ctx* ctx);
+void* p2p_ctx_stream(p2p_ctx* ctx); /* the context's cudaStream_t */
+/* Waits for `stream`, then reports device-side refusals since the last p2p_sync (a position
+ * read from meta_dev beyond the cache returns P2P_ERR_KV_FULL; the kernel skipped that work). */
+p2p_status p2p_sync(p2p_ctx* ctx, void* stream);
+
+/* engine.js:60-71: builds (once per (max_ctx, D, theta, dtype)) the table
+ * rope[p][i] = cos(p * theta^(-i/(D/2))), rope[p][D/2+i] = sin(...), evaluated in double and
+ * rounded through f32 to the storage type; returns a device pointer owned by the context. */
+p2p_status p2p_rope_table(p2p_ctx* ctx, int32_t max_ctx, int32_t head_dim, double theta,
+                          int32_t dtype, const void** dev_table);
+
+/* engine.js:144: the device meta buffer [pos0, M, step, 0]; p2p_meta_write is the
+ * queue.writeBuffer of engine.js:388/408/422 (an async 16-byte copy on `stream`). */
+p2p_status p2p_meta(p2p_ctx* ctx, uint32_t** dev_meta);
+p2p_status p2p_meta_write(p2p_ctx* ctx, uint32_t pos0, uint32_t m_tokens, uint32_t step,
+                          void* stream);
+
+/* engine.js:152-165: one K and one V buffer [cap][Hkv][D] per attention layer. */
+p2p_status p2p_kv_create(p2p_ctx* ctx, int32_t n_layers, int32_t num_kv_heads,
+                         int32_t head_dim, int64_t cap_tokens, int32_t dtype, p2p_kv** out);
+p2p_status p2p_kv_destroy(p2p_kv* kv);
+/* engine.js:274-304: if need > capacity, grow in steps of grow_tokens (at most max_tokens),
+ * copying the old rows; returns P2P_ERR_KV_FULL when need > max_tokens and P2P_ERR_OOM when
+ * the allocation fails (the old cache is then kept).  Pointers change on growth. */
+p2p_status p2p_kv_ensure_capacity(p2p_kv* kv, int64_t need_tokens, int64_t grow_tokens,
+                                  int64_t max_tokens, void* stream);
+int64_t p2p_kv_capacity(const p2p_kv* kv);
+void* p2p_kv_k(const p2p_kv* kv, int32_t layer);
+void* p2p_kv_v(const p2p_kv* kv, int32_t layer);
+
+/* kernels.js:216-266 (QK_PREP, dispatched (Hq+2Hkv, M) at engine.js:221): for token m at
+ * pos = pos0 + m, per-head RMSNorm of q and k (eps, weights norm_w = [q(D) | k(D)], result
+ * rounded to f16), rotate-half RoPE with the f16 table, rotated q to q_out, rotated k and raw
+ * v to cache row pos.  norm_w NULL skips the norm.  pos0 is read from meta_dev[0] on the
+ * device when meta_dev is not NULL (then the host pos0 argument is ignored).  kv_cap_tokens
+ * is the number of rows the cache buffers hold: a host pos0 + M beyond it returns
+ * P2P_ERR_KV_FULL; a device-side position beyond it is skipped and reported by p2p_sync. */
+p2p_status p2p_qk_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const void* qkv,
+                       int64_t ld_qkv, const void* norm_w, const void* rope, void* q_out,
+                       int64_t ld_q, void* k_cache, void* v_cache, int64_t kv_cap_tokens,
+                       const uint32_t* meta_dev, int32_t pos0, int32_t m_tokens, void* stream);
+
+/* kernels.js:268-319 (ATTN, dispatched (Hq, M) at engine.js:222): causal GQA of M rotated
+ * query rows at positions pos0..pos0+M-1 over cache keys 0..pos, kv head h / (Hq/Hkv),
+ * out = f16(softmax(scale * q.k) v).  M == 1 runs the split-KV decode kernel; M > 1 runs the
+ * tcgen05 flash-attention kernel.  kv_cap_tokens is the number of rows the cache buffers
+ * hold (bounds the work grid when pos0 comes from meta_dev). */
+p2p_status p2p_attn(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q, int64_t ld_q,
+                    const void* k_cache, const void* v_cache, int64_t kv_cap_tokens, void* out,
+                    int64_t ld_o, const uint32_t* meta_dev, int32_t pos0, int32_t m_tokens,
+                    void* stream);
+
+/* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to
+ * P2P_MAX_LAYERS attention layers in ONE launch: for each layer the new token's qkv row is
+ * normed/rotated, its k/v are appended at row pos, and its Hq output rows are written.
+ * Layers are independent (each layer's q comes from its own qkv row). */
+#define P2P_MAX_LAYERS 16
+typedef struct p2p_decode_layer {
+  const void* qkv;    /* [Hq*D + 2*Hkv*D] row of the new token */
+  const void* norm_w; /* [q(D) | k(D)] or NULL */
+  void* k_cache;      /* [cap][Hkv][D] */
+  void* v_cache;
+  void* out;          /* [Hq*D] */
+} p2p_decode_layer;
+p2p_status p2p_decode_step(p2p_ctx* ctx, const p2p_attn_params* prm, int32_t n_layers,
+                           const p2p_decode_layer* layers, const void* rope,
+                           int64_t kv_cap_tokens, const uint32_t* meta_dev, int32_t pos,
+                           void* stream);
+
+/* Batched decode over nseq independent sequences sharing one cache buffer pair
+ * [rows][Hkv][D]: sequence i owns rows offsets[i] .. offsets[i]+past[i] and its new token
+ * goes to row offsets[i]+past[i].  With fused_prep != 0, qkv rows [nseq][ld_qkv] are
+ * normed/rotated and the new k/v appended (as p2p_decode_step); with fused_prep == 0, qkv
+ * holds already-rotated q rows [nseq][ld_qkv] and the new k/v must already be in the cache.
+ * offsets and past are device int32 arrays; max_past bounds past[i] for grid sizing only
+ * (a longer sequence is still handled correctly, with longer splits). */
+p2p_status p2p_attn_decode_ragged(p2p_ctx* ctx, const p2p_attn_params* prm, const void* qkv,
+                                  int64_t ld_qkv, const void* norm_w, const void* rope,
+                                  void* k_cache, void* v_cache, const int32_t* offsets,
+                                  const int32_t* past, int32_t nseq, int32_t max_past,
+                                  int32_t fused_prep, void* out, int64_t ld_o, void* stream);
+
+/* vision-kernels.js:176-258 (VISION_ATTN, dispatched (NUM_HEADS, S) at vision.js:271-276),
+ * batched: out[b] = softmax(scale * q[b] k[b]^T) v[b] per head, no mask, tcgen05 kernel.
+ * q/k/v/out are [batch][s_tokens][ld] with head h at column h*D. */
+p2p_status p2p_attn_bidir(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q,
+                          const void* k, const void* v, void* out, int64_t ld, int32_t batch,
+                          int32_t s_tokens, void* stream);
+
+/* Test hook, no counterpart in the reference: cap this process's device allocations made by
+ * the library at `bytes` (< 0 removes the cap), so the P2P_ERR_OOM paths can be exercised
+ * without exhausting a shared GPU. */
+p2p_status p2p_debug_set_alloc_limit(int64_t bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,188 @@
+"""ctypes bindings for the CPU checker (TEST INFRASTRUCTURE ONLY).
+
+Loads oracle/libp2poracle.so (the C++ restatement of the reference path) and, when it has
+been built, oracle/_ref/libp2pref.so (the reference's own WGSL shaders translated to C++ by
+oracle/wgsl2cpp.py).  Only tests/, __graft_entry__.smoke() and bench.py's CPU legs import
+this module; the product library never does.
+
+Arrays are numpy: float16 for f16 storage (passed as their binary16 bit patterns), float32
+for the fp32 case, int64/int32 for offsets and lengths.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+_DIR = Path(__file__).resolve().parent
+_LIB = None
+_REF = None
+
+_p = C.c_void_p
+_i = C.c_int
+_i64 = C.c_int64
+_f = C.c_float
+_d = C.c_double
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "oracle inputs must be C-contiguous"
+    return a.ctypes.data
+
+
+def lib():
+    """The restatement library; builds it with make if it is missing."""
+    global _LIB
+    if _LIB is None:
+        path = _DIR / "libp2poracle.so"
+        if not path.exists():
+            import subprocess
+
+            subprocess.run(["make", "-C", str(_DIR), "libp2poracle.so"], check=True)
+        L = C.CDLL(str(path))
+        L.p2p_or_f32_to_f16.restype = C.c_uint16
+        L.p2p_or_f32_to_f16.argtypes = [_f]
+        L.p2p_or_f16_to_f32.restype = _f
+        L.p2p_or_f16_to_f32.argtypes = [C.c_uint16]
+        L.p2p_or_f32_to_f16_array.argtypes = [_p, _p, _i64]
+        L.p2p_or_f16_to_f32_array.argtypes = [_p, _p, _i64]
+        L.p2p_or_rope_table.argtypes = [_i, _i, _d, _p]
+        L.p2p_or_rope_table_f32.argtypes = [_i, _i, _d, _p]
+        L.p2p_or_qk_prep_h.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _i64, _p, _p, _i, _i]
+        L.p2p_or_qk_prep_f.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _i64, _p, _p, _i, _i]
+        L.p2p_or_attn_h.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _i64, _i, _i]
+        L.p2p_or_attn_f.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _i64, _i, _i]
+        L.p2p_or_attn_ragged_h.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _p, _i, _p, _i64]
+        L.p2p_or_vision_attn_h.argtypes = [_i, _i, _f, _i, _i, _p, _p, _p, _p, _i64]
+        L.p2p_or_attn_exact.argtypes = [_i, _i, _i, _d, _p, _i64, _p, _p, _p, _i64, _i, _i]
+        L.p2p_or_set_threads.restype = _i
+        L.p2p_or_set_threads.argtypes = [_i]
+        _LIB = L
+    return _LIB
+
+
+def ref_available() -> bool:
+    return (_DIR / "_ref" / "libp2pref.so").exists()
+
+
+def ref():
+    """The translated reference shaders (oracle/_ref); raises if they were never built."""
+    global _REF
+    if _REF is None:
+        path = _DIR / "_ref" / "libp2pref.so"
+        if not path.exists():
+            raise FileNotFoundError(f"{path} not built (needs the reference sources)")
+        L = C.CDLL(str(path))
+        for name in ("QK_PREP", "ATTN", "VISION_ATTN"):
+            fn = getattr(L, f"ref_{name}")
+            fn.restype = _i
+            fn.argtypes = [_p, _p, C.c_uint32, C.c_uint32, C.c_uint32]
+        _REF = L
+    return _REF
+
+
+def set_threads(n: int = 0) -> int:
+    return lib().p2p_or_set_threads(int(n))
+
+
+# ---- f16 helpers (engine.js:28-50, 331-345) ----------------------------------------------
+
+def f32_to_f16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, np.float16)
+    lib().p2p_or_f32_to_f16_array(_ptr(x), _ptr(out), x.size)
+    return out
+
+
+def f16_to_f32(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    out = np.empty(x.shape, np.float32)
+    lib().p2p_or_f16_to_f32_array(_ptr(x), _ptr(out), x.size)
+    return out
+
+
+def rope_table(max_ctx: int, d: int = 64, theta: float = 1e6, f32: bool = False) -> np.ndarray:
+    if f32:
+        out = np.empty((max_ctx, d), np.float32)
+        lib().p2p_or_rope_table_f32(max_ctx, d, theta, _ptr(out))
+    else:
+        out = np.empty((max_ctx, d), np.float16)
+        lib().p2p_or_rope_table(max_ctx, d, theta, _ptr(out))
+    return out
+
+
+# ---- the three shaders, restated ----------------------------------------------------------
+
+def qk_prep(hq, hkv, d, qkv, nw, rope, q_out, kc, vc, pos0, m_tokens, eps=1e-5):
+    """kernels.js:216-266 in place on q_out / kc / vc (f16 or f32 storage)."""
+    fn = lib().p2p_or_qk_prep_f if qkv.dtype == np.float32 else lib().p2p_or_qk_prep_h
+    fn(hq, hkv, d, eps, _ptr(qkv), qkv.shape[-1], _ptr(nw), _ptr(rope), _ptr(q_out),
+       q_out.shape[-1], _ptr(kc), _ptr(vc), pos0, m_tokens)
+
+
+def attn(hq, hkv, d, q, kc, vc, out, pos0, m_tokens, scale=0.125):
+    """kernels.js:268-319 (f16 or f32 storage)."""
+    fn = lib().p2p_or_attn_f if q.dtype == np.float32 else lib().p2p_or_attn_h
+    fn(hq, hkv, d, scale, _ptr(q), q.shape[-1], _ptr(kc), _ptr(vc), _ptr(out), out.shape[-1],
+       pos0, m_tokens)
+
+
+def attn_ragged(hq, hkv, d, q, kc, vc, offsets, past, out, scale=0.125):
+    offsets = np.ascontiguousarray(offsets, dtype=np.int64)
+    past = np.ascontiguousarray(past, dtype=np.int32)
+    lib().p2p_or_attn_ragged_h(hq, hkv, d, scale, _ptr(q), q.shape[-1], _ptr(kc), _ptr(vc),
+                               _ptr(offsets), _ptr(past), len(past), _ptr(out), out.shape[-1])
+
+
+def vision_attn(nh, d, q, k, v, out, scale=0.125):
+    """vision-kernels.js:176-258; q/k/v/out are [B][S][NH*D] float16."""
+    b, s, ld = q.shape
+    lib().p2p_or_vision_attn_h(nh, d, scale, b, s, _ptr(q), _ptr(k), _ptr(v), _ptr(out), ld)
+
+
+def attn_exact(hq, hkv, d, q, kc, vc, pos0, m_tokens, scale=0.125):
+    out = np.empty((m_tokens, hq * d), np.float64)
+    lib().p2p_or_attn_exact(hq, hkv, d, scale, _ptr(q), q.shape[-1], _ptr(kc), _ptr(vc),
+                            _ptr(out), out.shape[-1], pos0, m_tokens)
+    return out
+
+
+# ---- the reference's own shaders (translated), fixed reference shapes ---------------------
+
+def _bind(*arrays):
+    ptrs = (C.c_void_p * len(arrays))(*[_ptr(a) for a in arrays])
+    return ptrs
+
+
+def ref_qk_prep(qkv, nwb, qout, kc, vc, meta, rope, m_tokens):
+    """QK_PREP dispatched as engine.js:221 does: grid (32, M).  Reference shapes only:
+    qkv [M][2048], qout [M][1024], caches [cap][8][64]."""
+    b = _bind(qkv, nwb, qout, kc, vc, meta, rope)
+    rc = ref().ref_QK_PREP(b, None, 32, m_tokens, 1)
+    if rc != 0:
+        raise RuntimeError("QK_PREP: non-uniform barrier")
+
+
+def ref_attn(q, kc, vc, out, meta, m_tokens):
+    """ATTN dispatched as engine.js:222 does: grid (16, M)."""
+    b = _bind(q, kc, vc, out, meta)
+    rc = ref().ref_ATTN(b, None, 16, m_tokens, 1)
+    if rc != 0:
+        raise RuntimeError("ATTN: non-uniform barrier")
+
+
+def ref_vision_attn(q, k, v, out, s_tokens=1024, num_heads=12, scale=0.125):
+    """VISION_ATTN dispatched as vision.js:271-276 does: grid (NUM_HEADS, S), one image."""
+    b = _bind(q, k, v, out)
+    ov = (C.c_double * 4)(float(s_tokens), float(num_heads), 64.0, float(scale))
+    rc = ref().ref_VISION_ATTN(b, ov, num_heads, s_tokens, 1)
+    if rc != 0:
+        raise RuntimeError("VISION_ATTN: non-uniform barrier")
+
+
+def threads_env() -> int:
+    return int(os.environ.get("OMP_NUM_THREADS", "0") or 0)

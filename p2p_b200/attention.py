@@ -1,0 +1,263 @@
+"""Host-side mirror of the reference engine's attention plumbing, over the C ABI.
+
+The reference engine (src/scripts/lfm-engine/engine.js, vision.js) builds, for each attention
+layer, a QK_PREP op and an ATTN op bound to [qkv, norm weights, qrot, K cache, V cache, meta,
+rope] and dispatches them per prefill chunk and per decode step; the vision encoder dispatches
+VISION_ATTN on separate q/k/v buffers.  This module keeps those operators, their buffer
+layouts, their argument meaning and their error behaviour (KV growth failure -> 'kv_full'),
+with device memory held in torch tensors and every kernel in libp2pattn.so:
+
+    Context.qk_prep        QK_PREP   kernels.js:216-266, dispatched engine.js:213-221
+    Context.attn           ATTN      kernels.js:268-319, dispatched engine.js:214-222
+    Context.decode_step    QK_PREP + ATTN at M=1 for all attention layers (engine.js:425-429)
+    Context.attn_decode_ragged  ATTN at M=1 over many sequences sharing one cache
+    Context.attn_bidir     VISION_ATTN vision-kernels.js:176-258, dispatched vision.js:271-276
+    KVCache                K/V buffers engine.js:152-165 and ensureCapacity engine.js:274-304
+    LfmAttention           the per-layer op pair + meta + rope + KV cache of createLfmEngine
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import AttnParams, DecodeLayer, check, lib
+
+HEAD_DIM = 64
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream) -> C.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+@dataclass
+class Params:
+    """Uniform parameters of one attention layer (kernels.js:268: 16 q heads, 8 kv heads,
+    head_dim 64, scale 0.125; vision-kernels.js:182-185: S, NUM_HEADS, HEAD_DIM, SCALE)."""
+
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int = HEAD_DIM
+    scale: float = 0.0  # 0 -> 1/sqrt(head_dim)
+    eps: float = 1e-5
+    dtype: torch.dtype = torch.float16
+
+    def c(self) -> AttnParams:
+        dt = {torch.float16: _lib.P2P_F16, torch.float32: _lib.P2P_F32}[self.dtype]
+        return AttnParams(self.num_heads, self.num_kv_heads, self.head_dim, self.scale,
+                          self.eps, dt)
+
+    @property
+    def qkv_width(self) -> int:
+        return (self.num_heads + 2 * self.num_kv_heads) * self.head_dim
+
+
+class Context:
+    """One p2p_ctx: a CUDA device, its split-KV workspace and its meta buffer."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        check(lib.p2p_ctx_create(device, C.byref(h)))
+        self.h = h
+        self.device = device
+        m = C.c_void_p()
+        check(lib.p2p_meta(self.h, C.byref(m)), self.h)
+        self.meta_ptr = m
+        self._rope = {}
+
+    def close(self):
+        if self.h:
+            lib.p2p_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _chk(self, status):
+        check(status, self.h)
+
+    # -- engine.js:60-71, :144-146 ----------------------------------------------------------
+    def rope_table(self, max_ctx: int, head_dim: int = HEAD_DIM, theta: float = 1e6,
+                   dtype: torch.dtype = torch.float16) -> C.c_void_p:
+        dt = _lib.P2P_F16 if dtype == torch.float16 else _lib.P2P_F32
+        p = C.c_void_p()
+        self._chk(lib.p2p_rope_table(self.h, max_ctx, head_dim, theta, dt, C.byref(p)))
+        return p
+
+    def meta_write(self, pos0: int, m_tokens: int, step: int = 0, stream=None):
+        self._chk(lib.p2p_meta_write(self.h, pos0, m_tokens, step, _stream(stream)))
+
+    def sync(self, stream=None):
+        self._chk(lib.p2p_sync(self.h, _stream(stream)))
+
+    # -- the shader entry points ----------------------------------------------------------------
+    def qk_prep(self, prm: Params, qkv: torch.Tensor, norm_w: Optional[torch.Tensor], rope,
+                q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+                pos0: int = 0, m_tokens: Optional[int] = None, use_meta: bool = False,
+                stream=None):
+        m = qkv.shape[0] if m_tokens is None else m_tokens
+        self._chk(lib.p2p_qk_prep(
+            self.h, C.byref(prm.c()), _ptr(qkv), qkv.stride(0), _ptr(norm_w),
+            rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(q_out), q_out.stride(0),
+            _ptr(k_cache), _ptr(v_cache), k_cache.shape[0], self.meta_ptr if use_meta else None,
+            pos0, m, _stream(stream)))
+
+    def attn(self, prm: Params, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+             out: torch.Tensor, *, pos0: int = 0, m_tokens: Optional[int] = None,
+             use_meta: bool = False, stream=None):
+        m = q.shape[0] if m_tokens is None else m_tokens
+        self._chk(lib.p2p_attn(
+            self.h, C.byref(prm.c()), _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache),
+            k_cache.shape[0], _ptr(out), out.stride(0), self.meta_ptr if use_meta else None,
+            pos0, m, _stream(stream)))
+
+    def decode_step(self, prm: Params, layers: Sequence[tuple], rope, kv_cap: int, *,
+                    pos: int = 0, use_meta: bool = False, stream=None):
+        """layers: (qkv_row, norm_w or None, k_cache, v_cache, out_row) per attention layer."""
+        arr = (DecodeLayer * len(layers))()
+        for i, (qkv, nw, kc, vc, out) in enumerate(layers):
+            arr[i] = DecodeLayer(qkv.data_ptr(), nw.data_ptr() if nw is not None else None,
+                                 kc.data_ptr(), vc.data_ptr(), out.data_ptr())
+        self._chk(lib.p2p_decode_step(
+            self.h, C.byref(prm.c()), len(layers), arr,
+            rope if isinstance(rope, C.c_void_p) else _ptr(rope), kv_cap,
+            self.meta_ptr if use_meta else None, pos, _stream(stream)))
+
+    def attn_decode_ragged(self, prm: Params, qkv: torch.Tensor, norm_w, rope,
+                           k_cache: torch.Tensor, v_cache: torch.Tensor, offsets: torch.Tensor,
+                           past: torch.Tensor, out: torch.Tensor, *, max_past: int,
+                           fused_prep: bool = True, stream=None):
+        assert offsets.dtype == torch.int32 and past.dtype == torch.int32
+        self._chk(lib.p2p_attn_decode_ragged(
+            self.h, C.byref(prm.c()), _ptr(qkv), qkv.stride(0), _ptr(norm_w),
+            rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(k_cache), _ptr(v_cache),
+            _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep), _ptr(out),
+            out.stride(0), _stream(stream)))
+
+    def attn_bidir(self, prm: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                   out: torch.Tensor, stream=None):
+        """q/k/v/out: [B][S][ld] (vision-kernels.js:198 layout)."""
+        b, s, ld = q.shape
+        self._chk(lib.p2p_attn_bidir(self.h, C.byref(prm.c()), _ptr(q), _ptr(k), _ptr(v),
+                                     _ptr(out), ld, b, s, _stream(stream)))
+
+
+class KVCache:
+    """engine.js:152-165: one K and one V buffer [cap][Hkv][D] per attention layer, grown by
+    ensure_capacity as engine.js:274-304 does (allocate, copy, rebind, free)."""
+
+    def __init__(self, ctx: Context, n_layers: int, num_kv_heads: int, cap_tokens: int,
+                 dtype: torch.dtype = torch.float16):
+        self.ctx = ctx
+        self.n_layers = n_layers
+        self.num_kv_heads = num_kv_heads
+        self.dtype = dtype
+        h = C.c_void_p()
+        dt = _lib.P2P_F16 if dtype == torch.float16 else _lib.P2P_F32
+        ctx._chk(lib.p2p_kv_create(ctx.h, n_layers, num_kv_heads, HEAD_DIM, cap_tokens, dt,
+                                   C.byref(h)))
+        self.h = h
+
+    @property
+    def capacity(self) -> int:
+        return lib.p2p_kv_capacity(self.h)
+
+    def ensure_capacity(self, need: int, grow: int, max_tokens: int, stream=None) -> bool:
+        """True when the cache holds `need` tokens; False for 'kv_full' or OOM
+        (engine.js:274-286 returns false in both cases)."""
+        st = lib.p2p_kv_ensure_capacity(self.h, need, grow, max_tokens, _stream(stream))
+        if st in (_lib.P2P_ERR_KV_FULL, _lib.P2P_ERR_OOM):
+            return False
+        self.ctx._chk(st)
+        return True
+
+    def _view(self, ptr: int) -> torch.Tensor:
+        n = self.capacity * self.num_kv_heads * HEAD_DIM
+        es = 2 if self.dtype == torch.float16 else 4
+        # Wrap the library-owned buffer without copying (the KVCache keeps it alive).
+        t = _from_device_ptr(ptr, n * es, self.ctx.device)
+        return t.view(self.dtype).view(self.capacity, self.num_kv_heads, HEAD_DIM)
+
+    def k(self, layer: int) -> torch.Tensor:
+        return self._view(lib.p2p_kv_k(self.h, layer))
+
+    def v(self, layer: int) -> torch.Tensor:
+        return self._view(lib.p2p_kv_v(self.h, layer))
+
+    def close(self):
+        if self.h:
+            lib.p2p_kv_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _CudaArrayView:
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {
+            "shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+            "strides": None,
+        }
+
+
+def _from_device_ptr(ptr: int, nbytes: int, device: int) -> torch.Tensor:
+    with torch.cuda.device(device):
+        return torch.as_tensor(_CudaArrayView(ptr, nbytes), device=f"cuda:{device}")
+
+
+class LfmAttention:
+    """The attention half of createLfmEngine (engine.js:73-304) for a decoder with
+    `n_layers` attention layers: RoPE table, meta buffer, KV cache with growth, and the
+    QK_PREP/ATTN pair per layer, dispatched per prefill chunk or per decode step."""
+
+    KV_INIT_BYTES = 20 * 1024 * 1024  # engine.js:14
+    KV_GROW_BYTES = 2 * 1024 * 1024   # engine.js:15
+
+    def __init__(self, ctx: Context, prm: Params, n_layers: int, max_ctx: int = 4096,
+                 rope_theta: float = 1e6, kv_init_bytes: int = KV_INIT_BYTES,
+                 kv_grow_bytes: int = KV_GROW_BYTES):
+        self.ctx, self.prm, self.n_layers, self.max_ctx = ctx, prm, n_layers, max_ctx
+        self.kv_bytes_per_token = n_layers * 2 * prm.num_kv_heads * prm.head_dim * 2  # :24
+        self.rope = ctx.rope_table(max_ctx, prm.head_dim, rope_theta)
+        self.kv = KVCache(ctx, n_layers, prm.num_kv_heads,
+                          max(1, kv_init_bytes // self.kv_bytes_per_token))  # :153
+        self.grow_step = max(1, kv_grow_bytes // self.kv_bytes_per_token)   # :272
+
+    def ensure_capacity(self, need: int) -> bool:
+        if need > self.max_ctx:  # engine.js:276
+            return False
+        return self.kv.ensure_capacity(need, self.grow_step, self.max_ctx)
+
+    def prefill_layer(self, layer: int, qkv: torch.Tensor, norm_w, q_rot: torch.Tensor,
+                      out: torch.Tensor, pos0: int, stream=None):
+        """QK_PREP then ATTN for one prefill chunk of M = qkv.shape[0] tokens at pos0
+        (engine.js:384-401 writes meta = [s, mc, 0, 0] then dispatches the pair)."""
+        m = qkv.shape[0]
+        kc, vc = self.kv.k(layer), self.kv.v(layer)
+        self.ctx.qk_prep(self.prm, qkv, norm_w, self.rope, q_rot, kc, vc, pos0=pos0,
+                         m_tokens=m, stream=stream)
+        self.ctx.attn(self.prm, q_rot, kc, vc, out, pos0=pos0, m_tokens=m, stream=stream)
+
+    def decode_step(self, qkv_rows: Sequence[torch.Tensor], norm_ws, outs, pos: int,
+                    use_meta: bool = False, stream=None):
+        """All attention layers of one decode step at position `pos` in one launch."""
+        layers = [(qkv_rows[l], norm_ws[l] if norm_ws else None, self.kv.k(l), self.kv.v(l),
+                   outs[l]) for l in range(self.n_layers)]
+        self.ctx.decode_step(self.prm, layers, self.rope, self.kv.capacity, pos=pos,
+                             use_meta=use_meta, stream=stream)

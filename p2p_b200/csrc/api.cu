@@ -1,0 +1,667 @@
+// api.cu -- the extern "C" boundary of libp2pattn.so (declared in include/p2p_attn.h).
+//
+// Host-side responsibilities the reference engine keeps in JavaScript:
+//   - argument validation and error reporting (engine.js:83, :379-380 throw; here statuses)
+//   - the RoPE table (engine.js:60-71) and the meta buffer (engine.js:144, :388, :408, :422)
+//   - per-layer K/V cache buffers and their growth (engine.js:152-165, :274-304)
+//   - choosing the launch for each shader dispatch (engine.js:245-259)
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <new>
+#include <string>
+#include <tuple>
+#include <vector>
+
+// The library is built with -fvisibility=hidden; only the declared C ABI is exported.
+#pragma GCC visibility push(default)
+#include "../../include/p2p_attn.h"
+#pragma GCC visibility pop
+#include "kernels.h"
+
+struct p2p_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  uint32_t* meta = nullptr;
+  int32_t* dev_err = nullptr;  // kernels set bits here (kErrPosBeyondCache); read by p2p_sync
+  float* partials = nullptr;
+  size_t partials_bytes = 0;
+  int32_t* counters = nullptr;
+  size_t counters_bytes = 0;
+  std::map<std::tuple<int, int, double, int>, void*> rope;
+  std::string err;
+};
+
+struct p2p_kv {
+  p2p_ctx* ctx = nullptr;
+  int n_layers = 0, hkv = 0, d = 0, dtype = 0;
+  int64_t cap = 0;
+  std::vector<void*> k, v;
+};
+
+namespace {
+
+// Test hook: a device-allocation budget for this process (bytes; <0 = unlimited), used to
+// exercise the OOM path without exhausting the GPU.
+int64_t g_alloc_limit = -1;
+int64_t g_alloc_used = 0;
+std::mutex g_alloc_mu;
+
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+p2p_status fail(p2p_ctx* ctx, p2p_status s, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->err = buf;
+  }
+  return s;
+}
+
+p2p_status cuda_fail(p2p_ctx* ctx, cudaError_t e, const char* what) {
+  return fail(ctx, P2P_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+cudaError_t dev_alloc(void** p, size_t bytes) {
+  {
+    std::lock_guard<std::mutex> lk(g_alloc_mu);
+    if (g_alloc_limit >= 0 && g_alloc_used + int64_t(bytes) > g_alloc_limit) {
+      *p = nullptr;
+      return cudaErrorMemoryAllocation;
+    }
+  }
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e == cudaSuccess) {
+    std::lock_guard<std::mutex> lk(g_alloc_mu);
+    g_alloc_used += int64_t(bytes);
+  }
+  return e;
+}
+
+void dev_free(void* p, size_t bytes) {
+  if (!p) return;
+  cudaFree(p);
+  std::lock_guard<std::mutex> lk(g_alloc_mu);
+  g_alloc_used -= int64_t(bytes);
+}
+
+cudaStream_t pick_stream(p2p_ctx* ctx, void* stream) {
+  return stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+}
+
+size_t elem_bytes(int dtype) { return dtype == P2P_F32 ? 4 : 2; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Shared validation of the uniform parameters.
+p2p_status check_params(p2p_ctx* ctx, const p2p_attn_params* prm, bool allow_f32) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  if (!prm) return fail(ctx, P2P_ERR_INVALID_ARG, "params is NULL");
+  if (prm->head_dim != 64)
+    return fail(ctx, P2P_ERR_UNSUPPORTED, "head_dim %d: only 64 is implemented", prm->head_dim);
+  if (prm->num_heads <= 0 || prm->num_kv_heads <= 0 || prm->num_heads % prm->num_kv_heads)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "num_heads %d / num_kv_heads %d", prm->num_heads,
+                prm->num_kv_heads);
+  const int g = prm->num_heads / prm->num_kv_heads;
+  if (g != 1 && g != 2 && g != 4 && g != 8)
+    return fail(ctx, P2P_ERR_UNSUPPORTED, "group size %d not in {1,2,4,8}", g);
+  if (prm->dtype != P2P_F16 && !(allow_f32 && prm->dtype == P2P_F32))
+    return fail(ctx, P2P_ERR_UNSUPPORTED, "dtype %d not supported by this entry point",
+                prm->dtype);
+  if (!(prm->scale >= 0.f) || !std::isfinite(prm->scale))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "scale must be finite and >= 0");
+  return P2P_OK;
+}
+
+float eff_scale(const p2p_attn_params* prm) {
+  return prm->scale > 0.f ? prm->scale : 1.0f / std::sqrt(float(prm->head_dim));
+}
+float eff_eps(const p2p_attn_params* prm) { return prm->eps > 0.f ? prm->eps : 1e-5f; }
+
+p2p_status ensure_workspace(p2p_ctx* ctx, size_t pbytes, size_t cbytes, cudaStream_t s) {
+  if (pbytes > ctx->partials_bytes) {
+    cudaStreamSynchronize(s);
+    cudaStreamSynchronize(ctx->stream);
+    dev_free(ctx->partials, ctx->partials_bytes);
+    ctx->partials = nullptr;
+    ctx->partials_bytes = 0;
+    void* p = nullptr;
+    if (dev_alloc(&p, pbytes) != cudaSuccess)
+      return fail(ctx, P2P_ERR_OOM, "split-KV workspace of %zu bytes", pbytes);
+    ctx->partials = static_cast<float*>(p);
+    ctx->partials_bytes = pbytes;
+  }
+  if (cbytes > ctx->counters_bytes) {
+    cudaStreamSynchronize(s);
+    cudaStreamSynchronize(ctx->stream);
+    dev_free(ctx->counters, ctx->counters_bytes);
+    ctx->counters = nullptr;
+    ctx->counters_bytes = 0;
+    void* p = nullptr;
+    if (dev_alloc(&p, cbytes) != cudaSuccess)
+      return fail(ctx, P2P_ERR_OOM, "split-KV counters of %zu bytes", cbytes);
+    cudaError_t e = cudaMemsetAsync(p, 0, cbytes, s);
+    if (e != cudaSuccess) {
+      dev_free(p, cbytes);
+      return cuda_fail(ctx, e, "cudaMemsetAsync(counters)");
+    }
+    ctx->counters = static_cast<int32_t*>(p);
+    ctx->counters_bytes = cbytes;
+  }
+  return P2P_OK;
+}
+
+// engine.js:28-50 semantics for the host-built table: double -> f32 (RNE) -> f16 (RNE).
+uint16_t half_bits(float f) {
+  const __half h = __float2half_rn(f);
+  uint16_t b;
+  std::memcpy(&b, &h, 2);
+  return b;
+}
+
+p2p_status run_decode(p2p_ctx* ctx, const p2p_attn_params* prm, p2p::DecodeArgs& a, int mode,
+                      bool fused, int nz, int64_t max_len, cudaStream_t s) {
+  const int hkv = prm->num_kv_heads;
+  const int group = prm->num_heads / hkv;
+  int min_split = 16;
+  const int splits = p2p::decode_max_splits(max_len, hkv, nz, ctx->num_sms, &min_split);
+  p2p_status st = ensure_workspace(ctx, p2p::decode_partials_bytes(splits, hkv, nz, group),
+                                   p2p::decode_counters_bytes(hkv, nz), s);
+  if (st != P2P_OK) return st;
+  a.hq = prm->num_heads;
+  a.hkv = hkv;
+  a.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
+  a.eps = eff_eps(prm);
+  a.min_split = min_split;
+  a.partials = ctx->partials;
+  a.counters = ctx->counters;
+  a.err = ctx->dev_err;
+  cudaError_t e = p2p::launch_decode(a, mode, fused, prm->dtype, splits, nz, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "decode launch");
+  return P2P_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int p2p_abi_version(void) { return P2P_ATTN_ABI_VERSION; }
+
+const char* p2p_status_string(p2p_status s) {
+  switch (s) {
+    case P2P_OK: return "ok";
+    case P2P_ERR_INVALID_ARG: return "invalid argument";
+    case P2P_ERR_OOM: return "out of device memory";
+    case P2P_ERR_KV_FULL: return "kv cache full";
+    case P2P_ERR_CUDA: return "cuda error";
+    case P2P_ERR_TIMEOUT: return "device wait timed out";
+    case P2P_ERR_NCCL: return "nccl error";
+    case P2P_ERR_UNSUPPORTED: return "unsupported";
+  }
+  return "unknown status";
+}
+
+p2p_status p2p_ctx_create(int device, p2p_ctx** out) {
+  if (!out) return P2P_ERR_INVALID_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    cudaGetLastError();
+    return P2P_ERR_CUDA;
+  }
+  p2p_ctx* ctx = new (std::nothrow) p2p_ctx;
+  if (!ctx) return P2P_ERR_OOM;
+  ctx->device = device;
+  DeviceGuard g(device);
+  if (!g.ok) {
+    delete ctx;
+    return P2P_ERR_CUDA;
+  }
+  cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete ctx;
+    return P2P_ERR_CUDA;
+  }
+  void* m = nullptr;
+  if (dev_alloc(&m, 16) != cudaSuccess) {
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return P2P_ERR_OOM;
+  }
+  cudaMemset(m, 0, 16);
+  ctx->meta = static_cast<uint32_t*>(m);
+  void* e = nullptr;
+  if (dev_alloc(&e, sizeof(int32_t)) != cudaSuccess) {
+    dev_free(m, 16);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return P2P_ERR_OOM;
+  }
+  cudaMemset(e, 0, sizeof(int32_t));
+  ctx->dev_err = static_cast<int32_t*>(e);
+  *out = ctx;
+  return P2P_OK;
+}
+
+p2p_status p2p_ctx_destroy(p2p_ctx* ctx) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  for (auto& kv : ctx->rope) cudaFree(kv.second);
+  dev_free(ctx->meta, 16);
+  dev_free(ctx->dev_err, sizeof(int32_t));
+  dev_free(ctx->partials, ctx->partials_bytes);
+  dev_free(ctx->counters, ctx->counters_bytes);
+  cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return P2P_OK;
+}
+
+const char* p2p_last_error(const p2p_ctx* ctx) { return ctx ? ctx->err.c_str() : "no context"; }
+
+void* p2p_ctx_stream(p2p_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+p2p_status p2p_sync(p2p_ctx* ctx, void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaStreamSynchronize(pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+  int32_t flags = 0;
+  e = cudaMemcpy(&flags, ctx->dev_err, sizeof flags, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "reading the device error word");
+  if (flags) {
+    cudaMemset(ctx->dev_err, 0, sizeof flags);
+    if (flags & p2p::kErrPosBeyondCache)
+      return fail(ctx, P2P_ERR_KV_FULL,
+                  "a kernel was given a device-side position beyond its KV cache; that work "
+                  "was skipped");
+  }
+  return P2P_OK;
+}
+
+// Test hook (not part of the reference contract): cap this process's device allocations.
+p2p_status p2p_debug_set_alloc_limit(int64_t bytes) {
+  std::lock_guard<std::mutex> lk(g_alloc_mu);
+  g_alloc_limit = bytes;
+  return P2P_OK;
+}
+
+p2p_status p2p_rope_table(p2p_ctx* ctx, int32_t max_ctx, int32_t head_dim, double theta,
+                          int32_t dtype, const void** dev_table) {
+  if (!ctx || !dev_table) return P2P_ERR_INVALID_ARG;
+  if (max_ctx <= 0 || head_dim <= 0 || head_dim % 2 || !(theta > 0.0))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "rope table: max_ctx %d head_dim %d theta %g",
+                max_ctx, head_dim, theta);
+  if (dtype != P2P_F16 && dtype != P2P_F32)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "rope table dtype %d", dtype);
+  auto key = std::make_tuple(max_ctx, head_dim, theta, dtype);
+  auto it = ctx->rope.find(key);
+  if (it != ctx->rope.end()) {
+    *dev_table = it->second;
+    return P2P_OK;
+  }
+  const int half = head_dim / 2;
+  const size_t n = size_t(max_ctx) * head_dim;
+  std::vector<uint16_t> h16;
+  std::vector<float> h32;
+  if (dtype == P2P_F16) h16.resize(n);
+  else h32.resize(n);
+  for (int p = 0; p < max_ctx; ++p)
+    for (int i = 0; i < half; ++i) {  // engine.js:64-67
+      const double ang = double(p) * std::pow(theta, double(-i) / double(half));
+      const float c = float(std::cos(ang)), s = float(std::sin(ang));
+      const size_t o = size_t(p) * head_dim;
+      if (dtype == P2P_F16) {
+        h16[o + i] = half_bits(c);
+        h16[o + half + i] = half_bits(s);
+      } else {
+        h32[o + i] = c;
+        h32[o + half + i] = s;
+      }
+    }
+  DeviceGuard g(ctx->device);
+  void* d = nullptr;
+  const size_t bytes = n * elem_bytes(dtype);
+  if (dev_alloc(&d, bytes) != cudaSuccess) return fail(ctx, P2P_ERR_OOM, "rope table");
+  cudaError_t e = cudaMemcpy(d, dtype == P2P_F16 ? static_cast<const void*>(h16.data())
+                                                 : static_cast<const void*>(h32.data()),
+                             bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    dev_free(d, bytes);
+    return cuda_fail(ctx, e, "rope upload");
+  }
+  ctx->rope[key] = d;
+  *dev_table = d;
+  return P2P_OK;
+}
+
+p2p_status p2p_meta(p2p_ctx* ctx, uint32_t** dev_meta) {
+  if (!ctx || !dev_meta) return P2P_ERR_INVALID_ARG;
+  *dev_meta = ctx->meta;
+  return P2P_OK;
+}
+
+p2p_status p2p_meta_write(p2p_ctx* ctx, uint32_t pos0, uint32_t m_tokens, uint32_t step,
+                          void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  // A small pageable source: cudaMemcpyAsync stages it before returning, so the local array
+  // may go out of scope immediately.
+  const uint32_t v[4] = {pos0, m_tokens, step, 0u};
+  cudaError_t e =
+      cudaMemcpyAsync(ctx->meta, v, sizeof v, cudaMemcpyHostToDevice, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "meta write");
+  return P2P_OK;
+}
+
+p2p_status p2p_kv_create(p2p_ctx* ctx, int32_t n_layers, int32_t num_kv_heads,
+                         int32_t head_dim, int64_t cap_tokens, int32_t dtype, p2p_kv** out) {
+  if (!ctx || !out) return P2P_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (n_layers <= 0 || num_kv_heads <= 0 || head_dim != 64 || cap_tokens <= 0 ||
+      (dtype != P2P_F16 && dtype != P2P_F32))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "kv_create: layers %d kv_heads %d head_dim %d cap %lld",
+                n_layers, num_kv_heads, head_dim, (long long)cap_tokens);
+  DeviceGuard g(ctx->device);
+  p2p_kv* kv = new (std::nothrow) p2p_kv;
+  if (!kv) return P2P_ERR_OOM;
+  kv->ctx = ctx;
+  kv->n_layers = n_layers;
+  kv->hkv = num_kv_heads;
+  kv->d = head_dim;
+  kv->dtype = dtype;
+  kv->cap = cap_tokens;
+  const size_t bytes = size_t(cap_tokens) * num_kv_heads * head_dim * elem_bytes(dtype);
+  for (int l = 0; l < n_layers; ++l) {
+    void* k = nullptr;
+    void* v = nullptr;
+    if (dev_alloc(&k, bytes) != cudaSuccess || dev_alloc(&v, bytes) != cudaSuccess) {
+      dev_free(k, k ? bytes : 0);
+      for (size_t i = 0; i < kv->k.size(); ++i) {
+        dev_free(kv->k[i], bytes);
+        dev_free(kv->v[i], bytes);
+      }
+      delete kv;
+      return fail(ctx, P2P_ERR_OOM, "kv cache of %zu bytes per buffer", bytes);
+    }
+    kv->k.push_back(k);
+    kv->v.push_back(v);
+  }
+  *out = kv;
+  return P2P_OK;
+}
+
+p2p_status p2p_kv_destroy(p2p_kv* kv) {
+  if (!kv) return P2P_ERR_INVALID_ARG;
+  DeviceGuard g(kv->ctx->device);
+  cudaStreamSynchronize(kv->ctx->stream);
+  const size_t bytes = size_t(kv->cap) * kv->hkv * kv->d * elem_bytes(kv->dtype);
+  for (int l = 0; l < kv->n_layers; ++l) {
+    dev_free(kv->k[l], bytes);
+    dev_free(kv->v[l], bytes);
+  }
+  delete kv;
+  return P2P_OK;
+}
+
+p2p_status p2p_kv_ensure_capacity(p2p_kv* kv, int64_t need_tokens, int64_t grow_tokens,
+                                  int64_t max_tokens, void* stream) {
+  if (!kv) return P2P_ERR_INVALID_ARG;
+  p2p_ctx* ctx = kv->ctx;
+  if (need_tokens <= kv->cap) return P2P_OK;                  // engine.js:275
+  if (need_tokens > max_tokens)                               // engine.js:276
+    return fail(ctx, P2P_ERR_KV_FULL, "need %lld tokens > max %lld", (long long)need_tokens,
+                (long long)max_tokens);
+  if (grow_tokens <= 0) grow_tokens = 1;
+  int64_t nc = kv->cap;
+  while (nc < need_tokens) nc += grow_tokens;                 // engine.js:277-279
+  if (nc > max_tokens) nc = max_tokens;
+  DeviceGuard g(ctx->device);
+  const size_t eb = size_t(kv->hkv) * kv->d * elem_bytes(kv->dtype);
+  const size_t nbytes = size_t(nc) * eb, obytes = size_t(kv->cap) * eb;
+  std::vector<void*> nk, nv;
+  for (int l = 0; l < kv->n_layers; ++l) {                    // engine.js:280-286
+    void* k = nullptr;
+    void* v = nullptr;
+    const bool ok = dev_alloc(&k, nbytes) == cudaSuccess && dev_alloc(&v, nbytes) == cudaSuccess;
+    if (k) nk.push_back(k);
+    if (v) nv.push_back(v);
+    if (!ok) {
+      for (void* p : nk) dev_free(p, nbytes);
+      for (void* p : nv) dev_free(p, nbytes);
+      return fail(ctx, P2P_ERR_OOM, "kv growth to %lld tokens", (long long)nc);
+    }
+  }
+  cudaStream_t s = pick_stream(ctx, stream);
+  for (int l = 0; l < kv->n_layers; ++l) {                    // engine.js:287-293
+    cudaMemcpyAsync(nk[l], kv->k[l], obytes, cudaMemcpyDeviceToDevice, s);
+    cudaMemcpyAsync(nv[l], kv->v[l], obytes, cudaMemcpyDeviceToDevice, s);
+  }
+  cudaError_t e = cudaStreamSynchronize(s);                   // engine.js:301
+  for (int l = 0; l < kv->n_layers; ++l) {                    // engine.js:302
+    dev_free(kv->k[l], obytes);
+    dev_free(kv->v[l], obytes);
+  }
+  kv->k = nk;
+  kv->v = nv;
+  kv->cap = nc;
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "kv growth copy");
+  return P2P_OK;
+}
+
+int64_t p2p_kv_capacity(const p2p_kv* kv) { return kv ? kv->cap : 0; }
+void* p2p_kv_k(const p2p_kv* kv, int32_t layer) {
+  return (kv && layer >= 0 && layer < kv->n_layers) ? kv->k[layer] : nullptr;
+}
+void* p2p_kv_v(const p2p_kv* kv, int32_t layer) {
+  return (kv && layer >= 0 && layer < kv->n_layers) ? kv->v[layer] : nullptr;
+}
+
+p2p_status p2p_qk_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const void* qkv,
+                       int64_t ld_qkv, const void* norm_w, const void* rope, void* q_out,
+                       int64_t ld_q, void* k_cache, void* v_cache, int64_t kv_cap_tokens,
+                       const uint32_t* meta_dev, int32_t pos0, int32_t m_tokens, void* stream) {
+  p2p_status st = check_params(ctx, prm, true);
+  if (st != P2P_OK) return st;
+  const int64_t row = int64_t(prm->num_heads + 2 * prm->num_kv_heads) * prm->head_dim;
+  if (!qkv || !rope || !q_out || !k_cache || !v_cache)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "qk_prep: NULL buffer");
+  if (m_tokens < 0 || m_tokens > 65535 || ld_qkv < row ||
+      ld_q < int64_t(prm->num_heads) * prm->head_dim || (!meta_dev && pos0 < 0) ||
+      kv_cap_tokens <= 0)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "qk_prep: M %d ld_qkv %lld ld_q %lld pos0 %d cap %lld",
+                m_tokens, (long long)ld_qkv, (long long)ld_q, pos0, (long long)kv_cap_tokens);
+  if (!meta_dev && int64_t(pos0) + m_tokens > kv_cap_tokens)
+    return fail(ctx, P2P_ERR_KV_FULL, "qk_prep: pos0 %d + M %d > cache rows %lld", pos0,
+                m_tokens, (long long)kv_cap_tokens);
+  DeviceGuard g(ctx->device);
+  p2p::QkPrepArgs a{qkv, ld_qkv, norm_w, rope, q_out, ld_q, k_cache, v_cache, kv_cap_tokens,
+                    meta_dev, pos0, m_tokens, prm->num_heads, prm->num_kv_heads, eff_eps(prm),
+                    ctx->dev_err};
+  cudaError_t e = p2p::launch_qk_prep(a, prm->dtype, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "qk_prep launch");
+  return P2P_OK;
+}
+
+p2p_status p2p_attn(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q, int64_t ld_q,
+                    const void* k_cache, const void* v_cache, int64_t kv_cap_tokens, void* out,
+                    int64_t ld_o, const uint32_t* meta_dev, int32_t pos0, int32_t m_tokens,
+                    void* stream) {
+  p2p_status st = check_params(ctx, prm, m_tokens == 1);
+  if (st != P2P_OK) return st;
+  const int64_t qw = int64_t(prm->num_heads) * prm->head_dim;
+  if (!q || !k_cache || !v_cache || !out) return fail(ctx, P2P_ERR_INVALID_ARG, "attn: NULL buffer");
+  if (m_tokens < 0 || ld_q < qw || ld_o < qw || kv_cap_tokens <= 0 || (!meta_dev && pos0 < 0))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn: M %d ld_q %lld ld_o %lld cap %lld pos0 %d",
+                m_tokens, (long long)ld_q, (long long)ld_o, (long long)kv_cap_tokens, pos0);
+  if (!meta_dev && int64_t(pos0) + m_tokens > kv_cap_tokens)
+    return fail(ctx, P2P_ERR_KV_FULL, "attn: pos0 %d + M %d > cache rows %lld", pos0, m_tokens,
+                (long long)kv_cap_tokens);
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn: cache buffers must be 16-byte aligned");
+  if (m_tokens == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  if (m_tokens == 1) {
+    p2p::DecodeArgs a{};
+    a.layers[0] = {q, nullptr, const_cast<void*>(k_cache), const_cast<void*>(v_cache), out};
+    a.meta = meta_dev;
+    a.pos_host = pos0;
+    a.kv_cap = kv_cap_tokens;
+    const int64_t max_len = meta_dev ? kv_cap_tokens : int64_t(pos0) + 1;
+    return run_decode(ctx, prm, a, p2p::kLayers, false, 1, max_len, s);
+  }
+  if ((ld_q % 8) || (ld_o % 8) || !aligned16(q) || !aligned16(out))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn prefill: q/out must be 16-byte aligned rows");
+  p2p::FlashArgs f{};
+  f.q = q;
+  f.k = k_cache;
+  f.v = v_cache;
+  f.out = out;
+  f.ld_q = ld_q;
+  f.ld_kv = int64_t(prm->num_kv_heads) * prm->head_dim;
+  f.ld_o = ld_o;
+  f.q_rows_total = m_tokens;
+  f.kv_rows_total = kv_cap_tokens;
+  f.batch_stride_q_rows = 0;
+  f.batch_stride_kv_rows = 0;
+  f.batch = 1;
+  f.s_q = m_tokens;
+  f.s_kv = 0;
+  f.hq = prm->num_heads;
+  f.hkv = prm->num_kv_heads;
+  f.causal = 1;
+  f.meta = meta_dev;
+  f.pos0_host = pos0;
+  f.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
+  f.err = ctx->dev_err;
+  cudaError_t e = p2p::launch_flash(f, s);
+  if (e == cudaErrorNotSupported) return fail(ctx, P2P_ERR_UNSUPPORTED, "prefill kernel");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill launch");
+  return P2P_OK;
+}
+
+p2p_status p2p_decode_step(p2p_ctx* ctx, const p2p_attn_params* prm, int32_t n_layers,
+                           const p2p_decode_layer* layers, const void* rope,
+                           int64_t kv_cap_tokens, const uint32_t* meta_dev, int32_t pos,
+                           void* stream) {
+  p2p_status st = check_params(ctx, prm, true);
+  if (st != P2P_OK) return st;
+  if (n_layers <= 0 || n_layers > P2P_MAX_LAYERS || !layers || !rope)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_step: n_layers %d (max %d)", n_layers,
+                P2P_MAX_LAYERS);
+  if (kv_cap_tokens <= 0 || (!meta_dev && (pos < 0 || int64_t(pos) >= kv_cap_tokens)))
+    return fail(ctx, meta_dev ? P2P_ERR_INVALID_ARG : P2P_ERR_KV_FULL,
+                "decode_step: pos %d cache rows %lld", pos, (long long)kv_cap_tokens);
+  p2p::DecodeArgs a{};
+  for (int l = 0; l < n_layers; ++l) {
+    const p2p_decode_layer& L = layers[l];
+    if (!L.qkv || !L.k_cache || !L.v_cache || !L.out || !aligned16(L.k_cache) ||
+        !aligned16(L.v_cache))
+      return fail(ctx, P2P_ERR_INVALID_ARG, "decode_step: layer %d has a NULL or misaligned buffer", l);
+    a.layers[l] = {L.qkv, L.norm_w, L.k_cache, L.v_cache, L.out};
+  }
+  a.rope = rope;
+  a.meta = meta_dev;
+  a.pos_host = pos;
+  a.kv_cap = kv_cap_tokens;
+  DeviceGuard g(ctx->device);
+  const int64_t max_len = meta_dev ? kv_cap_tokens : int64_t(pos) + 1;
+  return run_decode(ctx, prm, a, p2p::kLayers, true, n_layers, max_len,
+                    pick_stream(ctx, stream));
+}
+
+p2p_status p2p_attn_decode_ragged(p2p_ctx* ctx, const p2p_attn_params* prm, const void* qkv,
+                                  int64_t ld_qkv, const void* norm_w, const void* rope,
+                                  void* k_cache, void* v_cache, const int32_t* offsets,
+                                  const int32_t* past, int32_t nseq, int32_t max_past,
+                                  int32_t fused_prep, void* out, int64_t ld_o, void* stream) {
+  p2p_status st = check_params(ctx, prm, true);
+  if (st != P2P_OK) return st;
+  const int64_t qw = int64_t(prm->num_heads) * prm->head_dim;
+  const int64_t row = qw + 2 * int64_t(prm->num_kv_heads) * prm->head_dim;
+  if (!qkv || !k_cache || !v_cache || !offsets || !past || !out || (fused_prep && !rope))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_ragged: NULL buffer");
+  if (nseq < 0 || nseq > 65535 || max_past < 0 || ld_o < qw || ld_qkv < (fused_prep ? row : qw))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_ragged: nseq %d max_past %d ld_qkv %lld ld_o %lld",
+                nseq, max_past, (long long)ld_qkv, (long long)ld_o);
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_ragged: cache buffers must be 16-byte aligned");
+  if (nseq == 0) return P2P_OK;
+  p2p::DecodeArgs a{};
+  a.qkv = qkv;
+  a.ld_qkv = ld_qkv;
+  a.norm_w = norm_w;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.offsets = offsets;
+  a.past = past;
+  a.out = out;
+  a.ld_o = ld_o;
+  a.rope = rope;
+  DeviceGuard g(ctx->device);
+  return run_decode(ctx, prm, a, p2p::kRagged, fused_prep != 0, nseq, int64_t(max_past) + 1,
+                    pick_stream(ctx, stream));
+}
+
+p2p_status p2p_attn_bidir(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q,
+                          const void* k, const void* v, void* out, int64_t ld, int32_t batch,
+                          int32_t s_tokens, void* stream) {
+  p2p_status st = check_params(ctx, prm, false);
+  if (st != P2P_OK) return st;
+  if (!q || !k || !v || !out) return fail(ctx, P2P_ERR_INVALID_ARG, "attn_bidir: NULL buffer");
+  const int64_t w = int64_t(prm->num_heads) * prm->head_dim;
+  const int64_t kw = int64_t(prm->num_kv_heads) * prm->head_dim;
+  if (batch < 0 || s_tokens < 0 || ld < (w > kw ? w : kw) || (ld % 8))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn_bidir: batch %d S %d ld %lld", batch, s_tokens,
+                (long long)ld);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn_bidir: buffers must be 16-byte aligned");
+  if (batch == 0 || s_tokens == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  p2p::FlashArgs f{};
+  f.q = q;
+  f.k = k;
+  f.v = v;
+  f.out = out;
+  f.ld_q = f.ld_kv = f.ld_o = ld;
+  f.q_rows_total = f.kv_rows_total = int64_t(batch) * s_tokens;
+  f.batch_stride_q_rows = f.batch_stride_kv_rows = s_tokens;
+  f.batch = batch;
+  f.s_q = s_tokens;
+  f.s_kv = s_tokens;
+  f.hq = prm->num_heads;
+  f.hkv = prm->num_kv_heads;
+  f.causal = 0;
+  f.meta = nullptr;
+  f.pos0_host = 0;
+  f.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
+  f.err = ctx->dev_err;
+  cudaError_t e = p2p::launch_flash(f, pick_stream(ctx, stream));
+  if (e == cudaErrorNotSupported) return fail(ctx, P2P_ERR_UNSUPPORTED, "bidir kernel");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "bidir launch");
+  return P2P_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,103 @@
+// kernels.h -- host-side launchers of the sm_100a kernels (internal to libp2pattn.so).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace p2p {
+
+// ---- qk_prep.cu -----------------------------------------------------------------------------
+struct QkPrepArgs {
+  const void* qkv;
+  int64_t ld_qkv;
+  const void* norm_w;  // nullable
+  const void* rope;
+  void* q_out;
+  int64_t ld_q;
+  void* k_cache;
+  void* v_cache;
+  int64_t kv_cap;        // rows the cache buffers hold; rows >= kv_cap are never touched
+  const uint32_t* meta;  // nullable -> pos0
+  int32_t pos0;
+  int32_t m_tokens;
+  int32_t hq, hkv;
+  float eps;
+  int32_t* err;          // device error word: bit 0 = position beyond the cache
+};
+cudaError_t launch_qk_prep(const QkPrepArgs& a, int dtype, cudaStream_t s);
+
+// ---- decode.cu ------------------------------------------------------------------------------
+constexpr int kMaxLayers = 16;
+
+struct DecodeLayer {
+  const void* qkv;  // fused: qkv row [Hq*D + 2*Hkv*D]; unfused: rotated q row [Hq*D]
+  const void* norm_w;
+  void* k_cache;
+  void* v_cache;
+  void* out;
+};
+
+// One work "sequence" per blockIdx.z.  Mode kLayers: z indexes layers[], every sequence has
+// the same past (meta[0] or pos_host).  Mode kRagged: z indexes sequences of one cache pair;
+// rows start at offsets[z], past = past_dev[z], q/out rows z*ld.
+struct DecodeArgs {
+  DecodeLayer layers[kMaxLayers];
+  // ragged mode
+  const void* qkv;
+  int64_t ld_qkv;
+  const void* norm_w;
+  void* k_cache;
+  void* v_cache;
+  const int32_t* offsets;
+  const int32_t* past;
+  void* out;
+  int64_t ld_o;
+  // common
+  const void* rope;
+  const uint32_t* meta;  // nullable -> pos_host
+  int32_t pos_host;
+  int64_t kv_cap;        // kLayers: rows per cache buffer; a position >= kv_cap is refused
+  int32_t* err;          // device error word: bit 0 = position beyond the cache
+  int32_t hq, hkv;
+  float scale_log2;  // scale * log2(e)
+  float eps;
+  int32_t min_split;  // keys per split lower bound (multiple of 64)
+  float* partials;    // [nz][hkv][max_splits][G][66]
+  int32_t* counters;  // [nz][hkv], zero between launches
+};
+
+enum DecodeMode { kLayers = 0, kRagged = 1 };
+
+// grid = (max_splits, hkv, nz).  Workspace sizes in bytes for that grid.
+size_t decode_partials_bytes(int max_splits, int hkv, int nz, int group);
+size_t decode_counters_bytes(int hkv, int nz);
+cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, int max_splits,
+                          int nz, cudaStream_t s);
+// Choose the split count for a sequence of up to max_len keys.
+int decode_max_splits(int64_t max_len, int hkv, int nz, int num_sms, int* min_split);
+
+// ---- prefill_sm100.cu ----------------------------------------------------------------------
+struct FlashArgs {
+  const void* q;  // [B][Sq][ld_q] rows, head h at column h*64
+  const void* k;  // [B][Skv][ld_kv] rows, kv head at column kh*64
+  const void* v;
+  void* out;      // [B][Sq][ld_o]
+  int64_t ld_q, ld_kv, ld_o;
+  int64_t q_rows_total, kv_rows_total;  // rows of the q / kv 2-D views (tensor-map extents)
+  int64_t batch_stride_q_rows, batch_stride_kv_rows;  // rows between images
+  int32_t batch;
+  int32_t s_q;       // query rows per image (M)
+  int32_t s_kv;      // key rows per image for non-causal; ignored when causal
+  int32_t hq, hkv;
+  int32_t causal;
+  const uint32_t* meta;  // causal: pos0 = meta[0] (nullable -> pos0_host)
+  int32_t pos0_host;
+  float scale_log2;
+  int32_t* err;          // device error word: bit 0 = position beyond the cache
+};
+
+// Device error word bits.
+constexpr int kErrPosBeyondCache = 1;
+cudaError_t launch_flash(const FlashArgs& a, cudaStream_t s);
+
+}  // namespace p2p

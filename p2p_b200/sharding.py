@@ -1,0 +1,59 @@
+"""Multi-GPU partitioning of the attention path (one process per GPU).
+
+Where the work shards naturally:
+  * batched decode -- independent sequences: greedy LPT by token count (not by sequence
+    count) gives every rank a near-equal share of KV bytes to stream; no collective on the
+    data path.
+  * long-context prefill -- KV-head groups: rank g owns kv heads [g*Hkv/G, (g+1)*Hkv/G) and
+    their query heads, computes out[:, heads_g] and its KV-cache slice; one all-gather over
+    NVLink assembles the [S][Hq*D] output.
+  * vision -- independent images.
+  * single-sequence decode does not shard (8.4 MB per layer is less than the cost of a
+    cross-GPU exchange): replicas only.
+"""
+from __future__ import annotations
+
+import heapq
+from typing import List, Sequence, Tuple
+
+
+def lpt_partition(costs: Sequence[int], world: int) -> List[List[int]]:
+    """Longest-processing-time-first assignment of items (by cost) to `world` bins.
+
+    Returns, per rank, the item indices in ascending order.  Deterministic: ties go to the
+    lower rank, items of equal cost in index order."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    order = sorted(range(len(costs)), key=lambda i: (-int(costs[i]), i))
+    heap = [(0, r) for r in range(world)]
+    bins: List[List[int]] = [[] for _ in range(world)]
+    for i in order:
+        load, r = heapq.heappop(heap)
+        bins[r].append(i)
+        heapq.heappush(heap, (load + int(costs[i]), r))
+    return [sorted(b) for b in bins]
+
+
+def head_groups(num_heads: int, num_kv_heads: int, world: int, rank: int) -> Tuple[int, int, int, int]:
+    """KV-head group of `rank`: (kv_head0, kv_heads, q_head0, q_heads).  world must divide
+    num_kv_heads so that every rank owns whole GQA groups."""
+    if num_kv_heads % world:
+        raise ValueError(f"{world} ranks do not divide {num_kv_heads} kv heads")
+    g = num_heads // num_kv_heads
+    kv_per = num_kv_heads // world
+    return rank * kv_per, kv_per, rank * kv_per * g, kv_per * g
+
+
+def split_images(batch: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous image range [start, start+count) of `rank`."""
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return start, base + (1 if rank < extra else 0)
+
+
+def assemble_head_shards(gathered, s_tokens: int, q_heads_per_rank: int, head_dim: int = 64):
+    """Turn the all-gathered per-rank outputs [world][S][q_heads_per_rank*D] into the
+    reference layout [S][Hq*D] (head h at column h*D).  Works on torch tensors."""
+    world = gathered.shape[0]
+    x = gathered.reshape(world, s_tokens, q_heads_per_rank * head_dim)
+    return x.permute(1, 0, 2).reshape(s_tokens, world * q_heads_per_rank * head_dim)

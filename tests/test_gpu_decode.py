@@ -1,0 +1,315 @@
+"""GPU parity of QK_PREP and the split-KV decode kernels against the oracle (C ABI calls).
+
+QK_PREP outputs (rotated q, appended k/v cache rows) must be bit-identical to the oracle;
+attention outputs must satisfy |x - r| <= 2e-3 + 1e-2 |r| on the same seeded inputs.
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_close
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+D = 64
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    import p2p_b200
+    c = p2p_b200.Context(0)
+    yield c
+    c.close()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint16 if a.dtype == np.float16 else np.uint32)
+
+
+def make_layer(rng, hq, hkv, past, cap, dtype=np.float16, norm=True):
+    qkv = rng.standard_normal((1, (hq + 2 * hkv) * D)).astype(dtype)
+    nw = (1 + 0.1 * rng.standard_normal(2 * D)).astype(dtype) if norm else None
+    kc = np.zeros((cap, hkv, D), dtype)
+    vc = np.zeros((cap, hkv, D), dtype)
+    kc[:past] = rng.standard_normal((past, hkv, D))
+    vc[:past] = rng.standard_normal((past, hkv, D))
+    return qkv, nw, kc, vc
+
+
+def oracle_decode(oracle, hq, hkv, qkv, nw, rope, kc, vc, past):
+    q = np.zeros((1, hq * D), qkv.dtype)
+    kc, vc = kc.copy(), vc.copy()
+    oracle.qk_prep(hq, hkv, D, qkv, nw, rope, q, kc, vc, past, 1)
+    out = np.zeros((1, hq * D), qkv.dtype)
+    oracle.attn(hq, hkv, D, q, kc, vc, out, past, 1)
+    return q, kc, vc, out
+
+
+@pytest.mark.parametrize("hq,hkv,pos0,m,norm", [(32, 8, 0, 5, True), (32, 8, 4000, 3, True),
+                                                (16, 8, 77, 64, True), (32, 8, 9, 2, False),
+                                                (12, 12, 3, 7, True)])
+def test_qk_prep_bit_exact(ctx, oracle, hq, hkv, pos0, m, norm):
+    import p2p_b200
+    rng = np.random.default_rng(hq * 1000 + pos0 + m)
+    cap = pos0 + m
+    qkv = rng.standard_normal((m, (hq + 2 * hkv) * D)).astype(np.float16)
+    nw = (1 + 0.1 * rng.standard_normal(2 * D)).astype(np.float16) if norm else None
+    rope_np = oracle.rope_table(cap)
+    kc = rng.standard_normal((cap, hkv, D)).astype(np.float16)
+    vc = rng.standard_normal((cap, hkv, D)).astype(np.float16)
+    q_o = np.zeros((m, hq * D), np.float16)
+    kc_o, vc_o = kc.copy(), vc.copy()
+    oracle.qk_prep(hq, hkv, D, qkv, nw, rope_np, q_o, kc_o, vc_o, pos0, m)
+    prm = p2p_b200.Params(hq, hkv)
+    q_g = torch.zeros((m, hq * D), dtype=torch.float16, device="cuda")
+    kc_g, vc_g = dev(kc), dev(vc)
+    ctx.qk_prep(prm, dev(qkv), None if nw is None else dev(nw), dev(rope_np), q_g, kc_g, vc_g,
+                pos0=pos0, m_tokens=m)
+    assert np.array_equal(bits(host(q_g)), bits(q_o))
+    assert np.array_equal(bits(host(kc_g)), bits(kc_o))
+    assert np.array_equal(bits(host(vc_g)), bits(vc_o))
+
+
+def test_library_rope_table_equals_oracle(ctx, oracle):
+    import p2p_b200  # noqa: F401
+    p = ctx.rope_table(40000, D, 1e6)
+    from p2p_b200.attention import _from_device_ptr
+    t = _from_device_ptr(p.value, 40000 * D * 2, 0).view(torch.float16).view(40000, D)
+    assert np.array_equal(bits(host(t)), bits(oracle.rope_table(40000)))
+
+
+def test_golden_decode_fixture(ctx, golden_dir):
+    """The reference shaders' own output (16 q / 8 kv heads, position 130, 2 key chunks)."""
+    import p2p_b200
+    z = np.load(golden_dir / "decoder_decode_16x8.npz")
+    pos0 = int(z["meta"][0])
+    kc = np.concatenate([z["kc_in"], np.zeros((1, 8, D), np.float16)])
+    vc = np.concatenate([z["vc_in"], np.zeros((1, 8, D), np.float16)])
+    prm = p2p_b200.Params(16, 8, scale=0.125)
+    # separate QK_PREP then ATTN (engine.js:213-222) through the meta buffer
+    ctx.meta_write(pos0, 1)
+    q = torch.zeros((1, 1024), dtype=torch.float16, device="cuda")
+    kc_g, vc_g = dev(kc), dev(vc)
+    ctx.qk_prep(prm, dev(z["qkv"]), dev(z["nwb"]), dev(z["rope"]), q, kc_g, vc_g,
+                m_tokens=1, use_meta=True)
+    out = torch.zeros((1, 1024), dtype=torch.float16, device="cuda")
+    ctx.attn(prm, q, kc_g, vc_g, out, m_tokens=1, use_meta=True)
+    assert np.array_equal(bits(host(q)), bits(z["qout"]))
+    assert np.array_equal(bits(host(kc_g)[pos0:]), bits(z["k_new"]))
+    assert_close(host(out), z["out"], what="golden decode (separate ops)")
+    # fused one-launch decode step
+    kc_g, vc_g = dev(kc), dev(vc)
+    out2 = torch.zeros((1024,), dtype=torch.float16, device="cuda")
+    ctx.decode_step(prm, [(dev(z["qkv"][0]), dev(z["nwb"]), kc_g, vc_g, out2)], dev(z["rope"]),
+                    kc.shape[0], pos=pos0)
+    assert np.array_equal(bits(host(kc_g)[pos0:]), bits(z["k_new"]))
+    assert np.array_equal(bits(host(vc_g)[pos0:]), bits(z["v_new"]))
+    assert_close(host(out2)[None], z["out"], what="golden decode (fused)")
+
+
+@pytest.mark.parametrize("past", [0, 1, 15, 16, 63, 64, 65, 127, 128, 1000, 4096, 20000])
+def test_decode_positions(ctx, oracle, past):
+    import p2p_b200
+    hq, hkv = 32, 8
+    rng = np.random.default_rng(past + 11)
+    qkv, nw, kc, vc = make_layer(rng, hq, hkv, past, past + 1)
+    rope = oracle.rope_table(past + 1)
+    q_o, kc_o, vc_o, out_o = oracle_decode(oracle, hq, hkv, qkv, nw, rope, kc, vc, past)
+    prm = p2p_b200.Params(hq, hkv)
+    kc_g, vc_g = dev(kc), dev(vc)
+    out = torch.zeros((hq * D,), dtype=torch.float16, device="cuda")
+    ctx.decode_step(prm, [(dev(qkv[0]), dev(nw), kc_g, vc_g, out)], dev(rope), past + 1, pos=past)
+    assert np.array_equal(bits(host(kc_g)), bits(kc_o))
+    assert np.array_equal(bits(host(vc_g)), bits(vc_o))
+    assert_close(host(out)[None], out_o, what=f"fused decode past={past}")
+    # unfused ATTN on the oracle's rotated q and cache
+    out3 = torch.zeros((1, hq * D), dtype=torch.float16, device="cuda")
+    ctx.attn(prm, dev(q_o), dev(kc_o), dev(vc_o), out3, pos0=past, m_tokens=1)
+    assert_close(host(out3), out_o, what=f"attn M=1 past={past}")
+
+
+@pytest.mark.parametrize("hq,hkv", [(16, 8), (8, 8), (64, 8), (32, 4)])
+def test_decode_group_sizes(ctx, oracle, hq, hkv):
+    import p2p_b200
+    past = 777
+    rng = np.random.default_rng(hq + hkv)
+    qkv, nw, kc, vc = make_layer(rng, hq, hkv, past, past + 1)
+    rope = oracle.rope_table(past + 1)
+    _, kc_o, _, out_o = oracle_decode(oracle, hq, hkv, qkv, nw, rope, kc, vc, past)
+    kc_g, vc_g = dev(kc), dev(vc)
+    out = torch.zeros((hq * D,), dtype=torch.float16, device="cuda")
+    ctx.decode_step(p2p_b200.Params(hq, hkv), [(dev(qkv[0]), dev(nw), kc_g, vc_g, out)],
+                    dev(rope), past + 1, pos=past)
+    assert np.array_equal(bits(host(kc_g)), bits(kc_o))
+    assert_close(host(out)[None], out_o, what=f"G={hq // hkv}")
+
+
+def test_decode_step_six_layers_ctx4096(ctx, oracle):
+    """LFM2.5-1.2B decode: 32 q / 8 kv heads, 4096 past tokens + 1 new, 6 independent layers,
+    all in one launch; position from the device meta buffer."""
+    import p2p_b200
+    hq, hkv, past, n_layers = 32, 8, 4096, 6
+    cap = past + 1
+    rope = oracle.rope_table(cap)
+    rope_g = dev(rope)
+    prm = p2p_b200.Params(hq, hkv)
+    layers, want = [], []
+    for l in range(n_layers):
+        rng = np.random.default_rng(1000 + l)
+        qkv, nw, kc, vc = make_layer(rng, hq, hkv, past, cap)
+        _, kc_o, vc_o, out_o = oracle_decode(oracle, hq, hkv, qkv, nw, rope, kc, vc, past)
+        out = torch.zeros((hq * D,), dtype=torch.float16, device="cuda")
+        layers.append((dev(qkv[0]), dev(nw), dev(kc), dev(vc), out))
+        want.append((kc_o, vc_o, out_o))
+    ctx.meta_write(past, 1)
+    ctx.decode_step(prm, layers, rope_g, cap, use_meta=True)
+    for l in range(n_layers):
+        kc_o, vc_o, out_o = want[l]
+        assert np.array_equal(bits(host(layers[l][2])[past]), bits(kc_o[past]))
+        assert np.array_equal(bits(host(layers[l][3])[past]), bits(vc_o[past]))
+        assert_close(host(layers[l][4])[None], out_o, what=f"layer {l}")
+
+
+def test_decode_fp32_storage(ctx, oracle):
+    """The fp32 case: past 512 + 1 new, RoPE theta 1e6 on positions 0..512, no q/k norm."""
+    import p2p_b200
+    hq, hkv, past = 32, 8, 512
+    rng = np.random.default_rng(512)
+    qkv, _, kc, vc = make_layer(rng, hq, hkv, past, past + 1, dtype=np.float32, norm=False)
+    rope = oracle.rope_table(past + 1, D, 1e6, f32=True)
+    _, kc_o, _, out_o = oracle_decode(oracle, hq, hkv, qkv, None, rope, kc, vc, past)
+    prm = p2p_b200.Params(hq, hkv, dtype=torch.float32)
+    kc_g, vc_g = dev(kc), dev(vc)
+    out = torch.zeros((hq * D,), dtype=torch.float32, device="cuda")
+    ctx.decode_step(prm, [(dev(qkv[0]), None, kc_g, vc_g, out)], dev(rope), past + 1, pos=past)
+    assert np.array_equal(bits(host(kc_g)), bits(kc_o))
+    np.testing.assert_allclose(host(out)[None], out_o, atol=2e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_ragged_decode(ctx, oracle, fused):
+    import p2p_b200
+    hq, hkv = 32, 8
+    rng = np.random.default_rng(7 + fused)
+    past = np.array([0, 1, 17, 64, 300, 1023, 1024, 1025, 2500, 5000, 7, 3333], np.int32)
+    nseq = len(past)
+    offsets = np.zeros(nseq, np.int32)
+    offsets[1:] = np.cumsum(past[:-1] + 1 + 3)  # 3 spare rows between sequences
+    rows = int(offsets[-1] + past[-1] + 1)
+    kc = rng.standard_normal((rows, hkv, D)).astype(np.float16)
+    vc = rng.standard_normal((rows, hkv, D)).astype(np.float16)
+    rope = oracle.rope_table(int(past.max()) + 1)
+    nw = (1 + 0.1 * rng.standard_normal(2 * D)).astype(np.float16)
+    qkv = rng.standard_normal((nseq, (hq + 2 * hkv) * D)).astype(np.float16)
+    kc_o, vc_o = kc.copy(), vc.copy()
+    q_o = np.zeros((nseq, hq * D), np.float16)
+    for i in range(nseq):
+        o = offsets[i]
+        sl = slice(o, o + past[i] + 1)
+        kk, vv = kc_o[sl], vc_o[sl]
+        qq = np.zeros((1, hq * D), np.float16)
+        oracle.qk_prep(hq, hkv, D, qkv[i:i + 1], nw, rope, qq, kk, vv, int(past[i]), 1)
+        kc_o[sl], vc_o[sl], q_o[i] = kk, vv, qq[0]
+    out_o = np.zeros((nseq, hq * D), np.float16)
+    oracle.attn_ragged(hq, hkv, D, q_o, kc_o, vc_o, offsets.astype(np.int64), past, out_o)
+    prm = p2p_b200.Params(hq, hkv)
+    out = torch.zeros((nseq, hq * D), dtype=torch.float16, device="cuda")
+    if fused:
+        kc_g, vc_g = dev(kc), dev(vc)
+        ctx.attn_decode_ragged(prm, dev(qkv), dev(nw), dev(rope), kc_g, vc_g, dev(offsets),
+                               dev(past), out, max_past=int(past.max()), fused_prep=True)
+        assert np.array_equal(bits(host(kc_g)), bits(kc_o))
+        assert np.array_equal(bits(host(vc_g)), bits(vc_o))
+    else:
+        ctx.attn_decode_ragged(prm, dev(q_o), None, None, dev(kc_o), dev(vc_o), dev(offsets),
+                               dev(past), out, max_past=1000, fused_prep=False)
+    assert_close(host(out), out_o, what="ragged")
+
+
+def test_repeated_calls_reuse_counters(ctx, oracle):
+    """The split counters reset themselves: many back-to-back launches stay correct."""
+    import p2p_b200
+    hq, hkv, past = 32, 8, 3000
+    rng = np.random.default_rng(99)
+    qkv, nw, kc, vc = make_layer(rng, hq, hkv, past, past + 1)
+    rope = oracle.rope_table(past + 1)
+    _, _, _, out_o = oracle_decode(oracle, hq, hkv, qkv, nw, rope, kc, vc, past)
+    kc_g, vc_g, rg, qg, ng = dev(kc), dev(vc), dev(rope), dev(qkv[0]), dev(nw)
+    out = torch.zeros((hq * D,), dtype=torch.float16, device="cuda")
+    for _ in range(50):
+        ctx.decode_step(p2p_b200.Params(hq, hkv), [(qg, ng, kc_g, vc_g, out)], rg, past + 1,
+                        pos=past)
+    assert_close(host(out)[None], out_o, what="after 50 launches")
+
+
+def test_errors_are_statuses(ctx):
+    import p2p_b200
+    prm = p2p_b200.Params(32, 8, head_dim=128)
+    x = torch.zeros(16, dtype=torch.float16, device="cuda")
+    with pytest.raises(p2p_b200.P2PError) as e:
+        ctx.attn(prm, x.view(1, 16), x.view(1, 1, 16), x.view(1, 1, 16), x.view(1, 16))
+    assert e.value.status == 7  # UNSUPPORTED
+    with pytest.raises(p2p_b200.P2PError) as e:
+        ctx.attn(p2p_b200.Params(30, 8), x.view(1, 16), x.view(1, 1, 16), x.view(1, 1, 16),
+                 x.view(1, 16))
+    assert e.value.status == 1
+    # host-known position beyond the cache -> KV_FULL
+    kc = torch.zeros((4, 8, D), dtype=torch.float16, device="cuda")
+    q = torch.zeros((1, 32 * D), dtype=torch.float16, device="cuda")
+    with pytest.raises(p2p_b200.KvFullError):
+        ctx.attn(p2p_b200.Params(32, 8), q, kc, kc, q, pos0=4, m_tokens=1)
+
+
+def test_kv_cache_growth_and_kv_full(ctx, oracle):
+    import p2p_b200
+    prm = p2p_b200.Params(16, 8)
+    eng = p2p_b200.LfmAttention(ctx, prm, n_layers=2, max_ctx=600, kv_init_bytes=2 * 2 * 8 * 64
+                                * 2 * 100, kv_grow_bytes=2 * 2 * 8 * 64 * 2 * 64)
+    assert eng.kv.capacity == 100
+    k0 = eng.kv.k(1)
+    k0.copy_(torch.randn_like(k0))
+    before = host(k0).copy()
+    assert eng.ensure_capacity(250)
+    assert eng.kv.capacity == 292  # 100 + 3 * 64
+    assert np.array_equal(bits(host(eng.kv.k(1))[:100]), bits(before))
+    assert not eng.ensure_capacity(601)  # beyond max_ctx -> 'kv_full'
+    assert eng.ensure_capacity(600) and eng.kv.capacity == 600
+    # allocation failure keeps the old cache and reports failure
+    p2p_b200.lib.p2p_debug_set_alloc_limit(0)
+    try:
+        eng2 = p2p_b200.LfmAttention.__new__(p2p_b200.LfmAttention)
+        with pytest.raises(p2p_b200.OomError):
+            p2p_b200.KVCache(ctx, 1, 8, 10)
+        del eng2
+    finally:
+        p2p_b200.lib.p2p_debug_set_alloc_limit(-1)
+
+
+def test_device_position_beyond_cache_is_refused(ctx):
+    """A meta position the cache cannot hold: the kernel touches nothing and p2p_sync reports
+    P2P_ERR_KV_FULL (the reference's 'kv_full'), leaving the context usable."""
+    import p2p_b200
+    hq, hkv, cap = 32, 8, 64
+    prm = p2p_b200.Params(hq, hkv)
+    kc = torch.zeros((cap, hkv, D), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    qkv = torch.ones(((hq + 2 * hkv) * D,), dtype=torch.float16, device="cuda")
+    out = torch.full((hq * D,), 7.0, dtype=torch.float16, device="cuda")
+    rope = ctx.rope_table(cap + 8)
+    ctx.meta_write(cap, 1)
+    ctx.decode_step(prm, [(qkv, None, kc, vc, out)], rope, cap, use_meta=True)
+    with pytest.raises(p2p_b200.KvFullError):
+        ctx.sync()
+    assert float(kc.abs().sum()) == 0 and float(out[0]) == 7.0
+    ctx.meta_write(cap - 1, 1)
+    ctx.decode_step(prm, [(qkv, None, kc, vc, out)], rope, cap, use_meta=True)
+    ctx.sync()
