@@ -313,3 +313,41 @@ def test_device_position_beyond_cache_is_refused(ctx):
     ctx.meta_write(cap - 1, 1)
     ctx.decode_step(prm, [(qkv, None, kc, vc, out)], rope, cap, use_meta=True)
     ctx.sync()
+
+
+def test_ragged_decode_full_scale_sampled(ctx, oracle):
+    """The 256-sequence ragged workload at full size (past ~ U[1024, 32768], ~9 GB of KV):
+    run on the GPU, then check a sample of sequences (shortest, longest, a few others)
+    against the oracle on their downloaded cache slices."""
+    import p2p_b200
+    hq, hkv = 32, 8
+    rng = np.random.default_rng(4)
+    past = rng.integers(1024, 32769, 256).astype(np.int32)
+    offsets = np.zeros(256, np.int64)
+    offsets[1:] = np.cumsum(past[:-1].astype(np.int64) + 1)
+    rows = int(offsets[-1] + past[-1] + 1)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    kc = torch.randn((rows, hkv, D), generator=g, device="cuda", dtype=torch.float16)
+    vc = torch.randn((rows, hkv, D), generator=g, device="cuda", dtype=torch.float16)
+    qkv = torch.randn((256, (hq + 2 * hkv) * D), generator=g, device="cuda", dtype=torch.float16)
+    nw = (1 + 0.1 * torch.randn((2 * D,), generator=g, device="cuda")).half()
+    rope = oracle.rope_table(int(past.max()) + 1)
+    sample = sorted({int(np.argmin(past)), int(np.argmax(past)), 0, 77, 128, 255})
+    before = {i: (host(kc[offsets[i]:offsets[i] + past[i] + 1]).copy(),
+                  host(vc[offsets[i]:offsets[i] + past[i] + 1]).copy()) for i in sample}
+    out = torch.zeros((256, hq * D), dtype=torch.float16, device="cuda")
+    ctx.attn_decode_ragged(p2p_b200.Params(hq, hkv), qkv, nw, dev(rope), kc, vc,
+                           dev(offsets.astype(np.int32)), dev(past), out,
+                           max_past=int(past.max()), fused_prep=True)
+    got = host(out)
+    qkv_h, nw_h = host(qkv), host(nw)
+    for i in sample:
+        k_i, v_i = before[i]
+        q_o = np.zeros((1, hq * D), np.float16)
+        oracle.qk_prep(hq, hkv, D, qkv_h[i:i + 1], nw_h, rope, q_o, k_i, v_i, int(past[i]), 1)
+        want = np.zeros((1, hq * D), np.float16)
+        oracle.attn(hq, hkv, D, q_o, k_i, v_i, want, int(past[i]), 1)
+        assert np.array_equal(bits(host(kc[offsets[i] + past[i]])), bits(k_i[past[i]]))
+        assert_close(got[i:i + 1], want, what=f"ragged seq {i} (past {past[i]})")
+    del kc, vc
+    torch.cuda.empty_cache()
