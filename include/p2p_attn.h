@@ -22,8 +22,8 @@
  *   meta         uint32[4] = [pos0, M, step, 0] in device memory (engine.js:144, :388)
  *   vision q/k/v [B][S][ld] with head h at column h*D         (vision-kernels.js:198)
  *
- * Conventions: every call is asynchronous on the given CUDA stream (passed as void*; NULL
- * means the context's own stream).  A context is not thread-safe; use one per host thread.
+ * Conventions: every call is asynchronous on the given CUDA stream (a cudaStream_t passed as
+ * void*; NULL is the CUDA default stream, p2p_ctx_stream() the context's own stream).  A context is not thread-safe; use one per host thread.
  * Calls return a p2p_status and never abort; p2p_last_error() describes the last failure.
  * head_dim must be 64 (the reference's only head size); num_heads % num_kv_heads == 0 and
  * num_heads / num_kv_heads in {1, 2, 4, 8}.

@@ -106,9 +106,9 @@ void dev_free(void* p, size_t bytes) {
   g_alloc_used -= int64_t(bytes);
 }
 
-cudaStream_t pick_stream(p2p_ctx* ctx, void* stream) {
-  return stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-}
+// NULL is the CUDA default stream (as for every CUDA library), not the context's stream:
+// a caller that wants the context's own stream passes p2p_ctx_stream(ctx).
+cudaStream_t pick_stream(p2p_ctx*, void* stream) { return static_cast<cudaStream_t>(stream); }
 
 size_t elem_bytes(int dtype) { return dtype == P2P_F32 ? 4 : 2; }
 
@@ -141,8 +141,7 @@ float eff_eps(const p2p_attn_params* prm) { return prm->eps > 0.f ? prm->eps : 1
 
 p2p_status ensure_workspace(p2p_ctx* ctx, size_t pbytes, size_t cbytes, cudaStream_t s) {
   if (pbytes > ctx->partials_bytes) {
-    cudaStreamSynchronize(s);
-    cudaStreamSynchronize(ctx->stream);
+    cudaDeviceSynchronize();  // rare growth: no launch may still use the old workspace
     dev_free(ctx->partials, ctx->partials_bytes);
     ctx->partials = nullptr;
     ctx->partials_bytes = 0;
@@ -153,8 +152,7 @@ p2p_status ensure_workspace(p2p_ctx* ctx, size_t pbytes, size_t cbytes, cudaStre
     ctx->partials_bytes = pbytes;
   }
   if (cbytes > ctx->counters_bytes) {
-    cudaStreamSynchronize(s);
-    cudaStreamSynchronize(ctx->stream);
+    cudaDeviceSynchronize();
     dev_free(ctx->counters, ctx->counters_bytes);
     ctx->counters = nullptr;
     ctx->counters_bytes = 0;
@@ -267,7 +265,7 @@ p2p_status p2p_ctx_create(int device, p2p_ctx** out) {
 p2p_status p2p_ctx_destroy(p2p_ctx* ctx) {
   if (!ctx) return P2P_ERR_INVALID_ARG;
   DeviceGuard g(ctx->device);
-  cudaStreamSynchronize(ctx->stream);
+  cudaDeviceSynchronize();
   for (auto& kv : ctx->rope) cudaFree(kv.second);
   dev_free(ctx->meta, 16);
   dev_free(ctx->dev_err, sizeof(int32_t));
@@ -415,7 +413,7 @@ p2p_status p2p_kv_create(p2p_ctx* ctx, int32_t n_layers, int32_t num_kv_heads,
 p2p_status p2p_kv_destroy(p2p_kv* kv) {
   if (!kv) return P2P_ERR_INVALID_ARG;
   DeviceGuard g(kv->ctx->device);
-  cudaStreamSynchronize(kv->ctx->stream);
+  cudaDeviceSynchronize();
   const size_t bytes = size_t(kv->cap) * kv->hkv * kv->d * elem_bytes(kv->dtype);
   for (int l = 0; l < kv->n_layers; ++l) {
     dev_free(kv->k[l], bytes);

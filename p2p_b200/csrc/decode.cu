@@ -7,15 +7,29 @@
 // heads, so for G <= 4 every K/V byte is read from HBM exactly once (the shader reads each kv
 // head once per q head, kernels.js:282).
 //
-// Memory pipeline: a kStages-deep cp.async ring of 64-key tiles in shared memory; every warp
-// instruction copies four whole 128-byte K (or V) rows.  Compute: lane = 8*slot + part; the 8
-// lanes of a slot hold one key row's 8-element chunks, complete the dot products with a
-// 3-level xor-shuffle, and each slot keeps its own online-softmax state (running max and sum,
-// 8 accumulator dims per q head) in the log2 domain.  Slots merge with shuffles, warps through
-// shared memory.  A CTA whose sequence needs more than one split writes its partial
-// (acc, max, sum) to the workspace; the last CTA of the (sequence, head chunk) to arrive --
-// counted with one atomic -- runs the second pass that combines the partials and writes the
-// output, then resets its counter.  Nothing ever waits on another CTA.
+// Memory pipeline (both kernels): a cp.async ring of 64-key tiles in shared memory; every
+// warp instruction copies four whole 128-byte K (or V) rows with 16-byte copies.
+//
+// f16 kernel (decode_mma_kernel): each warp owns 16 keys of a tile and runs the two
+// contractions on the tensor cores with warp-level mma.sync.m16n8k16 (f16 in, f32 out):
+//     S^T[16 keys x 8]   = K[16 x 64] . Q^T[64 x 8]         (the G query heads, zero padded)
+//     O^T[64 dims x 8]  += V^T[64 x 16] . P^T[16 x 8]
+// K/V fragments come from the ring with ldmatrix (rows XOR-swizzled in 16-byte chunks, so
+// the 128-byte rows are bank-conflict free); P^T is the S^T accumulator rounded to f16 and
+// transposed in registers with movmatrix.  The softmax runs on the accumulator fragment:
+// per-head block max by xor-shuffle over the 8 lanes holding a head's keys, exp2 on the MUFU,
+// running max / sum kept per lane.  That is ~4 warp instructions per key instead of ~60 for
+// a CUDA-core dot-product formulation, so the kernel is bound by HBM, not by issue.
+//
+// f32 kernel (decode_simt_kernel, the fp32 storage case): CUDA-core formulation, lane =
+// 8*slot + part, each slot of 8 lanes holds one key row, dot products completed with a
+// 3-level xor-shuffle, per-slot online softmax.
+//
+// Both finish the same way: warps merge through shared memory; a CTA whose sequence needs
+// more than one split writes its partial (acc, max, sum) to the workspace, and the last CTA
+// of the (sequence, head chunk) to arrive -- counted with one atomic -- runs the second pass
+// that combines the partials and writes the output, then resets its counter.  Nothing ever
+// waits on another CTA.
 #include <mutex>
 #include <set>
 
@@ -27,8 +41,7 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr int kWarps = 4;
-constexpr int kStageKeys = 64;                   // keys per pipeline stage
-constexpr int kKeysPerThread = kStageKeys / 16;  // 4 warps x 4 slots cover 16 rows per pass
+constexpr int kStageKeys = 64;  // keys per pipeline stage
 constexpr float kNegBig = -1e30f;
 constexpr int kPartialStride = kHeadDim + 2;  // acc[64], max, sum
 
@@ -39,6 +52,377 @@ struct Ring {
   static constexpr int kBytes = 2 * kStages * kTileElems * int(sizeof(T));  // K and V
 };
 
+// ---- per-sequence view ------------------------------------------------------------------------
+template <class T>
+struct Seq {
+  int past;
+  const T* qrow;
+  const T* nw;
+  T* kc;
+  T* vc;
+  T* orow;
+};
+
+template <class T, int MODE>
+__device__ __forceinline__ Seq<T> resolve(const DecodeArgs& a, int z) {
+  Seq<T> q;
+  if (MODE == kLayers) {
+    const DecodeLayer& L = a.layers[z];
+    q.past = a.meta ? int(a.meta[0]) : a.pos_host;
+    q.qrow = static_cast<const T*>(L.qkv);
+    q.nw = static_cast<const T*>(L.norm_w);
+    q.kc = static_cast<T*>(L.k_cache);
+    q.vc = static_cast<T*>(L.v_cache);
+    q.orow = static_cast<T*>(L.out);
+  } else {
+    q.past = a.past[z];
+    q.qrow = static_cast<const T*>(a.qkv) + int64_t(z) * a.ld_qkv;
+    q.nw = static_cast<const T*>(a.norm_w);
+    const int64_t row0 = int64_t(a.offsets[z]) * a.hkv * kHeadDim;
+    q.kc = static_cast<T*>(a.k_cache) + row0;
+    q.vc = static_cast<T*>(a.v_cache) + row0;
+    q.orow = static_cast<T*>(a.out) + int64_t(z) * a.ld_o;
+  }
+  return q;
+}
+
+// Rotated query heads head0..head0+GC-1 into q_s (times `qscale`), and for the split that
+// holds the new token its normed/rotated k and raw v (QK_PREP's k and v units) into
+// knew_s/vnew_s and, by head chunk 0, into cache row `past`.  Unfused: q is read as given.
+template <class T, int GC, bool FUSED>
+__device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T>& sq, int kh, int hc,
+                                         int head0, bool has_new, float qscale,
+                                         float (*q_s)[kHeadDim], float* knew_s, float* vnew_s) {
+  constexpr int D = kHeadDim;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (FUSED) {
+    const int64_t kv_stride = int64_t(a.hkv) * D;
+    const T* rope = static_cast<const T*>(a.rope) + int64_t(sq.past) * D;
+    const float cs = to_f32(rope[lane]);
+    const float sn = to_f32(rope[32 + lane]);
+    const int units = GC + (has_new ? 2 : 0);
+    for (int u = warp; u < units; u += kWarps) {
+      if (u < GC) {  // QK_PREP q unit (kernels.js:255-263), f16 rounding of the stored q
+        const int64_t off = int64_t(head0 + u) * D;
+        float r0, r1;
+        norm_rope_head<T>(to_f32(sq.qrow[off + lane]), to_f32(sq.qrow[off + lane + 32]), sq.nw,
+                          sq.nw != nullptr, a.eps, cs, sn, r0, r1);
+        q_s[u][lane] = round_st<T>(r0) * qscale;
+        q_s[u][lane + 32] = round_st<T>(r1) * qscale;
+      } else if (u == GC) {  // QK_PREP k unit -> cache row `past`
+        const int64_t off = int64_t(a.hq + kh) * D;
+        float r0, r1;
+        norm_rope_head<T>(to_f32(sq.qrow[off + lane]), to_f32(sq.qrow[off + lane + 32]),
+                          sq.nw ? sq.nw + D : nullptr, sq.nw != nullptr, a.eps, cs, sn, r0, r1);
+        const T k0 = from_f32<T>(r0), k1 = from_f32<T>(r1);
+        if (hc == 0) {
+          T* dst = sq.kc + int64_t(sq.past) * kv_stride + kh * D;
+          dst[lane] = k0;
+          dst[lane + 32] = k1;
+        }
+        knew_s[lane] = to_f32(k0);
+        knew_s[lane + 32] = to_f32(k1);
+      } else {  // QK_PREP v unit: raw copy -> cache row `past`
+        const int64_t off = int64_t(a.hq + a.hkv + kh) * D;
+        const T x0 = sq.qrow[off + lane], x1 = sq.qrow[off + lane + 32];
+        if (hc == 0) {
+          T* dst = sq.vc + int64_t(sq.past) * kv_stride + kh * D;
+          dst[lane] = x0;
+          dst[lane + 32] = x1;
+        }
+        vnew_s[lane] = to_f32(x0);
+        vnew_s[lane + 32] = to_f32(x1);
+      }
+    }
+  } else {
+    for (int i = tid; i < GC * D; i += kThreads)
+      q_s[i / D][i % D] = to_f32(sq.qrow[int64_t(head0) * D + i]) * qscale;
+  }
+}
+
+// Cross-warp merge of (red_m, red_l, red_acc) and the split-KV second pass.
+template <class T, int GC>
+__device__ __forceinline__ void finish(const DecodeArgs& a, T* out_h, int pair, int split,
+                                       int nsplit, int ngrid, const float (*red_m)[GC],
+                                       const float (*red_l)[GC],
+                                       const float (*red_acc)[GC][kHeadDim], int* s_last) {
+  constexpr int D = kHeadDim;
+  const int tid = threadIdx.x;
+  float* part_base = a.partials + int64_t(pair) * ngrid * (GC * kPartialStride);
+  for (int idx = tid; idx < GC * D; idx += kThreads) {
+    const int g = idx / D, d = idx % D;
+    float mx = red_m[0][g];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, red_m[w][g]);
+    float l = 0.f, ac = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float c = fast_exp2(red_m[w][g] - mx);
+      l = fmaf(red_l[w][g], c, l);
+      ac = fmaf(red_acc[w][g][d], c, ac);
+    }
+    if (nsplit == 1) {
+      out_h[idx] = from_f32<T>(ac / l);  // kernels.js:317
+    } else {
+      float* p = part_base + int64_t(split) * (GC * kPartialStride) + g * kPartialStride;
+      p[d] = ac;
+      if (d == 0) {
+        p[D] = mx;
+        p[D + 1] = l;
+      }
+    }
+  }
+  if (nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(&a.counters[pair], 1);
+    *s_last = (prev == nsplit - 1);
+  }
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
+  for (int idx = tid; idx < GC * D; idx += kThreads) {
+    const int g = idx / D, d = idx % D;
+    const float* p0 = part_base + g * kPartialStride;
+    float mx = kNegBig;
+    for (int sp = 0; sp < nsplit; ++sp)
+      mx = fmaxf(mx, __ldcg(p0 + int64_t(sp) * (GC * kPartialStride) + D));
+    float l = 0.f, ac = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float* p = p0 + int64_t(sp) * (GC * kPartialStride);
+      const float c = fast_exp2(__ldcg(p + D) - mx);
+      l = fmaf(__ldcg(p + D + 1), c, l);
+      ac = fmaf(__ldcg(p + d), c, ac);
+    }
+    out_h[idx] = from_f32<T>(ac / l);
+  }
+  if (tid == 0) a.counters[pair] = 0;
+}
+
+// ---- warp-level MMA helpers -------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Byte offset of 16-byte chunk `c` of row `r` in a 64-element f16 tile whose rows are 128
+// bytes and whose chunks are XOR-swizzled with the row's low 3 bits.
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return uint32_t(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+template <int G, bool FUSED, int MODE>
+__global__ void __launch_bounds__(kThreads, 3)
+    decode_mma_kernel(const __grid_constant__ DecodeArgs a) {
+  using T = __half;
+  constexpr int D = kHeadDim;
+  constexpr int GC = G > 4 ? 4 : G;
+  constexpr int NHC = G / GC;
+  constexpr int kStages = Ring<T>::kStages;
+  constexpr int kTile = Ring<T>::kTileElems;
+  constexpr uint32_t kVOff = kStages * kTile * 2;  // byte offset of the V ring
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int split = blockIdx.x, z = blockIdx.z;
+  const int kh = blockIdx.y / NHC, hc = blockIdx.y % NHC;
+  const int head0 = kh * G + hc * GC;
+  const int ngrid = gridDim.x;
+  const Seq<T> sq = resolve<T, MODE>(a, z);
+  if (MODE == kLayers && int64_t(sq.past) >= a.kv_cap) {  // refuse rows beyond the cache
+    if (tid == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
+    return;
+  }
+  const int len = sq.past + 1;  // keys 0..past, key `past` is the new token
+  const int split_len = max(a.min_split, (ceil_div(len, ngrid) + 15) & ~15);
+  const int nsplit = ceil_div(len, split_len);
+  if (split >= nsplit) return;
+  const int j0 = split * split_len;
+  const int j1 = min(j0 + split_len, len);
+  const bool has_new = FUSED && (j1 == len);
+  const int jcopy = has_new ? sq.past : j1;  // rows streamed from the cache
+  const int64_t kv_stride = int64_t(a.hkv) * D;
+
+  __shared__ float q_s[GC][D];
+  __shared__ float knew_s[D];
+  __shared__ float vnew_s[D];
+  __shared__ float red_m[kWarps][GC];
+  __shared__ float red_l[kWarps][GC];
+  __shared__ float red_acc[kWarps][GC][D];
+  __shared__ int s_last;
+
+  const T* kbase = sq.kc + kh * D;
+  const T* vbase = sq.vc + kh * D;
+  const int n_tiles = ceil_div(j1 - j0, kStageKeys);
+  const uint32_t ring = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  auto issue_tile = [&](int tile) {
+    if (tile < n_tiles) {
+      const uint32_t off = (tile % kStages) * (kTile * 2);
+      const int jt = j0 + tile * kStageKeys;
+      const int c = tid & 7;
+#pragma unroll
+      for (int i = 0; i < kStageKeys / 16; ++i) {
+        const int r = (tid >> 3) + 16 * i;
+        const bool ok = jt + r < jcopy;
+        const int64_t src = int64_t(ok ? jt + r : j0) * kv_stride + c * 8;
+        cp_async16(smem_raw + off + swz(r, c), kbase + src, ok);
+        cp_async16(smem_raw + kVOff + off + swz(r, c), vbase + src, ok);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int t = 0; t < kStages - 1; ++t) issue_tile(t);
+
+  prologue<T, GC, FUSED>(a, sq, kh, hc, head0, has_new, 1.0f, q_s, knew_s, vnew_s);
+  __syncthreads();
+
+  // Q^T as the B operand (k = dims, n = heads): lane holds head n = lane/4 (zero when
+  // n >= GC), dims 2(lane%4)+{0,1} and +8 of every 16-dim k-step.
+  const int gid = lane >> 2, tig = lane & 3;
+  uint32_t qb[4][2];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const int d0 = kk * 16 + 2 * tig;
+    if (gid < GC) {
+      qb[kk][0] = pack_h2(q_s[gid][d0], q_s[gid][d0 + 1]);
+      qb[kk][1] = pack_h2(q_s[gid][d0 + 8], q_s[gid][d0 + 9]);
+    } else {
+      qb[kk][0] = qb[kk][1] = 0u;
+    }
+  }
+  // Running state for heads 2*tig, 2*tig+1 (columns of the accumulator fragments).
+  float m_run[2] = {kNegBig, kNegBig}, l_run[2] = {0.f, 0.f};
+  float o[4][4];  // O^T tiles: dims 16i + gid (+8), heads 2*tig + {0,1}
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  const float sl2 = a.scale_log2;
+  const int mi = lane >> 3;
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    cp_async_wait<kStages - 2>();
+    __syncthreads();  // tile landed for every thread; slot (tile-1) % kStages is free again
+    issue_tile(tile + kStages - 1);
+    const uint32_t off = (tile % kStages) * (kTile * 2);
+    const int jt = j0 + tile * kStageKeys;
+    if (FUSED && has_new && sq.past >= jt && sq.past < jt + kStageKeys) {
+      // the new token's k/v (computed in the prologue) replace the zero-filled ring row
+      const int r = sq.past - jt;
+      if (tid < 16) {
+        const int c = tid & 7;
+        const float* src = (tid < 8 ? knew_s : vnew_s) + c * 8;
+        const uint4 val = make_uint4(pack_h2(src[0], src[1]), pack_h2(src[2], src[3]),
+                                     pack_h2(src[4], src[5]), pack_h2(src[6], src[7]));
+        *reinterpret_cast<uint4*>(smem_raw + (tid < 8 ? 0u : kVOff) + off + swz(r, c)) = val;
+      }
+      __syncthreads();
+    }
+    const int rw = warp * 16;  // this warp's 16 keys of the tile
+    // ---- S^T = K Q^T (4 k-steps over the 64 dims)
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int r = rw + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t af[4];
+        ldsm_x4(ring + off + swz(r, kk * 2 + (mi >> 1)), af);
+        mma16816(sacc, af, qb[kk][0], qb[kk][1]);
+      }
+    }
+    // ---- online softmax on the fragment: keys rw+gid (sacc 0,1) and rw+gid+8 (sacc 2,3)
+    const bool v0 = jt + rw + gid < j1, v1 = jt + rw + gid + 8 < j1;
+    const float t0 = v0 ? sacc[0] * sl2 : -INFINITY;
+    const float t1 = v0 ? sacc[1] * sl2 : -INFINITY;
+    const float t2 = v1 ? sacc[2] * sl2 : -INFINITY;
+    const float t3 = v1 ? sacc[3] * sl2 : -INFINITY;
+    float mb0 = fmaxf(t0, t2), mb1 = fmaxf(t1, t3);
+#pragma unroll
+    for (int sh = 4; sh <= 16; sh <<= 1) {
+      mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, sh));
+      mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, sh));
+    }
+    const float mn0 = fmaxf(m_run[0], mb0), mn1 = fmaxf(m_run[1], mb1);
+    const float c0 = fast_exp2(m_run[0] - mn0), c1 = fast_exp2(m_run[1] - mn1);
+    m_run[0] = mn0;
+    m_run[1] = mn1;
+    const float p0 = fast_exp2(t0 - mn0), p1 = fast_exp2(t1 - mn1);
+    const float p2 = fast_exp2(t2 - mn0), p3 = fast_exp2(t3 - mn1);
+    l_run[0] = fmaf(l_run[0], c0, p0 + p2);
+    l_run[1] = fmaf(l_run[1], c1, p1 + p3);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o[i][0] *= c0;
+      o[i][1] *= c1;
+      o[i][2] *= c0;
+      o[i][3] *= c1;
+    }
+    // P^T as the B operand: the f16 accumulator fragment transposed in registers
+    const uint32_t pb0 = movmatrix_trans(pack_h2(p0, p1));
+    const uint32_t pb1 = movmatrix_trans(pack_h2(p2, p3));
+    // ---- O^T += V^T P^T (4 m-tiles of 16 dims)
+    {
+      const int r = rw + (mi >> 1) * 8 + (lane & 7);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t af[4];
+        ldsm_x4_trans(ring + kVOff + off + swz(r, 2 * i + (mi & 1)), af);
+        mma16816(o[i], af, pb0, pb1);
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // ---- warp totals: sum l over the 8 lanes that share a head column, then publish
+#pragma unroll
+  for (int sh = 4; sh <= 16; sh <<= 1) {
+    l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], sh);
+    l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], sh);
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int g = 2 * tig + e;
+    if (g < GC) {
+      if (gid == 0) {
+        red_m[warp][g] = m_run[e];
+        red_l[warp][g] = l_run[e];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        red_acc[warp][g][16 * i + gid] = o[i][e];
+        red_acc[warp][g][16 * i + gid + 8] = o[i][2 + e];
+      }
+    }
+  }
+  __syncthreads();
+  finish<T, GC>(a, sq.orow + int64_t(head0) * D, z * gridDim.y + blockIdx.y, split, nsplit,
+                ngrid, red_m, red_l, red_acc, &s_last);
+}
+
+// ---- CUDA-core kernel (fp32 storage) ----------------------------------------------------------
 template <int G, int NU>
 __device__ __forceinline__ void softmax_update(float (&s)[NU][G], const bool (&valid)[NU],
                                                const float (&vf)[NU][8], float (&m_run)[G],
@@ -50,12 +434,12 @@ __device__ __forceinline__ void softmax_update(float (&s)[NU][G], const bool (&v
     for (int u = 0; u < NU; ++u)
       if (valid[u]) mb = fmaxf(mb, s[u][g]);
     const float mn = fmaxf(m_run[g], mb);
-    const float c = exp2f(m_run[g] - mn);
+    const float c = fast_exp2(m_run[g] - mn);
     m_run[g] = mn;
     float psum = 0.f;
 #pragma unroll
     for (int u = 0; u < NU; ++u) {
-      s[u][g] = valid[u] ? exp2f(s[u][g] - mn) : 0.f;  // s now holds p
+      s[u][g] = valid[u] ? fast_exp2(s[u][g] - mn) : 0.f;  // s now holds p
       psum += s[u][g];
     }
     l_run[g] = fmaf(l_run[g], c, psum);
@@ -95,15 +479,16 @@ __device__ __forceinline__ void reduce_slot(float (&s)[G]) {
   }
 }
 
-// G: query heads per kv head; GC: query heads handled by one CTA (G / GC head chunks).
-template <class T, int G, bool FUSED, int MODE>
-__global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_constant__ DecodeArgs a) {
+template <int G, bool FUSED, int MODE>
+__global__ void __launch_bounds__(kThreads, 2)
+    decode_simt_kernel(const __grid_constant__ DecodeArgs a) {
+  using T = float;
   constexpr int D = kHeadDim;
   constexpr int GC = G > 4 ? 4 : G;
   constexpr int NHC = G / GC;
   constexpr int kStages = Ring<T>::kStages;
   constexpr int kTile = Ring<T>::kTileElems;
-  constexpr int kCopies = int(sizeof(T)) * 8 / 16;  // 16-byte copies per 8-element chunk
+  constexpr int kKeysPerThread = kStageKeys / 16;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   T* k_s = reinterpret_cast<T*>(smem_raw);
   T* v_s = k_s + kStages * kTile;
@@ -112,44 +497,21 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
   const int slot = lane >> 3, part = lane & 7;
   const int split = blockIdx.x, z = blockIdx.z;
   const int kh = blockIdx.y / NHC, hc = blockIdx.y % NHC;
-  const int head0 = kh * G + hc * GC;  // first q head of this CTA
+  const int head0 = kh * G + hc * GC;
   const int ngrid = gridDim.x;
-
-  int past;
-  const T* qrow;
-  const T* nw;
-  T* kc;
-  T* vc;
-  T* orow;
-  if (MODE == kLayers) {
-    const DecodeLayer& L = a.layers[z];
-    past = a.meta ? int(a.meta[0]) : a.pos_host;
-    qrow = static_cast<const T*>(L.qkv);
-    nw = static_cast<const T*>(L.norm_w);
-    kc = static_cast<T*>(L.k_cache);
-    vc = static_cast<T*>(L.v_cache);
-    orow = static_cast<T*>(L.out);
-  } else {
-    past = a.past[z];
-    qrow = static_cast<const T*>(a.qkv) + int64_t(z) * a.ld_qkv;
-    nw = static_cast<const T*>(a.norm_w);
-    const int64_t row0 = int64_t(a.offsets[z]) * a.hkv * D;
-    kc = static_cast<T*>(a.k_cache) + row0;
-    vc = static_cast<T*>(a.v_cache) + row0;
-    orow = static_cast<T*>(a.out) + int64_t(z) * a.ld_o;
-  }
-  if (MODE == kLayers && int64_t(past) >= a.kv_cap) {  // refuse rows beyond the cache
-    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
+  const Seq<T> sq = resolve<T, MODE>(a, z);
+  if (MODE == kLayers && int64_t(sq.past) >= a.kv_cap) {
+    if (tid == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
     return;
   }
-  const int len = past + 1;  // keys 0..past, key `past` is the new token
+  const int len = sq.past + 1;
   const int split_len = max(a.min_split, (ceil_div(len, ngrid) + 15) & ~15);
   const int nsplit = ceil_div(len, split_len);
   if (split >= nsplit) return;
   const int j0 = split * split_len;
   const int j1 = min(j0 + split_len, len);
   const bool has_new = FUSED && (j1 == len);
-  const int jend = has_new ? past : j1;  // keys streamed from the cache
+  const int jend = has_new ? sq.past : j1;
   const int64_t kv_stride = int64_t(a.hkv) * D;
 
   __shared__ float q_s[GC][D];
@@ -160,9 +522,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
   __shared__ float red_acc[kWarps][GC][D];
   __shared__ int s_last;
 
-  // ---- start streaming K/V rows [j0, jend) of kv head kh --------------------------------
-  const T* kbase = kc + kh * D;
-  const T* vbase = vc + kh * D;
+  const T* kbase = sq.kc + kh * D;
+  const T* vbase = sq.vc + kh * D;
   const int n_tiles = ceil_div(max(jend - j0, 0), kStageKeys);
   auto issue_tile = [&](int tile) {
     if (tile < n_tiles) {
@@ -175,8 +536,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
         const bool ok = jt + r < jend;
         const int64_t src = int64_t(ok ? jt + r : j0) * kv_stride;
 #pragma unroll
-        for (int c = 0; c < kCopies; ++c) {
-          const int e = part * 8 + c * (16 / int(sizeof(T)));
+        for (int c = 0; c < 2; ++c) {
+          const int e = part * 8 + c * 4;
           cp_async16(ks + r * D + e, kbase + src + e, ok);
           cp_async16(vs + r * D + e, vbase + src + e, ok);
         }
@@ -187,49 +548,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
 #pragma unroll
   for (int t = 0; t < kStages - 1; ++t) issue_tile(t);
 
-  // ---- prologue (overlaps the first copies): rotated q heads and, fused, the new k/v -----
-  if (FUSED) {
-    const T* rope = static_cast<const T*>(a.rope) + int64_t(past) * D;
-    const float cs = to_f32(rope[lane]);
-    const float sn = to_f32(rope[32 + lane]);
-    const int units = GC + (has_new ? 2 : 0);
-    for (int u = warp; u < units; u += kWarps) {
-      if (u < GC) {  // QK_PREP q unit, then ATTN's f32(q) * scale (kernels.js:255-263, :283)
-        const int64_t off = int64_t(head0 + u) * D;
-        float r0, r1;
-        norm_rope_head<T>(to_f32(qrow[off + lane]), to_f32(qrow[off + lane + 32]), nw,
-                          nw != nullptr, a.eps, cs, sn, r0, r1);
-        q_s[u][lane] = round_st<T>(r0) * a.scale_log2;
-        q_s[u][lane + 32] = round_st<T>(r1) * a.scale_log2;
-      } else if (u == GC) {  // QK_PREP k unit -> cache row `past`
-        const int64_t off = int64_t(a.hq + kh) * D;
-        float r0, r1;
-        norm_rope_head<T>(to_f32(qrow[off + lane]), to_f32(qrow[off + lane + 32]),
-                          nw ? nw + D : nullptr, nw != nullptr, a.eps, cs, sn, r0, r1);
-        const T k0 = from_f32<T>(r0), k1 = from_f32<T>(r1);
-        if (hc == 0) {
-          T* dst = kc + int64_t(past) * kv_stride + kh * D;
-          dst[lane] = k0;
-          dst[lane + 32] = k1;
-        }
-        knew_s[lane] = to_f32(k0);
-        knew_s[lane + 32] = to_f32(k1);
-      } else {  // QK_PREP v unit: raw copy -> cache row `past`
-        const int64_t off = int64_t(a.hq + a.hkv + kh) * D;
-        const T x0 = qrow[off + lane], x1 = qrow[off + lane + 32];
-        if (hc == 0) {
-          T* dst = vc + int64_t(past) * kv_stride + kh * D;
-          dst[lane] = x0;
-          dst[lane + 32] = x1;
-        }
-        vnew_s[lane] = to_f32(x0);
-        vnew_s[lane + 32] = to_f32(x1);
-      }
-    }
-  } else {
-    for (int i = tid; i < GC * D; i += kThreads)
-      q_s[i / D][i % D] = to_f32(qrow[int64_t(head0) * D + i]) * a.scale_log2;
-  }
+  prologue<T, GC, FUSED>(a, sq, kh, hc, head0, has_new, a.scale_log2, q_s, knew_s, vnew_s);
   __syncthreads();
 
   float qr[GC][8];
@@ -246,10 +565,9 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
     for (int i = 0; i < 8; ++i) acc[g][i] = 0.f;
   }
 
-  // ---- main loop over the ring ------------------------------------------------------------
   for (int tile = 0; tile < n_tiles; ++tile) {
     cp_async_wait<kStages - 2>();
-    __syncthreads();  // tile landed for every thread; slot (tile-1) % kStages is free again
+    __syncthreads();
     issue_tile(tile + kStages - 1);
     const T* ks = k_s + (tile % kStages) * kTile;
     const T* vs = v_s + (tile % kStages) * kTile;
@@ -274,8 +592,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
   }
   cp_async_wait<0>();
 
-  // ---- the new token (fused, last split): its k/v are in shared memory -------------------
-  if (FUSED && has_new && warp == 0) {
+  if (FUSED && has_new && warp == 0) {  // the new token: its k/v are in shared memory
     float kf[8], vfn[1][8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -289,7 +606,6 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
     softmax_update<GC, 1>(s1, v1, vfn, m_run, l_run, acc);
   }
 
-  // ---- merge the 4 slots of each warp, then the 4 warps ----------------------------------
 #pragma unroll
   for (int off = 8; off <= 16; off <<= 1) {
 #pragma unroll
@@ -297,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
       const float mo = __shfl_xor_sync(0xffffffffu, m_run[g], off);
       const float lo = __shfl_xor_sync(0xffffffffu, l_run[g], off);
       const float mn = fmaxf(m_run[g], mo);
-      const float c1 = exp2f(m_run[g] - mn), c2 = exp2f(mo - mn);
+      const float c1 = fast_exp2(m_run[g] - mn), c2 = fast_exp2(mo - mn);
       l_run[g] = l_run[g] * c1 + lo * c2;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -319,61 +635,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
     }
   }
   __syncthreads();
-
-  T* out_h = orow + int64_t(head0) * D;
-  const int pair = z * gridDim.y + blockIdx.y;
-  float* part_base = a.partials + int64_t(pair) * ngrid * (GC * kPartialStride);
-  for (int idx = tid; idx < GC * D; idx += kThreads) {
-    const int g = idx / D, d = idx % D;
-    float mx = red_m[0][g];
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, red_m[w][g]);
-    float l = 0.f, ac = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float c = exp2f(red_m[w][g] - mx);
-      l = fmaf(red_l[w][g], c, l);
-      ac = fmaf(red_acc[w][g][d], c, ac);
-    }
-    if (nsplit == 1) {
-      out_h[idx] = from_f32<T>(ac / l);  // kernels.js:317
-    } else {
-      float* p = part_base + int64_t(split) * (GC * kPartialStride) + g * kPartialStride;
-      p[d] = ac;
-      if (d == 0) {
-        p[D] = mx;
-        p[D + 1] = l;
-      }
-    }
-  }
-  if (nsplit == 1) return;
-
-  // ---- second pass: the last CTA of this (sequence, head chunk) combines the partials ----
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int prev = atomicAdd(&a.counters[pair], 1);
-    s_last = (prev == nsplit - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int idx = tid; idx < GC * D; idx += kThreads) {
-    const int g = idx / D, d = idx % D;
-    const float* p0 = part_base + g * kPartialStride;
-    float mx = kNegBig;
-    for (int sp = 0; sp < nsplit; ++sp)
-      mx = fmaxf(mx, __ldcg(p0 + int64_t(sp) * (GC * kPartialStride) + D));
-    float l = 0.f, ac = 0.f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float* p = p0 + int64_t(sp) * (GC * kPartialStride);
-      const float c = exp2f(__ldcg(p + D) - mx);
-      l = fmaf(__ldcg(p + D + 1), c, l);
-      ac = fmaf(__ldcg(p + d), c, ac);
-    }
-    out_h[idx] = from_f32<T>(ac / l);
-  }
-  if (tid == 0) a.counters[pair] = 0;
+  finish<T, GC>(a, sq.orow + int64_t(head0) * D, z * gridDim.y + blockIdx.y, split, nsplit,
+                ngrid, red_m, red_l, red_acc, &s_last);
 }
 
 struct KernelInfo {
@@ -381,24 +644,33 @@ struct KernelInfo {
   int smem;
 };
 
-template <class T, int G, bool FUSED, int MODE>
-KernelInfo info() {
-  return {reinterpret_cast<const void*>(&decode_kernel<T, G, FUSED, MODE>), Ring<T>::kBytes};
+template <int G, bool FUSED, int MODE>
+KernelInfo info_h() {
+  return {reinterpret_cast<const void*>(&decode_mma_kernel<G, FUSED, MODE>),
+          Ring<__half>::kBytes};
+}
+template <int G, bool FUSED, int MODE>
+KernelInfo info_f() {
+  return {reinterpret_cast<const void*>(&decode_simt_kernel<G, FUSED, MODE>),
+          Ring<float>::kBytes};
 }
 
-template <class T, int G>
-KernelInfo pick_fm(bool fused, int mode) {
-  if (mode == kLayers) return fused ? info<T, G, true, kLayers>() : info<T, G, false, kLayers>();
-  return fused ? info<T, G, true, kRagged>() : info<T, G, false, kRagged>();
+template <int G>
+KernelInfo pick_fm(bool half, bool fused, int mode) {
+  if (half) {
+    if (mode == kLayers) return fused ? info_h<G, true, kLayers>() : info_h<G, false, kLayers>();
+    return fused ? info_h<G, true, kRagged>() : info_h<G, false, kRagged>();
+  }
+  if (mode == kLayers) return fused ? info_f<G, true, kLayers>() : info_f<G, false, kLayers>();
+  return fused ? info_f<G, true, kRagged>() : info_f<G, false, kRagged>();
 }
 
-template <class T>
-KernelInfo pick_g(int group, bool fused, int mode) {
+KernelInfo pick(int group, bool half, bool fused, int mode) {
   switch (group) {
-    case 1: return pick_fm<T, 1>(fused, mode);
-    case 2: return pick_fm<T, 2>(fused, mode);
-    case 4: return pick_fm<T, 4>(fused, mode);
-    case 8: return pick_fm<T, 8>(fused, mode);
+    case 1: return pick_fm<1>(half, fused, mode);
+    case 2: return pick_fm<2>(half, fused, mode);
+    case 4: return pick_fm<4>(half, fused, mode);
+    case 8: return pick_fm<8>(half, fused, mode);
     default: return {nullptr, 0};
   }
 }
@@ -437,8 +709,7 @@ int decode_max_splits(int64_t max_len, int hkv, int nz, int num_sms, int* min_sp
 cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, int max_splits,
                           int nz, cudaStream_t s) {
   const int group = a.hq / a.hkv;
-  const KernelInfo k =
-      dtype == 0 ? pick_g<__half>(group, fused, mode) : pick_g<float>(group, fused, mode);
+  const KernelInfo k = pick(group, dtype == 0, fused, mode);
   if (!k.fn) return cudaErrorInvalidValue;
   static std::mutex mu;
   static std::set<const void*> configured;
