@@ -443,6 +443,25 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def run_only(ctx, args):
+    """One leg, one GPU, minimal setup: the commands the profiler wraps."""
+    import torch
+    if args.only == "decode":
+        wl = DecodeWorkload(ctx, 0, copies=4)
+        ms = timed_loop(wl.step, args.steps, args.warmup, 1, torch.cuda.current_stream())
+        res = {"us_per_step": ms * 1e3, "gbs": wl.bytes_per_step / (ms * 1e-3) / 1e9}
+    elif args.only == "ragged":
+        ms, b = run_ragged(ctx, 0, 1, args.steps, args.warmup)
+        res = {"ms_per_step": ms, "gbs": b / (ms * 1e-3) / 1e9}
+    elif args.only == "prefill":
+        pa, pb = run_prefill(ctx, args.steps, args.warmup)
+        res = {"us_attn": pa * 1e3, "tflops_attn": prefill_flops(2048) / (pa * 1e-3) / 1e12}
+    else:
+        va = run_vision(ctx, args.steps, args.warmup)
+        res = {"us": va * 1e3, "tflops": vision_flops() / (va * 1e-3) / 1e12}
+    print(json.dumps({"only": args.only, **res}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -451,6 +470,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip prefill/vision/ragged legs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--only", choices=["decode", "ragged", "prefill", "vision"],
+                    help="run one leg on one GPU and print its timing (profiling commands)")
     ap.add_argument("--quick", action="store_true",
                     help="headline kernel only (no e2e, side legs, CPU leg or clock tail); "
                          "the profiling command")
@@ -465,6 +486,10 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     import p2p_b200
     ctx = p2p_b200.Context(local)
+    if args.only:
+        run_only(ctx, args)
+        ctx.close()
+        return
     stream = torch.cuda.current_stream()
     hbm_peak, tensor_peak, peak_kind = load_peaks()
     traffic = load_traffic()
