@@ -190,16 +190,42 @@ def timed_loop(fn, steps, warmup, world, stream):
     return start.elapsed_time(end) / steps  # ms per step on this rank
 
 
+def timed_graph(fn, steps, warmup, world):
+    """Warm up with direct calls, capture `steps` calls into one CUDA graph, then time one
+    replay (the K steps back to back on the device, no host launch overhead)."""
+    import torch
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(steps):
+            fn(warmup + i)
+    g.replay()  # untimed: first replay uploads the graph
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    g.replay()
+    end.record(stream)
+    end.synchronize()
+    barrier(world)
+    del g
+    return start.elapsed_time(end) / steps
+
+
 class DecodeWorkload:
     """6 independent LFM2.5-1.2B attention layers at context 4096 (+1), R rotating copies."""
 
-    def __init__(self, ctx, rank, copies=12):
+    def __init__(self, ctx, rank, copies=12, past=PAST):
         import torch
         import p2p_b200
         self.torch = torch
         self.prm = p2p_b200.Params(HQ, HKV)
         self.ctx = ctx
-        cap = PAST + 1
+        cap = past + 1
         self.cap = cap
         g = torch.Generator(device="cuda").manual_seed(1234 + rank)
         self.rope = ctx.rope_table(cap, D, 1e6)
@@ -215,15 +241,16 @@ class DecodeWorkload:
                                dtype=torch.float16)
         self.nw = (1 + 0.1 * torch.randn((N_LAYERS, 2 * D), generator=g, device="cuda")).half()
         self.out = torch.zeros((N_LAYERS, HQ * D), device="cuda", dtype=torch.float16)
-        self.layer_sets = [
-            [(self.qkv[l], self.nw[l], kc, vc, self.out[l]) for l, (kc, vc) in enumerate(c)]
+        self.plans = [
+            ctx.plan_decode_step(self.prm, [(self.qkv[l], self.nw[l], kc, vc, self.out[l])
+                                            for l, (kc, vc) in enumerate(c)],
+                                 self.rope, cap, use_meta=True)
             for c in self.copies]
-        ctx.meta_write(PAST, 1, 0, stream=torch.cuda.current_stream())
-        self.bytes_per_step = N_LAYERS * decode_layer_bytes()
+        ctx.meta_write(past, 1, 0, stream=torch.cuda.current_stream())
+        self.bytes_per_step = N_LAYERS * decode_layer_bytes(past)
 
     def step(self, i):
-        self.ctx.decode_step(self.prm, self.layer_sets[i % len(self.layer_sets)], self.rope,
-                             self.cap, use_meta=True)
+        self.plans[i % len(self.plans)].run()
 
 
 def e2e_decode(wl, steps, warmup):
@@ -290,7 +317,7 @@ def run_ragged(ctx, rank, world, steps, warmup):
         ctx.attn_decode_ragged(prm, qkv, nw, rope, kc, vc, off_d, past_d, out,
                                max_past=int(past_all.max()), fused_prep=True)
 
-    ms = timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
+    ms = timed_graph(step, steps, warmup, world)
     my_bytes = float(rows.sum() * HKV * D * 2 * 2 + nseq * ((HQ + 2 * HKV) * D * 2 + 2 * HKV * D * 2
                                                           + HQ * D * 2))
     del kc, vc
@@ -323,8 +350,8 @@ def run_prefill(ctx, steps, warmup):
         ctx.qk_prep(prm, qkv[i % copies], None, rope, q, kc, vc, pos0=0, m_tokens=s)
         ctx.attn(prm, q, kc, vc, out, pos0=0, m_tokens=s)
 
-    ms_attn = timed_loop(attn_only, steps, warmup, 1, stream)
-    ms_both = timed_loop(prep_and_attn, steps, warmup, 1, stream)
+    ms_attn = timed_graph(attn_only, steps, warmup, 1)
+    ms_both = timed_graph(prep_and_attn, steps, warmup, 1)
     return ms_attn, ms_both
 
 
@@ -341,7 +368,7 @@ def run_vision(ctx, steps, warmup):
     def step(i):
         ctx.attn_bidir(prm, q, k, v, out)
 
-    return timed_loop(step, steps, warmup, 1, torch.cuda.current_stream())
+    return timed_graph(step, steps, warmup, 1)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -447,8 +474,8 @@ def run_only(ctx, args):
     """One leg, one GPU, minimal setup: the commands the profiler wraps."""
     import torch
     if args.only == "decode":
-        wl = DecodeWorkload(ctx, 0, copies=4)
-        ms = timed_loop(wl.step, args.steps, args.warmup, 1, torch.cuda.current_stream())
+        wl = DecodeWorkload(ctx, 0, copies=4, past=args.past)
+        ms = timed_graph(wl.step, args.steps, args.warmup, 1)
         res = {"us_per_step": ms * 1e3, "gbs": wl.bytes_per_step / (ms * 1e-3) / 1e9}
     elif args.only == "ragged":
         ms, b = run_ragged(ctx, 0, 1, args.steps, args.warmup)
@@ -472,6 +499,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--only", choices=["decode", "ragged", "prefill", "vision"],
                     help="run one leg on one GPU and print its timing (profiling commands)")
+    ap.add_argument("--past", type=int, default=PAST, help="decode context for --only decode")
     ap.add_argument("--quick", action="store_true",
                     help="headline kernel only (no e2e, side legs, CPU leg or clock tail); "
                          "the profiling command")
@@ -500,7 +528,8 @@ def main():
     if args.quick:
         args.no_side = args.no_cpu = True
     with ClockSampler(gpu_index) as clk:
-        ms = timed_loop(wl.step, args.steps, args.warmup, world, stream)
+        ms = timed_graph(wl.step, args.steps, args.warmup, world)
+        ms_direct = timed_loop(wl.step, args.steps, args.warmup, world, stream)
         # keep the same kernel under load ~1.5 s so the 200 ms clock sampler sees the timed state
         t_end = time.perf_counter() + (0.0 if args.quick else 1.5)
         i = 0
@@ -572,12 +601,15 @@ def main():
             "metric": "decode_attn_gbs_ctx4096", "value": round(value_gbs, 1), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_max, 5), "us_per_step": round(ms_max * 1e3, 3),
+            "us_per_step_direct_launch": round(max_over_ranks(ms_direct, world) * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded N(0,1), torch CUDA generator)",
             "config": {"workload": "lfm2.5-1.2b decode attention, ctx 4096+1, 6 layers, 32q/8kv, "
                                    "d64, fused qk-prep + split-KV, one launch per step",
                        "past": PAST, "layers": N_LAYERS, "bytes_per_step_per_gpu": wl.bytes_per_step,
                        "l2": "inputs rotate over 12 KV copies (605 MB > L2)",
+                       "timing": "K steps captured in one CUDA graph, one replay timed with "
+                                 "CUDA events; us_per_step_direct_launch = K host calls",
                        "parallelism": f"replicas x{world} (independent sequences per GPU)"},
             "roofline": {"bound": "hbm", "achieved": round(per_gpu_gbs, 1),
                          "peak": hbm_peak, "unit": "GB/s",

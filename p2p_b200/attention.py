@@ -135,6 +135,11 @@ class Context:
             rope if isinstance(rope, C.c_void_p) else _ptr(rope), kv_cap,
             self.meta_ptr if use_meta else None, pos, _stream(stream)))
 
+    def plan_decode_step(self, prm: Params, layers: Sequence[tuple], rope, kv_cap: int, *,
+                         pos: int = 0, use_meta: bool = False) -> "DecodeStepPlan":
+        """Builds the C arguments of decode_step once; plan.run() is one ctypes call."""
+        return DecodeStepPlan(self, prm, layers, rope, kv_cap, pos, use_meta)
+
     def attn_decode_ragged(self, prm: Params, qkv: torch.Tensor, norm_w, rope,
                            k_cache: torch.Tensor, v_cache: torch.Tensor, offsets: torch.Tensor,
                            past: torch.Tensor, out: torch.Tensor, *, max_past: int,
@@ -152,6 +157,28 @@ class Context:
         b, s, ld = q.shape
         self._chk(lib.p2p_attn_bidir(self.h, C.byref(prm.c()), _ptr(q), _ptr(k), _ptr(v),
                                      _ptr(out), ld, b, s, _stream(stream)))
+
+
+class DecodeStepPlan:
+    """Pre-marshalled arguments of p2p_decode_step (the per-token call of a decode loop)."""
+
+    def __init__(self, ctx: Context, prm: Params, layers, rope, kv_cap, pos, use_meta):
+        self.ctx = ctx
+        self.keep = list(layers)  # keeps the tensors alive
+        self.arr = (DecodeLayer * len(layers))()
+        for i, (qkv, nw, kc, vc, out) in enumerate(layers):
+            self.arr[i] = DecodeLayer(qkv.data_ptr(), nw.data_ptr() if nw is not None else None,
+                                      kc.data_ptr(), vc.data_ptr(), out.data_ptr())
+        self.prm = prm.c()
+        self.rope = rope if isinstance(rope, C.c_void_p) else _ptr(rope)
+        self.args = (ctx.h, C.byref(self.prm), len(layers), self.arr, self.rope, kv_cap,
+                     ctx.meta_ptr if use_meta else None, pos)
+        self.fn = lib.p2p_decode_step
+
+    def run(self, stream=None):
+        st = self.fn(*self.args, _stream(stream))
+        if st:
+            self.ctx._chk(st)
 
 
 class KVCache:

@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -178,12 +179,25 @@ uint16_t half_bits(float f) {
   return b;
 }
 
+// Tuning knob: P2P_DECODE_SPLITS=<n> forces n key splits per (sequence, kv head).
+int forced_splits() {
+  static const int v = [] {
+    const char* e = std::getenv("P2P_DECODE_SPLITS");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
 p2p_status run_decode(p2p_ctx* ctx, const p2p_attn_params* prm, p2p::DecodeArgs& a, int mode,
                       bool fused, int nz, int64_t max_len, cudaStream_t s) {
   const int hkv = prm->num_kv_heads;
   const int group = prm->num_heads / hkv;
   int min_split = 16;
-  const int splits = p2p::decode_max_splits(max_len, hkv, nz, ctx->num_sms, &min_split);
+  int splits = p2p::decode_max_splits(max_len, hkv, nz, ctx->num_sms, &min_split);
+  if (forced_splits() > 0) {
+    splits = forced_splits();
+    min_split = 16;
+  }
   p2p_status st = ensure_workspace(ctx, p2p::decode_partials_bytes(splits, hkv, nz, group),
                                    p2p::decode_counters_bytes(hkv, nz), s);
   if (st != P2P_OK) return st;
