@@ -163,6 +163,26 @@ p2p_status p2p_attn_bidir(p2p_ctx* ctx, const p2p_attn_params* prm, const void* 
                           const void* k, const void* v, void* out, int64_t ld, int32_t batch,
                           int32_t s_tokens, void* stream);
 
+/* No counterpart in the reference.  The same operation as p2p_attn_decode_ragged (same
+ * arguments, same kernel) for callers that cannot allocate device memory while serving:
+ * processes that hand nearly all free HBM to their own pool at start-up, and hosts whose device
+ * memory belongs to another component.  It never calls cudaMalloc/cudaFree: the split-KV
+ * scratch lives in a fixed array of P2P_NOALLOC_SCRATCH_BYTES inside the library, which every
+ * GPU that loads the library holds until the process exits.  A request whose scratch
+ * (nseq x kv heads x splits x up to 4 heads x 66 floats, plus counters) exceeds it returns
+ * P2P_ERR_INVALID_ARG with the sizes in p2p_last_error().  The first call on a device looks
+ * up the array's device address (and may load the library's device code), so make that call
+ * before capturing anything into a CUDA graph.  All calls share the array: calls that overlap
+ * on the GPU (other streams, other contexts on the same device) race and must be ordered by
+ * the caller. */
+#define P2P_NOALLOC_SCRATCH_BYTES (32u << 20)
+p2p_status p2p_attn_decode_ragged_noalloc(p2p_ctx* ctx, const p2p_attn_params* prm,
+                                          const void* qkv, int64_t ld_qkv, const void* norm_w,
+                                          const void* rope, void* k_cache, void* v_cache,
+                                          const int32_t* offsets, const int32_t* past,
+                                          int32_t nseq, int32_t max_past, int32_t fused_prep,
+                                          void* out, int64_t ld_o, void* stream);
+
 /* Test hook, no counterpart in the reference: cap this process's device allocations made by
  * the library at `bytes` (< 0 removes the cap), so the P2P_ERR_OOM paths can be exercised
  * without exhausting a shared GPU. */

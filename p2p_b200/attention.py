@@ -151,6 +151,19 @@ class Context:
             _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep), _ptr(out),
             out.stride(0), _stream(stream)))
 
+    def attn_decode_ragged_noalloc(self, prm: Params, qkv: torch.Tensor, norm_w, rope,
+                                   k_cache: torch.Tensor, v_cache: torch.Tensor,
+                                   offsets: torch.Tensor, past: torch.Tensor, out: torch.Tensor,
+                                   *, max_past: int, fused_prep: bool = True, stream=None):
+        """attn_decode_ragged without any device allocation: the split scratch is the
+        library's fixed array of P2P_NOALLOC_SCRATCH_BYTES (see include/p2p_attn.h)."""
+        assert offsets.dtype == torch.int32 and past.dtype == torch.int32
+        self._chk(lib.p2p_attn_decode_ragged_noalloc(
+            self.h, C.byref(prm.c()), _ptr(qkv), qkv.stride(0), _ptr(norm_w),
+            rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(k_cache), _ptr(v_cache),
+            _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep), _ptr(out),
+            out.stride(0), _stream(stream)))
+
     def attn_bidir(self, prm: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    out: torch.Tensor, stream=None):
         """q/k/v/out: [B][S][ld] (vision-kernels.js:198 layout)."""

@@ -677,3 +677,16 @@ p2p_status p2p_attn_bidir(p2p_ctx* ctx, const p2p_attn_params* prm, const void* 
 }
 
 }  // extern "C"
+
+namespace p2p {
+int ctx_device(const p2p_ctx* ctx) { return ctx->device; }
+int ctx_num_sms(const p2p_ctx* ctx) { return ctx->num_sms; }
+p2p_status ctx_fail(p2p_ctx* ctx, p2p_status s, const char* msg) { return fail(ctx, s, "%s", msg); }
+p2p_status ctx_check_params(p2p_ctx* ctx, const p2p_attn_params* prm) {
+  return check_params(ctx, prm, true);
+}
+float eff_scale_log2(const p2p_attn_params* prm) {
+  return eff_scale(prm) * 1.4426950408889634f;
+}
+float eff_eps_of(const p2p_attn_params* prm) { return eff_eps(prm); }
+}  // namespace p2p
