@@ -3,20 +3,24 @@
 // Replaces ATTN for M > 1 (causal GQA prefill over the KV cache,
 // src/scripts/lfm-engine/kernels.js:268-319) and VISION_ATTN (bidirectional MHA,
 // src/scripts/lfm-engine/vision-kernels.js:176-258).  Same math as the shaders -- scores
-// q.k * scale, running max / sum online softmax, P.V accumulated in f32, out = acc / sum in
-// f16 -- reorganised into 128 x 128 tiles:
+// q.k * scale, online softmax (running max / sum), P.V accumulated in f32, out = acc / sum in
+// f16 -- reorganised into 128 x 128 tiles on tcgen05 / TMEM / TMA:
 //
-//   CTA = one (image, q head, 128-row q tile); 6 warps.
-//   warp 4     TMA producer: Q tile once, then K/V tiles of 128 keys (SWIZZLE_128B) into a
-//              3-stage ring; mbarrier complete_tx signalling.  No multicast.
-//   warp 5     allocates 512 TMEM columns; one lane issues tcgen05.mma:
-//                S_j = Q K_j^T  -> TMEM S[j%2]   (M=128, N=128, K=64: 4 x K16 MMAs)
-//                O_j = P_j V_j  -> TMEM PV[j%2]  (M=128, N=64,  K=128: 8 x K16 MMAs)
-//              S_{j+1} is issued before O_j so QK^T of the next tile overlaps the softmax.
-//   warps 0-3  softmax, one thread per q row (= TMEM lane): tcgen05.ld of its S row, causal /
-//              length mask, running max, exp2, running sum, P_j rounded to f16 into shared
-//              memory in the 128B-swizzled K-major layout the MMA reads, then O kept in
-//              registers: O = O * alpha + PV_j.  Epilogue: O / sum -> f16 row store.
+//   CTA = one (image, q head, pair of 128-row q tiles); 10 warps.
+//   warp 8      TMA producer: the two Q tiles once, then K/V tiles of 128 keys (SWIZZLE_128B)
+//               into a 3-stage ring shared by both q tiles; mbarrier complete_tx.  No multicast.
+//   warp 9      allocates 512 TMEM columns; one lane issues tcgen05.mma (cta_group::1, f16):
+//                 S_w(j)  = Q_w K_j^T -> TMEM S_w   (M128 N128 K64)
+//                 O_w    += P_w(j) V_j -> TMEM O_w  (M128 N64 K128, V as an MN-major operand)
+//               S_w(j+1) is issued as soon as softmax warpgroup w has read S_w(j), so the
+//               tensor core computes it while the softmax of tile j runs.
+//   warps 0-3   softmax warpgroup 0 (q tile 0), warps 4-7 warpgroup 1 (q tile 1): one thread
+//               per q row (= TMEM lane).  tcgen05.ld of the S row; mask only on tiles that
+//               cross the causal diagonal / the key end; exp2 with the scale folded into one
+//               FFMA; P rounded to f16 into shared memory in the 128B-swizzled K-major layout
+//               the MMA reads.  O stays in TMEM; it is rescaled (tcgen05.ld/st) only when a
+//               row's max grows by more than 2^8 (lazy rescale: the final O / l is exact for
+//               any reference max), so most tiles skip it.
 //
 // Every mbarrier wait is bounded (about one second); a wait that gives up sets the device
 // error word, tells the other roles to stop, and the CTA still frees its TMEM and returns.
@@ -34,27 +38,29 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;  // q rows per tile
+constexpr int BM = 128;  // q rows per tile (two tiles per CTA)
 constexpr int BN = 128;  // keys per tile
 constexpr int D = kHeadDim;
 constexpr int kStages = 3;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // 10 warps: 0-7 softmax (two warpgroups), 8 TMA, 9 MMA
 constexpr uint32_t kTileBytes = BM * D * 2;  // one Q, K or V tile: 16 KB
 constexpr uint32_t kTmemCols = 512;
-// TMEM columns: S[0] 0..127, S[1] 128..255, PV[0] 256..319, PV[1] 320..383.
-__device__ __forceinline__ uint32_t col_s(int bf) { return bf ? 128u : 0u; }
-__device__ __forceinline__ uint32_t col_pv(int bf) { return bf ? 320u : 256u; }
 constexpr int kErrTimeout = 2;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (factor 256)
+
+// TMEM columns of q tile w: S at 256w (128 columns), O at 256w + 128 (64 columns).
+__device__ __forceinline__ uint32_t col_s(int w) { return uint32_t(w) * 256u; }
+__device__ __forceinline__ uint32_t col_o(int w) { return uint32_t(w) * 256u + 128u; }
 
 struct __align__(1024) Smem {
-  __half q[BM * D];
+  __half q[2][BM * D];
   __half k[kStages][BN * D];
   __half v[kStages][BN * D];
-  __half p[2][2][BM * 64];  // [buffer][key chunk of 64][128 rows x 64 keys], SW128 K-major
+  __half p[2][2][BM * 64];  // [q tile][key chunk of 64][128 rows x 64 keys], SW128 K-major
   uint64_t bar_q;
   uint64_t k_full[kStages], v_full[kStages], kv_empty[kStages];
-  uint64_t s_full[2], s_empty[2], p_full[2], pv_full[2];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
   uint32_t tmem_base;
   volatile int abort_flag;
 };
@@ -70,7 +76,7 @@ struct FlashParams {
   int32_t s_q, s_kv;
   int32_t hq, hkv;
   int32_t causal;
-  int32_t n_qtiles;
+  int32_t n_qpairs;
   float scale_log2;
 };
 
@@ -104,20 +110,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.causal ? (p.n_qtiles - 1 - int(blockIdx.x)) : int(blockIdx.x);
+  const int qp = p.causal ? (p.n_qpairs - 1 - int(blockIdx.x)) : int(blockIdx.x);
   const int h = blockIdx.y, b = blockIdx.z;
   const int kh = h / (p.hq / p.hkv);
   const int pos0 = p.causal ? (p.meta ? int(p.meta[0]) : p.pos0_host) : 0;
-  const int q_row0 = qt * BM;
-  const int q_rows = min(BM, p.s_q - q_row0);
-  // keys this tile needs: causal -> 0 .. pos0 + last row; bidirectional -> 0 .. s_kv - 1
-  const int64_t key_end = p.causal ? int64_t(pos0) + q_row0 + q_rows : int64_t(p.s_kv);
+  const int q_row0 = qp * 2 * BM;
+  // valid q rows of the two tiles and the keys each needs (causal: 0 .. pos0 + last row)
+  const int rows0 = min(BM, p.s_q - q_row0);
+  const int rows1 = max(0, min(BM, p.s_q - q_row0 - BM));
+  const int64_t kend0 = p.causal ? int64_t(pos0) + q_row0 + rows0 : int64_t(p.s_kv);
+  const int64_t kend1 =
+      rows1 == 0 ? 0 : (p.causal ? int64_t(pos0) + q_row0 + BM + rows1 : int64_t(p.s_kv));
+  const int64_t key_end = kend0 > kend1 ? kend0 : kend1;
   if (p.causal && key_end > p.kv_rows_total) {  // the cache does not hold these keys
     if (threadIdx.x == 0) atomicOr(p.err, kErrPosBeyondCache);
     return;
   }
-  const int n_kv = int((key_end + BN - 1) / BN);
-  const int last_valid = int(key_end - int64_t(n_kv - 1) * BN);  // valid rows of last tile
+  // KV tiles each q tile needs (no runtime-indexed local arrays: they would live in memory)
+  const int n_kv0 = int((kend0 + BN - 1) / BN);
+  const int n_kv1 = int((kend1 + BN - 1) / BN);
+  const int n_max = n_kv0 > n_kv1 ? n_kv0 : n_kv1;
+  const int last_valid = int(key_end - int64_t(n_max - 1) * BN);  // valid rows of last tile
 
   if (threadIdx.x == 0) {
     mbar_init(&s.bar_q, 1);
@@ -128,29 +141,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.s_full[i], 1);
-      mbar_init(&s.s_empty[i], 4);
+      mbar_init(&s.s_free[i], 4);
       mbar_init(&s.p_full[i], 4);
-      mbar_init(&s.pv_full[i], 1);
+      mbar_init(&s.pv_done[i], 1);
     }
     s.abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(&s.tmem_base, kTmemCols);
+  if (warp == 9) tmem_alloc(&s.tmem_base, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tensormap(&tm_q);
       prefetch_tensormap(&tm_k);
       prefetch_tensormap(&tm_v);
-      mbar_arrive_expect_tx(&s.bar_q, kTileBytes);
-      tma_load_2d(s.q, &tm_q, h * D, int32_t(int64_t(b) * p.bs_q + q_row0), &s.bar_q);
+      const int nq = rows1 > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(&s.bar_q, kTileBytes * nq);
+      for (int w = 0; w < nq; ++w)
+        tma_load_2d(s.q[w], &tm_q, h * D, int32_t(int64_t(b) * p.bs_q + q_row0 + w * BM),
+                    &s.bar_q);
       int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
+      for (int j = 0; j < n_max; ++j) {
         const int st = j % kStages;
         if (j >= kStages && !wait_bar(s, &s.kv_empty[st], ((j / kStages) - 1) & 1, p.err))
           break;
@@ -172,34 +188,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_s = idesc_f16_f32(BM, BN, 0, 0);
     constexpr uint32_t idesc_pv = idesc_f16_f32(BM, D, 0, 1);
-    const uint32_t q_addr = smem_u32(s.q);
     bool ok = wait_bar(s, &s.bar_q, 0, p.err);
-    auto issue_s = [&](int j) -> bool {
-      const int st = j % kStages, bf = j & 1;
-      if (!wait_bar(s, &s.k_full[st], (j / kStages) & 1, p.err)) return false;
-      if (j >= 2 && !wait_bar(s, &s.s_empty[bf], ((j >> 1) - 1) & 1, p.err)) return false;
-      tc_fence_after();
+    auto issue_s = [&](int w, int j) {  // S_w(j) = Q_w K_j^T
       if (lane == 0) {
-        const uint32_t k_addr = smem_u32(s.k[st]);
+        const uint32_t q_addr = smem_u32(s.q[w]);
+        const uint32_t k_addr = smem_u32(s.k[j % kStages]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          mma_f16_ss(tmem + col_s(bf), smem_desc_sw128(q_addr + kk * 32, 16, 1024),
+          mma_f16_ss(tmem + col_s(w), smem_desc_sw128(q_addr + kk * 32, 16, 1024),
                      smem_desc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0);
-        mma_commit(&s.s_full[bf]);
+        mma_commit(&s.s_full[w]);
       }
       __syncwarp();
-      return true;
     };
-    if (ok) ok = issue_s(0);
-    for (int j = 0; ok && j < n_kv; ++j) {
-      if (j + 1 < n_kv && !issue_s(j + 1)) break;
-      const int st = j % kStages, bf = j & 1;
+    if (ok) ok = wait_bar(s, &s.k_full[0], 0, p.err);
+    if (ok) {
+      tc_fence_after();
+      if (n_kv0 > 0) issue_s(0, 0);
+      if (n_kv1 > 0) issue_s(1, 0);
+    }
+    for (int j = 0; ok && j < n_max; ++j) {
+      const int st = j % kStages;
+      // next tile's scores, as soon as each warpgroup has read its S buffer
+      if (j + 1 < n_max) {
+        const int st1 = (j + 1) % kStages;
+        if (!wait_bar(s, &s.k_full[st1], ((j + 1) / kStages) & 1, p.err)) break;
+        for (int w = 0; w < 2 && ok; ++w) {
+          if (j + 1 >= (w ? n_kv1 : n_kv0)) continue;
+          if (!wait_bar(s, &s.s_free[w], j & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(w, j + 1);
+        }
+        if (!ok) break;
+      }
       if (!wait_bar(s, &s.v_full[st], (j / kStages) & 1, p.err)) break;
-      if (j == n_kv - 1 && last_valid < BN) {
+      if (j == n_max - 1 && last_valid < BN) {
         // Rows past the last valid key may hold anything (the cache is not cleared); P is 0
         // there, but 0 * NaN is NaN, so those V rows are zeroed before the P.V MMA.
         uint4* vrow = reinterpret_cast<uint4*>(s.v[st]);
@@ -207,126 +237,152 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
       }
-      if (!wait_bar(s, &s.p_full[bf], (j >> 1) & 1, p.err)) break;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t v_addr = smem_u32(s.v[st]);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t pa = smem_u32(s.p[bf][kk >> 2]) + (kk & 3) * 32;
-          mma_f16_ss(tmem + col_pv(bf), smem_desc_sw128(pa, 16, 1024),
-                     smem_desc_sw128(v_addr + kk * 2048, 0, 1024), idesc_pv, kk > 0);
+      for (int w = 0; w < 2 && ok; ++w) {
+        if (j >= (w ? n_kv1 : n_kv0)) continue;
+        if (!wait_bar(s, &s.p_full[w], j & 1, p.err)) {
+          ok = false;
+          break;
         }
-        mma_commit(&s.pv_full[bf]);
-        mma_commit(&s.kv_empty[st]);
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t v_addr = smem_u32(s.v[st]);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint32_t pa = smem_u32(s.p[w][kk >> 2]) + (kk & 3) * 32;
+            mma_f16_ss(tmem + col_o(w), smem_desc_sw128(pa, 16, 1024),
+                       smem_desc_sw128(v_addr + kk * 2048, 0, 1024), idesc_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&s.pv_done[w]);
+        }
+        __syncwarp();
       }
+      if (!ok) break;
+      if (lane == 0) mma_commit(&s.kv_empty[st]);
       __syncwarp();
     }
-  } else {
-    // ------------------------------------------------------------------ softmax warps 0-3
-    const int r = threadIdx.x;  // q row within the tile = TMEM lane
-    const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);
-    const int64_t qpos = int64_t(pos0) + q_row0 + r;
-    float m_run = -1e30f, l_run = 0.f, alpha_prev = 0.f;
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
+  } else if (warp < 8) {
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int w = warp >> 2;           // q tile of this warpgroup
+    const int r = threadIdx.x & 127;   // q row within the tile = TMEM lane
+    const uint32_t lane_addr = tmem + (uint32_t((warp & 3) * 32) << 16);
+    const int nk = w ? n_kv1 : n_kv0;
+    const int q_first = q_row0 + w * BM;  // first q row of this tile
+    // keys < key_lim are visible to this row
+    const int key_lim = p.causal ? pos0 + q_first + r + 1 : p.s_kv;
+    const float sl2 = p.scale_log2;
+    float m_raw = -INFINITY;  // reference max (raw score units) used for the exponent
+    float l_run = 0.f;
     bool ok = true;
-    auto fold_pv = [&](int j) -> bool {  // O = O * alpha_j + PV_j
-      const int bf = j & 1;
-      if (!wait_bar(s, &s.pv_full[bf], (j >> 1) & 1, p.err)) return false;
-      tc_fence_after();
-      uint32_t pv[2][32];
-      tmem_ld32(lane_addr + col_pv(bf), pv[0]);
-      tmem_ld32(lane_addr + col_pv(bf) + 32, pv[1]);
-      tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        o[i] = fmaf(o[i], alpha_prev, __uint_as_float(pv[0][i]));
-        o[32 + i] = fmaf(o[32 + i], alpha_prev, __uint_as_float(pv[1][i]));
-      }
-      return true;
-    };
-    for (int j = 0; j < n_kv; ++j) {
-      const int bf = j & 1;
-      if (!wait_bar(s, &s.s_full[bf], (j >> 1) & 1, p.err)) {
+    for (int j = 0; j < nk; ++j) {
+      if (!wait_bar(s, &s.s_full[w], j & 1, p.err)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t sv[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + col_s(bf) + c * 32, sv[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + col_s(w) + c * 32, sv[c]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.s_empty[bf]);
+      if (lane == 0) mbar_arrive(&s.s_free[w]);
 
-      const int64_t key0 = int64_t(j) * BN;
-      const bool need_mask = p.causal ? (key0 + BN - 1 > int64_t(pos0) + q_row0)
-                                      : (key0 + BN > int64_t(p.s_kv));
-      const int64_t key_lim = p.causal ? qpos + 1 : int64_t(p.s_kv);  // keys < key_lim
-      float mx = m_run;
+      const int key0 = j * BN;
+      const bool diag = p.causal ? (key0 + BN - 1 > pos0 + q_first) : (key0 + BN > p.s_kv);
+      if (diag) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (key0 + c * 32 + i >= key_lim) sv[c][i] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(sv[c][i]) * p.scale_log2;
-          if (need_mask && key0 + c * 32 + i >= key_lim) x = -INFINITY;
-          sv[c][i] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
-      const float alpha = fast_exp2(m_run - mx);
-      m_run = mx;
-      float psum = 0.f;
-      uint8_t* prow = reinterpret_cast<uint8_t*>(s.p[bf][0]) + r * 128;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(__uint_as_float(sv[c][2 * i]) - mx);
-          const float p1 = fast_exp2(__uint_as_float(sv[c][2 * i + 1]) - mx);
-          psum += p0 + p1;
-          packed[i] = pack_half2(p0, p1);
-        }
-        // keys c*32 .. c*32+31 -> chunk c/2, 16-byte pieces (c%2)*4 .. +3, swizzled by row
-        uint8_t* chunk = prow + (c >> 1) * (BM * 128);
-#pragma unroll
-        for (int pc = 0; pc < 4; ++pc) {
-          const int piece = (c & 1) * 4 + pc;
-          *reinterpret_cast<uint4*>(chunk + ((piece ^ (r & 7)) << 4)) =
-              make_uint4(packed[4 * pc], packed[4 * pc + 1], packed[4 * pc + 2],
-                         packed[4 * pc + 3]);
-        }
-      }
-      l_run = fmaf(l_run, alpha, psum);
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.p_full[bf]);
-      if (j > 0 && !fold_pv(j - 1)) {
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
+      // lazy rescale: keep the reference max unless this tile exceeds it by > 2^8
+      const bool grow = (mx - m_raw) * sl2 > kRescaleLog2;
+      const float alpha = grow ? fast_exp2((m_raw - mx) * sl2) : 1.0f;  // 0 on the first tile
+      if (grow) m_raw = mx;
+      const float neg = (m_raw == -INFINITY) ? 0.f : -m_raw * sl2;
+      // P buffer w is free (and O holds P(j-1).V) once P(j-1).V has completed
+      if (j > 0 && !wait_bar(s, &s.pv_done[w], (j - 1) & 1, p.err)) {
         ok = false;
         break;
       }
-      alpha_prev = alpha;
-    }
-    if (ok && fold_pv(n_kv - 1) && r < q_rows) {
-      const float inv = 1.0f / l_run;
-      __half* dst = p.out + (int64_t(b) * p.bs_q + q_row0 + r) * p.ld_o + int64_t(h) * D;
+      // P(j) = exp2(s * scale_log2 - m * scale_log2), rounded to f16, stored 8 keys at a time
+      float psum = 0.f;
+      uint8_t* prow = reinterpret_cast<uint8_t*>(s.p[w][0]) + r * 128;
 #pragma unroll
-      for (int i = 0; i < D; i += 8)
-        *reinterpret_cast<uint4*>(dst + i) =
-            make_uint4(pack_half2(o[i] * inv, o[i + 1] * inv),
-                       pack_half2(o[i + 2] * inv, o[i + 3] * inv),
-                       pack_half2(o[i + 4] * inv, o[i + 5] * inv),
-                       pack_half2(o[i + 6] * inv, o[i + 7] * inv));
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int pc = 0; pc < 4; ++pc) {
+          uint32_t q4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int e = pc * 8 + 2 * i;
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sv[c][e]), sl2, neg));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sv[c][e + 1]), sl2, neg));
+            psum += p0 + p1;
+            q4[i] = pack_half2(p0, p1);
+          }
+          // keys c*32 + pc*8 .. +7 -> chunk c/2, 16-byte piece (c%2)*4 + pc, swizzled by row
+          const int piece = (c & 1) * 4 + pc;
+          *reinterpret_cast<uint4*>(prow + (c >> 1) * (BM * 128) + ((piece ^ (r & 7)) << 4)) =
+              make_uint4(q4[0], q4[1], q4[2], q4[3]);
+        }
+      l_run = fmaf(l_run, alpha, psum);
+      // rescale O (it holds P(j-1).V) before P(j).V accumulates into it; warp-uniform because
+      // tcgen05.ld/st are warp-collective
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        tc_fence_after();
+        uint32_t ov[2][32];
+        tmem_ld32(lane_addr + col_o(w), ov[0]);
+        tmem_ld32(lane_addr + col_o(w) + 32, ov[1]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          ov[0][i] = __float_as_uint(__uint_as_float(ov[0][i]) * alpha);
+          ov[1][i] = __float_as_uint(__uint_as_float(ov[1][i]) * alpha);
+        }
+        tmem_st32(lane_addr + col_o(w), ov[0]);
+        tmem_st32(lane_addr + col_o(w) + 32, ov[1]);
+        tmem_st_wait();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.p_full[w]);
+    }
+    // epilogue: O / l -> f16 rows
+    if (ok && nk > 0 && wait_bar(s, &s.pv_done[w], (nk - 1) & 1, p.err)) {
+      tc_fence_after();
+      uint32_t ov[2][32];
+      tmem_ld32(lane_addr + col_o(w), ov[0]);
+      tmem_ld32(lane_addr + col_o(w) + 32, ov[1]);
+      tmem_ld_wait();
+      const int rows = w == 0 ? rows0 : rows1;
+      if (r < rows) {
+        const float inv = 1.0f / l_run;
+        __half* dst = p.out + (int64_t(b) * p.bs_q + q_first + r) * p.ld_o + int64_t(h) * D;
+#pragma unroll
+        for (int i = 0; i < D; i += 8) {
+          const int c = i >> 5, e = i & 31;
+          *reinterpret_cast<uint4*>(dst + i) = make_uint4(
+              pack_half2(__uint_as_float(ov[c][e]) * inv, __uint_as_float(ov[c][e + 1]) * inv),
+              pack_half2(__uint_as_float(ov[c][e + 2]) * inv, __uint_as_float(ov[c][e + 3]) * inv),
+              pack_half2(__uint_as_float(ov[c][e + 4]) * inv, __uint_as_float(ov[c][e + 5]) * inv),
+              pack_half2(__uint_as_float(ov[c][e + 6]) * inv, __uint_as_float(ov[c][e + 7]) * inv));
+        }
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -387,7 +443,7 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
   p.hq = a.hq;
   p.hkv = a.hkv;
   p.causal = a.causal;
-  p.n_qtiles = (a.s_q + BM - 1) / BM;
+  p.n_qpairs = (a.s_q + 2 * BM - 1) / (2 * BM);
   p.scale_log2 = a.scale_log2;
   const size_t smem = sizeof(Smem) + 1024;
   static std::once_flag once;
@@ -397,7 +453,7 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   });
   if (attr_err != cudaSuccess) return attr_err;
-  dim3 grid(p.n_qtiles, a.hq, a.batch);
+  dim3 grid(p.n_qpairs, a.hq, a.batch);
   void* args[] = {&tq, &tk, &tv, &p};
   return cudaLaunchKernel(reinterpret_cast<const void*>(&flash_fwd_kernel), grid,
                           dim3(kThreads), args, smem, stream);
