@@ -17,8 +17,9 @@
 //   warps 0-3   softmax warpgroup 0 (q tile 0), warps 4-7 warpgroup 1 (q tile 1): one thread
 //               per q row (= TMEM lane).  tcgen05.ld of the S row; mask only on tiles that
 //               cross the causal diagonal / the key end; exp2 with the scale folded into one
-//               FFMA; P rounded to f16 into shared memory in the 128B-swizzled K-major layout
-//               the MMA reads.  O stays in TMEM; it is rescaled (tcgen05.ld/st) only when a
+//               packed FFMA2 and evaluated two at a time by MUFU.EX2 on f16x2 (the result is
+//               already the f16 P pair; the row sum adds the same rounded values in f32); P
+//               goes to shared memory in the 128B-swizzled K-major layout the MMA reads.  O stays in TMEM; it is rescaled (tcgen05.ld/st) only when a
 //               row's max grows by more than 2^8 (lazy rescale: the final O / l is exact for
 //               any reference max), so most tiles skip it.
 //
@@ -297,11 +298,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (key0 + c * 32 + i >= key_lim) sv[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // row max with 8 independent chains (a single 128-long fmax chain is latency-bound)
+      float m8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
+        for (int i = 0; i < 32; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(sv[c][i]));
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       // lazy rescale: keep the reference max unless this tile exceeds it by > 2^8
       const bool grow = (mx - m_raw) * sl2 > kRescaleLog2;
       const float alpha = grow ? fast_exp2((m_raw - mx) * sl2) : 1.0f;  // 0 on the first tile
@@ -313,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       // P(j) = exp2(s * scale_log2 - m * scale_log2), rounded to f16, stored 8 keys at a time
-      float psum = 0.f;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};  // 4 independent partial sums
       uint8_t* prow = reinterpret_cast<uint8_t*>(s.p[w][0]) + r * 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
@@ -323,17 +329,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int e = pc * 8 + 2 * i;
-            const float p0 = fast_exp2(fmaf(__uint_as_float(sv[c][e]), sl2, neg));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(sv[c][e + 1]), sl2, neg));
-            psum += p0 + p1;
-            q4[i] = pack_half2(p0, p1);
+            float x0, x1;  // s * scale_log2 - m * scale_log2 for two keys (one FFMA2)
+            fma2(__uint_as_float(sv[c][e]), __uint_as_float(sv[c][e + 1]), sl2, neg, x0, x1);
+            q4[i] = ex2_f16x2(x0, x1);                 // both exps, already the f16 P pair
+            ps[i] = add_f16x2_to_f32(q4[i], ps[i]);    // row sum of the rounded P, in f32
           }
           // keys c*32 + pc*8 .. +7 -> chunk c/2, 16-byte piece (c%2)*4 + pc, swizzled by row
           const int piece = (c & 1) * 4 + pc;
           *reinterpret_cast<uint4*>(prow + (c >> 1) * (BM * 128) + ((piece ^ (r & 7)) << 4)) =
               make_uint4(q4[0], q4[1], q4[2], q4[3]);
         }
-      l_run = fmaf(l_run, alpha, psum);
+      l_run = fmaf(l_run, alpha, (ps[0] + ps[1]) + (ps[2] + ps[3]));
       // rescale O (it holds P(j-1).V) before P(j).V accumulates into it; warp-uniform because
       // tcgen05.ld/st are warp-collective
       if (j > 0 && __any_sync(0xffffffffu, grow)) {

@@ -176,6 +176,33 @@ __device__ __forceinline__ void regs_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// exp2 of two f32 arguments (a -> low half, b -> high half) as one packed f16x2:
+// the pair is rounded to f16 and one MUFU.EX2 f16x2 evaluates both.
+__device__ __forceinline__ uint32_t ex2_f16x2(float a, float b) {
+  uint32_t h, e;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
+  return e;
+}
+// acc + f32(low half) + f32(high half), without separate conversions (mixed-precision adds).
+__device__ __forceinline__ float add_f16x2_to_f32(uint32_t h2, float acc) {
+  const unsigned short lo = static_cast<unsigned short>(h2 & 0xffffu);
+  const unsigned short hi = static_cast<unsigned short>(h2 >> 16);
+  asm("add.rn.f32.f16 %0, %1, %0;" : "+f"(acc) : "h"(lo));
+  asm("add.rn.f32.f16 %0, %1, %0;" : "+f"(acc) : "h"(hi));
+  return acc;
+}
+// (a0, a1) * (b0, b1) + (c0, c1) as one packed fma.rn.f32x2.
+__device__ __forceinline__ void fma2(float a0, float a1, float b, float c, float& d0,
+                                     float& d1) {
+  uint64_t av, bv, cv, dv;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(av) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(bv) : "f"(b));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(cv) : "f"(c));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dv) : "l"(av), "l"(bv), "l"(cv));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(dv));
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
