@@ -11,7 +11,8 @@
 //               into a 3-stage ring shared by both q tiles; mbarrier complete_tx.  No multicast.
 //   warp 9      allocates 512 TMEM columns; one lane issues tcgen05.mma (cta_group::1, f16):
 //                 S_w(j)  = Q_w K_j^T -> TMEM S_w   (M128 N128 K64)
-//                 O_w    += P_w(j) V_j -> TMEM O_w  (M128 N64 K128, V as an MN-major operand)
+//                 O_w    += P_w(j) V_j -> TMEM O_w  (M128 N64 K128, A = P from TMEM, V an
+//                                                  MN-major shared-memory operand)
 //               S_w(j+1) is issued as soon as softmax warpgroup w has read S_w(j), so the
 //               tensor core computes it while the softmax of tile j runs.
 //   warps 0-3   softmax warpgroup 0 (q tile 0), warps 4-7 warpgroup 1 (q tile 1): one thread
@@ -19,7 +20,8 @@
 //               cross the causal diagonal / the key end; exp2 with the scale folded into one
 //               packed FFMA2 and evaluated two at a time by MUFU.EX2 on f16x2 (the result is
 //               already the f16 P pair; the row sum adds the same rounded values in f32); P
-//               goes to shared memory in the 128B-swizzled K-major layout the MMA reads.  O stays in TMEM; it is rescaled (tcgen05.ld/st) only when a
+//               is stored into TMEM (tcgen05.st) and the P.V MMA takes its A operand from
+//               there, so P never touches shared memory.  O stays in TMEM; it is rescaled (tcgen05.ld/st) only when a
 //               row's max grows by more than 2^8 (lazy rescale: the final O / l is exact for
 //               any reference max), so most tiles skip it.
 //
@@ -50,15 +52,16 @@ constexpr int kErrTimeout = 2;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (factor 256)
 
-// TMEM columns of q tile w: S at 256w (128 columns), O at 256w + 128 (64 columns).
+// TMEM columns of q tile w: S at 256w (128 f32 columns), P at 256w + 128 (128 keys as 64
+// packed f16x2 columns), O at 256w + 192 (64 f32 columns).
 __device__ __forceinline__ uint32_t col_s(int w) { return uint32_t(w) * 256u; }
-__device__ __forceinline__ uint32_t col_o(int w) { return uint32_t(w) * 256u + 128u; }
+__device__ __forceinline__ uint32_t col_p(int w) { return uint32_t(w) * 256u + 128u; }
+__device__ __forceinline__ uint32_t col_o(int w) { return uint32_t(w) * 256u + 192u; }
 
 struct __align__(1024) Smem {
   __half q[2][BM * D];
   __half k[kStages][BN * D];
   __half v[kStages][BN * D];
-  __half p[2][2][BM * 64];  // [q tile][key chunk of 64][128 rows x 64 keys], SW128 K-major
   uint64_t bar_q;
   uint64_t k_full[kStages], v_full[kStages], kv_empty[kStages];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
@@ -248,12 +251,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const uint32_t v_addr = smem_u32(s.v[st]);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint32_t pa = smem_u32(s.p[w][kk >> 2]) + (kk & 3) * 32;
-            mma_f16_ss(tmem + col_o(w), smem_desc_sw128(pa, 16, 1024),
+          for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P
+            mma_f16_ts(tmem + col_o(w), tmem + col_p(w) + kk * 8,
                        smem_desc_sw128(v_addr + kk * 2048, 0, 1024), idesc_pv,
                        (j > 0 || kk > 0) ? 1u : 0u);
-          }
           mma_commit(&s.pv_done[w]);
         }
         __syncwarp();
@@ -318,32 +319,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      // P(j) = exp2(s * scale_log2 - m * scale_log2), rounded to f16, stored 8 keys at a time
+      tc_fence_after();
+      // P(j) = exp2(s * scale_log2 - m * scale_log2) as packed f16 pairs into TMEM, 64 keys
+      // (32 columns) per store
       float ps[4] = {0.f, 0.f, 0.f, 0.f};  // 4 independent partial sums
-      uint8_t* prow = reinterpret_cast<uint8_t*>(s.p[w][0]) + r * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int pc = 0; pc < 4; ++pc) {
-          uint32_t q4[4];
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = half * 2 + cc;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int e = pc * 8 + 2 * i;
+          for (int i = 0; i < 16; ++i) {
             float x0, x1;  // s * scale_log2 - m * scale_log2 for two keys (one FFMA2)
-            fma2(__uint_as_float(sv[c][e]), __uint_as_float(sv[c][e + 1]), sl2, neg, x0, x1);
-            q4[i] = ex2_f16x2(x0, x1);                 // both exps, already the f16 P pair
-            ps[i] = add_f16x2_to_f32(q4[i], ps[i]);    // row sum of the rounded P, in f32
+            fma2(__uint_as_float(sv[c][2 * i]), __uint_as_float(sv[c][2 * i + 1]), sl2, neg, x0,
+                 x1);
+            pk[cc * 16 + i] = ex2_f16x2(x0, x1);              // both exps as the f16 P pair
+            ps[i & 3] = add_f16x2_to_f32(pk[cc * 16 + i], ps[i & 3]);  // f32 row sum
           }
-          // keys c*32 + pc*8 .. +7 -> chunk c/2, 16-byte piece (c%2)*4 + pc, swizzled by row
-          const int piece = (c & 1) * 4 + pc;
-          *reinterpret_cast<uint4*>(prow + (c >> 1) * (BM * 128) + ((piece ^ (r & 7)) << 4)) =
-              make_uint4(q4[0], q4[1], q4[2], q4[3]);
         }
+        tmem_st32(lane_addr + col_p(w) + half * 32, pk);
+      }
+      tmem_st_wait();
       l_run = fmaf(l_run, alpha, (ps[0] + ps[1]) + (ps[2] + ps[3]));
       // rescale O (it holds P(j-1).V) before P(j).V accumulates into it; warp-uniform because
       // tcgen05.ld/st are warp-collective
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        tc_fence_after();
         uint32_t ov[2][32];
         tmem_ld32(lane_addr + col_o(w), ov[0]);
         tmem_ld32(lane_addr + col_o(w) + 32, ov[1]);
@@ -357,7 +358,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st32(lane_addr + col_o(w) + 32, ov[1]);
         tmem_st_wait();
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.p_full[w]);
