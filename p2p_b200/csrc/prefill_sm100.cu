@@ -8,7 +8,7 @@
 //
 //   CTA = one (image, q head, pair of 128-row q tiles); 10 warps.
 //   warp 8      TMA producer: the two Q tiles once, then K/V tiles of 128 keys (SWIZZLE_128B)
-//               into a 3-stage ring shared by both q tiles; mbarrier complete_tx.  No multicast.
+//               into a 5-stage ring shared by both q tiles; mbarrier complete_tx.  No multicast.
 //   warp 9      allocates 512 TMEM columns; one lane issues tcgen05.mma (cta_group::1, f16):
 //                 S_w(j)  = Q_w K_j^T -> TMEM S_w   (M128 N128 K64)
 //                 O_w    += P_w(j) V_j -> TMEM O_w  (M128 N64 K128, A = P from TMEM, V an
@@ -44,7 +44,7 @@ using namespace sm100;
 constexpr int BM = 128;  // q rows per tile (two tiles per CTA)
 constexpr int BN = 128;  // keys per tile
 constexpr int D = kHeadDim;
-constexpr int kStages = 3;
+constexpr int kStages = 5;  // K/V ring depth: TMA latency (~2 us under load) spans >1 tile
 constexpr int kThreads = 320;  // 10 warps: 0-7 softmax (two warpgroups), 8 TMA, 9 MMA
 constexpr uint32_t kTileBytes = BM * D * 2;  // one Q, K or V tile: 16 KB
 constexpr uint32_t kTmemCols = 512;
@@ -420,7 +420,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t width, int64_t ld, int64
   cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
