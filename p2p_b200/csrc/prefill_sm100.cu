@@ -194,107 +194,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
-    // Event-driven: every pass polls the pending conditions and issues whichever MMA group is
-    // ready, so one warpgroup's late event never holds back the other's MMAs.
-    //   S_w(j)  needs K_j landed and warpgroup w done reading S_w(j-1)
-    //   PV_w(j) needs V_j landed and P_w(j) written (which also orders it after S_w(j))
-    //   K/V stage of tile j is released once both PV_0(j) and PV_1(j) are issued.
     constexpr uint32_t idesc_s = idesc_f16_f32(BM, BN, 0, 0);
     constexpr uint32_t idesc_pv = idesc_f16_f32(BM, D, 0, 1);
     bool ok = wait_bar(s, &s.bar_q, 0, p.err);
-    int s_next0 = 0, s_next1 = 0;    // next S tile per warpgroup
-    int pv_next0 = 0, pv_next1 = 0;  // next PV tile per warpgroup
-    int release = 0;                 // next K/V tile to hand back to the producer
-    bool zeroed = false;
-    uint64_t t_last = globaltimer_ns();
-    while (ok) {
-      const bool s_done = s_next0 >= n_kv0 && s_next1 >= n_kv1;
-      const bool pv_done_all = pv_next0 >= n_kv0 && pv_next1 >= n_kv1;
-      if (s_done && pv_done_all && release >= n_max) break;
-      int progressed = 0;
+    auto issue_s = [&](int w, int j) {  // S_w(j) = Q_w K_j^T
+      if (lane == 0) {
+        const uint32_t q_addr = smem_u32(s.q[w]);
+        const uint32_t k_addr = smem_u32(s.k[j % kStages]);
 #pragma unroll
-      for (int w = 0; w < 2; ++w) {
-        const int sn = w ? s_next1 : s_next0;
-        const int nk = w ? n_kv1 : n_kv0;
-        // ---- S_w(sn)
-        if (sn < nk) {
-          int ready = 0;
-          if (lane == 0)
-            ready = mbar_test_wait(&s.k_full[sn % kStages], (sn / kStages) & 1) &&
-                    (sn == 0 || mbar_test_wait(&s.s_free[w], (sn - 1) & 1));
-          ready = __shfl_sync(0xffffffffu, ready, 0);
-          if (ready) {
-            tc_fence_after();
-            if (lane == 0) {
-              const uint32_t q_addr = smem_u32(s.q[w]);
-              const uint32_t k_addr = smem_u32(s.k[sn % kStages]);
-#pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk)
-                mma_f16_ss(tmem + col_s(w), smem_desc_sw128(q_addr + kk * 32, 16, 1024),
-                           smem_desc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0);
-              mma_commit(&s.s_full[w]);
-            }
-            __syncwarp();
-            if (w) ++s_next1; else ++s_next0;
-            progressed = 1;
-          }
-        }
-        // ---- PV_w(pn)
-        const int pn = w ? pv_next1 : pv_next0;
-        if (pn < nk) {
-          const int st = pn % kStages;
-          int ready = 0;
-          if (lane == 0)
-            ready = mbar_test_wait(&s.v_full[st], (pn / kStages) & 1) &&
-                    mbar_test_wait(&s.p_full[w], pn & 1);
-          ready = __shfl_sync(0xffffffffu, ready, 0);
-          if (ready) {
-            if (pn == n_max - 1 && last_valid < BN && !zeroed) {
-              // Rows past the last valid key may hold anything (the cache is not cleared); P
-              // is 0 there, but 0 * NaN is NaN, so those V rows are zeroed before P.V.
-              uint4* vrow = reinterpret_cast<uint4*>(s.v[st]);
-              for (int i = last_valid * 8 + lane; i < BN * 8; i += 32)
-                vrow[i] = make_uint4(0, 0, 0, 0);
-              fence_proxy_async_smem();
-              __syncwarp();
-              zeroed = true;
-            }
-            tc_fence_after();
-            if (lane == 0) {
-              const uint32_t v_addr = smem_u32(s.v[st]);
-#pragma unroll
-              for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P
-                mma_f16_ts(tmem + col_o(w), tmem + col_p(w) + kk * 8,
-                           smem_desc_sw128(v_addr + kk * 2048, 0, 1024), idesc_pv,
-                           (pn > 0 || kk > 0) ? 1u : 0u);
-              mma_commit(&s.pv_done[w]);
-            }
-            __syncwarp();
-            if (w) ++pv_next1; else ++pv_next0;
-            progressed = 1;
-          }
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_f16_ss(tmem + col_s(w), smem_desc_sw128(q_addr + kk * 32, 16, 1024),
+                     smem_desc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0);
+        mma_commit(&s.s_full[w]);
       }
-      // ---- hand K/V stages back once every warpgroup that needs the tile has issued its PV
-      while (release < n_max && (release < pv_next0 || release >= n_kv0) &&
-             (release < pv_next1 || release >= n_kv1)) {
-        if (lane == 0) mma_commit(&s.kv_empty[release % kStages]);
+      __syncwarp();
+    };
+    if (ok) ok = wait_bar(s, &s.k_full[0], 0, p.err);
+    if (ok) {
+      tc_fence_after();
+      if (n_kv0 > 0) issue_s(0, 0);
+      if (n_kv1 > 0) issue_s(1, 0);
+    }
+    for (int j = 0; ok && j < n_max; ++j) {
+      const int st = j % kStages;
+      // next tile's scores, as soon as each warpgroup has read its S buffer
+      if (j + 1 < n_max) {
+        const int st1 = (j + 1) % kStages;
+        if (!wait_bar(s, &s.k_full[st1], ((j + 1) / kStages) & 1, p.err)) break;
+        for (int w = 0; w < 2 && ok; ++w) {
+          if (j + 1 >= (w ? n_kv1 : n_kv0)) continue;
+          if (!wait_bar(s, &s.s_free[w], j & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(w, j + 1);
+        }
+        if (!ok) break;
+      }
+      if (!wait_bar(s, &s.v_full[st], (j / kStages) & 1, p.err)) break;
+      if (j == n_max - 1 && last_valid < BN) {
+        // Rows past the last valid key may hold anything (the cache is not cleared); P is 0
+        // there, but 0 * NaN is NaN, so those V rows are zeroed before the P.V MMA.
+        uint4* vrow = reinterpret_cast<uint4*>(s.v[st]);
+        for (int i = last_valid * 8 + lane; i < BN * 8; i += 32) vrow[i] = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
         __syncwarp();
-        ++release;
-        progressed = 1;
       }
-      if (progressed) {
-        t_last = globaltimer_ns();
-      } else {
-        if (s.abort_flag) break;
-        if (globaltimer_ns() - t_last > kWaitLimitNs) {
-          if (lane == 0) {
-            s.abort_flag = 1;
-            atomicOr(p.err, kErrTimeout);
-          }
+      for (int w = 0; w < 2 && ok; ++w) {
+        if (j >= (w ? n_kv1 : n_kv0)) continue;
+        if (!wait_bar(s, &s.p_full[w], j & 1, p.err)) {
+          ok = false;
           break;
         }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t v_addr = smem_u32(s.v[st]);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P
+            mma_f16_ts(tmem + col_o(w), tmem + col_p(w) + kk * 8,
+                       smem_desc_sw128(v_addr + kk * 2048, 0, 1024), idesc_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&s.pv_done[w]);
+        }
+        __syncwarp();
       }
+      if (!ok) break;
+      if (lane == 0) mma_commit(&s.kv_empty[st]);
+      __syncwarp();
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------------ softmax warpgroups
