@@ -355,6 +355,49 @@ def run_prefill(ctx, steps, warmup):
     return ms_attn, ms_both
 
 
+def run_prefill_sharded(ctx, rank, world, s, steps, warmup):
+    """Causal prefill of an s-token prompt split by KV-head group over the ranks, with the NCCL
+    all-gather and the assembly of the [s][Hq*64] output inside the timed region."""
+    import torch
+    from p2p_b200.sharding import HeadShardedPrefill
+    sp = HeadShardedPrefill(ctx, HQ, HKV, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(33)
+    qkv_full = (0.5 * torch.randn((s, (HQ + 2 * HKV) * D), generator=g, device="cuda")).half()
+    qkv_l = qkv_full[:, sp.local_qkv_columns().cuda()].contiguous()
+    del qkv_full
+    rope = ctx.rope_table(s, D, 1e6)
+    kc = torch.zeros((s, sp.kvn, D), device="cuda", dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    q_buf = torch.zeros((s, sp.qn * D), device="cuda", dtype=torch.float16)
+    out_l = torch.zeros_like(q_buf)
+    gather = torch.zeros((world * s, sp.qn * D), device="cuda", dtype=torch.float16)
+    out = torch.zeros((s, HQ * D), device="cuda", dtype=torch.float16)
+
+    def step(i):
+        sp(qkv_l, None, rope, kc, vc, q_buf, out_l, gather, out, 0, s)
+
+    return timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
+
+
+def run_vision_split(ctx, rank, world, steps, warmup):
+    """The vision batch split by image over the ranks (no collective)."""
+    import torch
+    import p2p_b200
+    from p2p_b200.sharding import split_images
+    b0, nb = split_images(16, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(55 + rank)
+    q, k, v = ((0.5 * torch.randn((max(nb, 1), 1024, 768), generator=g, device="cuda")).half()
+               for _ in range(3))
+    out = torch.zeros_like(q)
+    prm = p2p_b200.Params(12, 12)
+
+    def step(i):
+        if nb:
+            ctx.attn_bidir(prm, q, k, v, out)
+
+    return timed_graph(step, steps, warmup, world)
+
+
 def run_vision(ctx, steps, warmup):
     import torch
     import p2p_b200
@@ -565,6 +608,18 @@ def main():
                     round(r_bytes / world / (r_ms * 1e-3) / 1e9 / hbm_peak, 4)}
         except p2p_b200.P2PError as e:
             side["ragged_decode"] = {"error": str(e)}
+        if world > 1:
+            for s_tok in (2048, 16384):
+                ms = max_over_ranks(run_prefill_sharded(ctx, rank, world, s_tok, 10, 3), world)
+                fl = prefill_flops(s_tok)
+                side[f"prefill_head_sharded_s{s_tok}"] = {
+                    "workload": f"causal prefill S={s_tok}, 32q/8kv split by kv-head group over "
+                                f"{world} GPUs + NCCL all-gather + [S][2048] assembly",
+                    "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
+            ms = max_over_ranks(run_vision_split(ctx, rank, world, 10, 3), world)
+            side["vision_image_split"] = {
+                "workload": f"vision B=16 S=1024 12 heads split by image over {world} GPUs",
+                "tflops": round(vision_flops() / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
         if world == 1:
             try:
                 pa, pb = run_prefill(ctx, steps=20, warmup=5)

@@ -57,3 +57,47 @@ def assemble_head_shards(gathered, s_tokens: int, q_heads_per_rank: int, head_di
     world = gathered.shape[0]
     x = gathered.reshape(world, s_tokens, q_heads_per_rank * head_dim)
     return x.permute(1, 0, 2).reshape(s_tokens, world * q_heads_per_rank * head_dim)
+
+
+class HeadShardedPrefill:
+    """Causal prefill over `world` GPUs split by KV-head group (one process per GPU).
+
+    Rank g owns kv heads [g*Hkv/G, (g+1)*Hkv/G) and their query heads: its QK_PREP writes only
+    its slice of the KV cache (dense [cap][Hkv/G][64] on this GPU, the layout a column-parallel
+    QKV projection produces) and its flash attention produces out[:, heads_g].  One NCCL
+    all-gather over NVLink exchanges the [M][Hq/G*64] slices and the reference's [M][Hq*64]
+    layout is assembled locally.  The only collective of the path.
+    """
+
+    def __init__(self, ctx, num_heads: int, num_kv_heads: int, world: int, rank: int,
+                 group=None):
+        from .attention import Params
+        self.ctx, self.world, self.rank, self.group = ctx, world, rank, group
+        self.kv0, self.kvn, self.q0, self.qn = head_groups(num_heads, num_kv_heads, world, rank)
+        self.prm = Params(self.qn, self.kvn)
+        self.num_heads = num_heads
+
+    def local_qkv_columns(self, head_dim: int = 64):
+        """Column indices of this rank's q, k and v heads inside a full qkv row."""
+        import torch
+        hq, d = self.num_heads, head_dim
+        hkv = self.kvn * self.world
+        cols = [torch.arange(self.q0 * d, (self.q0 + self.qn) * d),
+                torch.arange(hq * d + self.kv0 * d, hq * d + (self.kv0 + self.kvn) * d),
+                torch.arange((hq + hkv) * d + self.kv0 * d, (hq + hkv) * d + (self.kv0 + self.kvn) * d)]
+        return torch.cat(cols)
+
+    def __call__(self, qkv_local, norm_w, rope, k_cache, v_cache, q_buf, out_local, gather_buf,
+                 out_full, pos0: int, m_tokens: int, stream=None):
+        import torch.distributed as dist
+        self.ctx.qk_prep(self.prm, qkv_local, norm_w, rope, q_buf, k_cache, v_cache, pos0=pos0,
+                         m_tokens=m_tokens, stream=stream)
+        self.ctx.attn(self.prm, q_buf, k_cache, v_cache, out_local, pos0=pos0, m_tokens=m_tokens,
+                      stream=stream)
+        if self.world > 1:
+            dist.all_gather_into_tensor(gather_buf, out_local, group=self.group)
+            out_full.copy_(assemble_head_shards(
+                gather_buf.view(self.world, m_tokens, self.qn * 64), m_tokens, self.qn))
+        else:
+            out_full.copy_(out_local)
+        return out_full
