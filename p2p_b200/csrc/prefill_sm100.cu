@@ -8,7 +8,7 @@
 //
 //   CTA = one (image, q head, pair of 128-row q tiles); 10 warps.
 //   warp 8      TMA producer: the two Q tiles once, then K/V tiles of 128 keys (SWIZZLE_128B)
-//               into a 5-stage ring shared by both q tiles; mbarrier complete_tx.  No multicast.
+//               into a 5-stage ring shared by both q tiles; mbarrier complete_tx; single-CTA loads.
 //   warp 9      allocates 512 TMEM columns; one lane issues tcgen05.mma (cta_group::1, f16):
 //                 S_w(j)  = Q_w K_j^T -> TMEM S_w   (M128 N128 K64)
 //                 O_w    += P_w(j) V_j -> TMEM O_w  (M128 N64 K128, A = P from TMEM, V an

@@ -1,5 +1,5 @@
 // sm100.cuh -- hand-written PTX wrappers for the Blackwell (sm_100a) features the flash kernel
-// uses: mbarriers, TMA tile loads (no multicast), tcgen05 TMEM allocation, MMA, commit, loads,
+// uses: mbarriers, single-CTA TMA tile loads, tcgen05 TMEM allocation, MMA, commit, loads,
 // and the shared-memory matrix / instruction descriptors of tcgen05.mma.kind::f16.
 #pragma once
 
@@ -47,7 +47,7 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// ---- TMA (tile mode, one CTA, no multicast) -------------------------------------------------
+// ---- TMA (tile mode, each load lands in the issuing CTA only) -----------------------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x,
                                             int32_t y, uint64_t* bar) {
   asm volatile(
