@@ -188,6 +188,13 @@ p2p_status p2p_attn_decode_ragged_noalloc(p2p_ctx* ctx, const p2p_attn_params* p
  * without exhausting a shared GPU. */
 p2p_status p2p_debug_set_alloc_limit(int64_t bytes);
 
+/* Test hook, no counterpart in the reference: kernels launched afterwards that wait on other
+ * CTAs or on copies (the flash prefill's Q tile, the decode step's cluster combine) expect
+ * `bytes` more on that wait than will ever arrive, so the wait runs out after its 1 s limit,
+ * the kernel writes no output for that work and the next p2p_sync returns P2P_ERR_TIMEOUT.
+ * 0 restores normal operation.  Exercises the bounded-wait path without any fault. */
+p2p_status p2p_debug_set_wait_deficit(int32_t bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -97,6 +97,7 @@ PROTOTYPES = {
     "p2p_attn_decode_ragged_noalloc": (
         _st, [_v, _pp, _v, _i64, _v, _v, _v, _v, _v, _v, _i32, _i32, _i32, _v, _i64, _v]),
     "p2p_debug_set_alloc_limit": (_st, [_i64]),
+    "p2p_debug_set_wait_deficit": (_st, [_i32]),
 }
 
 

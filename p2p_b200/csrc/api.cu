@@ -8,6 +8,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -54,6 +56,9 @@ namespace {
 int64_t g_alloc_limit = -1;
 int64_t g_alloc_used = 0;
 std::mutex g_alloc_mu;
+
+// Test hook: extra bytes every bounded device-side wait expects (0 = normal operation).
+std::atomic<int32_t> g_wait_deficit{0};
 
 struct DeviceGuard {
   int prev = -1;
@@ -188,28 +193,51 @@ int forced_splits() {
   return v;
 }
 
+// Tuning knob: P2P_DECODE_CLUSTER=0 makes decode steps use the workspace combine instead of
+// the thread-block-cluster combine.
+bool cluster_combine_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("P2P_DECODE_CLUSTER");
+    return !(e && std::atoi(e) == 0);
+  }();
+  return v;
+}
+
 p2p_status run_decode(p2p_ctx* ctx, const p2p_attn_params* prm, p2p::DecodeArgs& a, int mode,
                       bool fused, int nz, int64_t max_len, cudaStream_t s) {
   const int hkv = prm->num_kv_heads;
   const int group = prm->num_heads / hkv;
-  int min_split = 16;
-  int splits = p2p::decode_max_splits(max_len, hkv, nz, ctx->num_sms, &min_split);
-  if (forced_splits() > 0) {
-    splits = forced_splits();
-    min_split = 16;
-  }
-  p2p_status st = ensure_workspace(ctx, p2p::decode_partials_bytes(splits, hkv, nz, group),
-                                   p2p::decode_counters_bytes(hkv, nz), s);
-  if (st != P2P_OK) return st;
   a.hq = prm->num_heads;
   a.hkv = hkv;
   a.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
   a.eps = eff_eps(prm);
-  a.min_split = min_split;
-  a.partials = ctx->partials;
-  a.counters = ctx->counters;
   a.err = ctx->dev_err;
-  cudaError_t e = p2p::launch_decode(a, mode, fused, prm->dtype, splits, nz, s);
+  a.wait_deficit = g_wait_deficit.load();
+  int min_split = 16;
+  int cluster = 0;
+  int splits = 0;
+  if (mode == p2p::kLayers && prm->dtype == P2P_F16 && cluster_combine_enabled()) {
+    // Decode step over layers: the splits of one (layer, head chunk) form a cluster.
+    cluster = forced_splits() > 0
+                  ? std::min(forced_splits(), 8)
+                  : p2p::decode_cluster_splits(max_len, hkv, group, nz, fused, ctx->num_sms);
+    if (cluster > 1) splits = cluster;
+    else cluster = 0;
+  }
+  if (cluster == 0) {
+    splits = p2p::decode_max_splits(max_len, hkv, nz, ctx->num_sms, &min_split);
+    if (forced_splits() > 0) {
+      splits = forced_splits();
+      min_split = 16;
+    }
+    p2p_status st = ensure_workspace(ctx, p2p::decode_partials_bytes(splits, hkv, nz, group),
+                                     p2p::decode_counters_bytes(hkv, nz), s);
+    if (st != P2P_OK) return st;
+    a.partials = ctx->partials;
+    a.counters = ctx->counters;
+  }
+  a.min_split = min_split;
+  cudaError_t e = p2p::launch_decode(a, mode, fused, prm->dtype, splits, nz, s, cluster);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "decode launch");
   return P2P_OK;
 }
@@ -308,7 +336,17 @@ p2p_status p2p_sync(p2p_ctx* ctx, void* stream) {
       return fail(ctx, P2P_ERR_KV_FULL,
                   "a kernel was given a device-side position beyond its KV cache; that work "
                   "was skipped");
+    if (flags & p2p::kErrTimeout)
+      return fail(ctx, P2P_ERR_TIMEOUT,
+                  "a kernel's bounded wait on another CTA ran out; its output was not written");
   }
+  return P2P_OK;
+}
+
+// Test hook (not part of the reference contract): make bounded device waits run out.
+p2p_status p2p_debug_set_wait_deficit(int32_t bytes) {
+  if (bytes < 0 || bytes > (1 << 19)) return P2P_ERR_INVALID_ARG;
+  g_wait_deficit.store(bytes);
   return P2P_OK;
 }
 
@@ -568,6 +606,7 @@ p2p_status p2p_attn(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q, int
   f.pos0_host = pos0;
   f.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
   f.err = ctx->dev_err;
+  f.wait_deficit = g_wait_deficit.load();
   cudaError_t e = p2p::launch_flash(f, s);
   if (e == cudaErrorNotSupported) return fail(ctx, P2P_ERR_UNSUPPORTED, "prefill kernel");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill launch");
@@ -670,6 +709,7 @@ p2p_status p2p_attn_bidir(p2p_ctx* ctx, const p2p_attn_params* prm, const void* 
   f.pos0_host = 0;
   f.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
   f.err = ctx->dev_err;
+  f.wait_deficit = g_wait_deficit.load();
   cudaError_t e = p2p::launch_flash(f, pick_stream(ctx, stream));
   if (e == cudaErrorNotSupported) return fail(ctx, P2P_ERR_UNSUPPORTED, "bidir kernel");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "bidir launch");

@@ -30,6 +30,13 @@
 // of the (sequence, head chunk) to arrive -- counted with one atomic -- runs the second pass
 // that combines the partials and writes the output, then resets its counter.  Nothing ever
 // waits on another CTA.
+//
+// Cluster form (f16, one decode step over the layers): the splits of one (layer, head chunk)
+// are the CTAs of one thread-block cluster (up to 8).  Head g's combine is owned by cluster
+// rank g % nsplit; every split pushes its partial for head g straight into the owner's shared
+// memory with st.async, which completes bytes on the owner's mbarrier.  The owner waits on
+// that mbarrier (bounded), combines and writes the output; every other CTA exits as soon as it
+// has pushed.  No workspace, no atomics, no global fences and no cluster barrier at the end.
 #include <mutex>
 #include <set>
 
@@ -200,6 +207,154 @@ __device__ __forceinline__ void finish(const DecodeArgs& a, T* out_h, int pair, 
   if (tid == 0) a.counters[pair] = 0;
 }
 
+// ---- cluster push-combine ---------------------------------------------------------------------
+constexpr int kMaxCluster = 8;
+constexpr int kPushStride = kHeadDim + 4;  // acc[64], max, sum, 2 pad: 17 16-byte chunks
+constexpr int kPushChunks = kPushStride / 4;
+constexpr int kRecvSlots = 8;  // ceil(GC / n) * n <= 8 for GC <= 4, n <= 8
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// Address of the same shared-memory variable in cluster CTA `rank` (shared::cluster window).
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+// 16 bytes into a cluster peer's shared memory; completes 16 bytes of transaction count on the
+// peer's mbarrier when they have landed.
+__device__ __forceinline__ void st_async16(uint32_t dst, const uint4& v, uint32_t bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, "
+      "[%5];" ::"r"(dst),
+      "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void recv_bar_init(uint64_t* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void recv_bar_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool recv_bar_try_wait(uint64_t* bar) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar))
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Cluster form of finish().  Split `split` (= cluster rank) of `nsplit` active splits merges
+// its warps into stage_s, pushes head g's partial to slot (g / nsplit) * nsplit + split of
+// rank g % nsplit, and, if it owns heads, waits for all nsplit partials of each and writes
+// them combined.  Splits >= nsplit (empty key ranges) push nothing and own nothing.  Every
+// CTA must have called cluster_arrive_relaxed() after recv_bar_init().
+template <class T, int GC>
+__device__ __forceinline__ void finish_push(const DecodeArgs& a, T* out_h, int split, int nsplit,
+                                            const float (*red_m)[GC], const float (*red_l)[GC],
+                                            const float (*red_acc)[GC][kHeadDim],
+                                            float (*stage_s)[kPushStride],
+                                            float (*recv_s)[kPushStride], uint64_t* recv_bar) {
+  constexpr int D = kHeadDim;
+  const int tid = threadIdx.x;
+  const bool active = split < nsplit;
+  if (active) {
+    for (int idx = tid; idx < GC * D; idx += kThreads) {
+      const int g = idx / D, d = idx % D;
+      float mx = red_m[0][g];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, red_m[w][g]);
+      float l = 0.f, ac = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float c = fast_exp2(red_m[w][g] - mx);
+        l = fmaf(red_l[w][g], c, l);
+        ac = fmaf(red_acc[w][g][d], c, ac);
+      }
+      stage_s[g][d] = ac;
+      if (d == 0) {
+        stage_s[g][D] = mx;
+        stage_s[g][D + 1] = l;
+        stage_s[g][D + 2] = 0.f;
+        stage_s[g][D + 3] = 0.f;
+      }
+    }
+    __syncthreads();
+  }
+  cluster_wait();  // every rank's receive mbarrier is initialised
+  if (!active) return;
+  for (int i = tid; i < GC * kPushChunks; i += kThreads) {
+    const int g = i / kPushChunks, c = i % kPushChunks;
+    const uint32_t owner = uint32_t(g % nsplit);
+    const int slot = (g / nsplit) * nsplit + split;
+    const uint4 v = *reinterpret_cast<const uint4*>(&stage_s[g][4 * c]);
+    st_async16(map_rank(smem_addr(&recv_s[slot][4 * c]), owner), v,
+               map_rank(smem_addr(recv_bar), owner));
+  }
+  // heads owned by this rank: g = split, split + nsplit, ...
+  const int owned = split < GC ? (GC - 1 - split) / nsplit + 1 : 0;
+  if (owned == 0) return;
+  if (tid == 0)
+    recv_bar_expect(recv_bar, uint32_t(owned * nsplit * kPushStride * 4 + a.wait_deficit));
+  if (!recv_bar_try_wait(recv_bar)) {
+    const uint64_t t0 = now_ns();
+    while (!recv_bar_try_wait(recv_bar)) {
+      if (now_ns() - t0 > kWaitLimitNs) {  // a peer never delivered: report, write nothing
+        if (tid == 0) atomicOr(a.err, kErrTimeout);
+        return;
+      }
+    }
+  }
+  for (int idx = tid; idx < owned * D; idx += kThreads) {
+    const int h = idx / D, d = idx % D;
+    const float(*src)[kPushStride] = recv_s + h * nsplit;
+    float m[kMaxCluster], l[kMaxCluster], ac[kMaxCluster];
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r) {
+      if (r < nsplit) {
+        m[r] = src[r][D];
+        l[r] = src[r][D + 1];
+        ac[r] = src[r][d];
+      }
+    }
+    float mx = kNegBig;
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r)
+      if (r < nsplit) mx = fmaxf(mx, m[r]);
+    float lt = 0.f, at = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r) {
+      if (r < nsplit) {
+        const float c = fast_exp2(m[r] - mx);
+        lt = fmaf(l[r], c, lt);
+        at = fmaf(ac[r], c, at);
+      }
+    }
+    out_h[(split + h * nsplit) * D + d] = from_f32<T>(at / lt);  // kernels.js:317
+  }
+}
+
 // ---- warp-level MMA helpers -------------------------------------------------------------------
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -235,7 +390,7 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return uint32_t(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-template <int G, bool FUSED, int MODE>
+template <int G, bool FUSED, int MODE, bool CL>
 __global__ void __launch_bounds__(kThreads, 3)
     decode_mma_kernel(const __grid_constant__ DecodeArgs a) {
   using T = __half;
@@ -260,13 +415,21 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int len = sq.past + 1;  // keys 0..past, key `past` is the new token
   const int split_len = max(a.min_split, (ceil_div(len, ngrid) + 15) & ~15);
   const int nsplit = ceil_div(len, split_len);
-  if (split >= nsplit) return;
-  const int j0 = split * split_len;
+  // A cluster CTA past the last split still takes part in the cluster barriers (empty range).
+  if (!CL && split >= nsplit) return;
+  const int j0 = min(split * split_len, len);
   const int j1 = min(j0 + split_len, len);
-  const bool has_new = FUSED && (j1 == len);
+  const bool has_new = FUSED && j0 < j1 && j1 == len;
   const int jcopy = has_new ? sq.past : j1;  // rows streamed from the cache
   const int64_t kv_stride = int64_t(a.hkv) * D;
 
+  __shared__ __align__(16) float stage_s[CL ? GC : 1][kPushStride];
+  __shared__ __align__(16) float recv_s[CL ? kRecvSlots : 1][kPushStride];
+  __shared__ __align__(8) uint64_t recv_bar;
+  if constexpr (CL) {
+    if (tid == 0) recv_bar_init(&recv_bar);
+    cluster_arrive_relaxed();  // matched by cluster_wait() in finish_push
+  }
   __shared__ float q_s[GC][D];
   __shared__ float knew_s[D];
   __shared__ float vnew_s[D];
@@ -418,8 +581,13 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
   }
   __syncthreads();
-  finish<T, GC>(a, sq.orow + int64_t(head0) * D, z * gridDim.y + blockIdx.y, split, nsplit,
-                ngrid, red_m, red_l, red_acc, &s_last);
+  if constexpr (CL) {
+    finish_push<T, GC>(a, sq.orow + int64_t(head0) * D, split, nsplit, red_m, red_l, red_acc,
+                       stage_s, recv_s, &recv_bar);
+  } else {
+    finish<T, GC>(a, sq.orow + int64_t(head0) * D, z * gridDim.y + blockIdx.y, split, nsplit,
+                  ngrid, red_m, red_l, red_acc, &s_last);
+  }
 }
 
 // ---- CUDA-core kernel (fp32 storage) ----------------------------------------------------------
@@ -644,9 +812,9 @@ struct KernelInfo {
   int smem;
 };
 
-template <int G, bool FUSED, int MODE>
+template <int G, bool FUSED, int MODE, bool CL>
 KernelInfo info_h() {
-  return {reinterpret_cast<const void*>(&decode_mma_kernel<G, FUSED, MODE>),
+  return {reinterpret_cast<const void*>(&decode_mma_kernel<G, FUSED, MODE, CL>),
           Ring<__half>::kBytes};
 }
 template <int G, bool FUSED, int MODE>
@@ -656,23 +824,46 @@ KernelInfo info_f() {
 }
 
 template <int G>
-KernelInfo pick_fm(bool half, bool fused, int mode) {
+KernelInfo pick_fm(bool half, bool fused, int mode, bool cl) {
   if (half) {
-    if (mode == kLayers) return fused ? info_h<G, true, kLayers>() : info_h<G, false, kLayers>();
-    return fused ? info_h<G, true, kRagged>() : info_h<G, false, kRagged>();
+    if (cl) {  // cluster combine: decode steps over layers only
+      if (mode != kLayers) return {nullptr, 0};
+      return fused ? info_h<G, true, kLayers, true>() : info_h<G, false, kLayers, true>();
+    }
+    if (mode == kLayers)
+      return fused ? info_h<G, true, kLayers, false>() : info_h<G, false, kLayers, false>();
+    return fused ? info_h<G, true, kRagged, false>() : info_h<G, false, kRagged, false>();
   }
+  if (cl) return {nullptr, 0};
   if (mode == kLayers) return fused ? info_f<G, true, kLayers>() : info_f<G, false, kLayers>();
   return fused ? info_f<G, true, kRagged>() : info_f<G, false, kRagged>();
 }
 
-KernelInfo pick(int group, bool half, bool fused, int mode) {
+KernelInfo pick(int group, bool half, bool fused, int mode, bool cl) {
   switch (group) {
-    case 1: return pick_fm<1>(half, fused, mode);
-    case 2: return pick_fm<2>(half, fused, mode);
-    case 4: return pick_fm<4>(half, fused, mode);
-    case 8: return pick_fm<8>(half, fused, mode);
+    case 1: return pick_fm<1>(half, fused, mode, cl);
+    case 2: return pick_fm<2>(half, fused, mode, cl);
+    case 4: return pick_fm<4>(half, fused, mode, cl);
+    case 8: return pick_fm<8>(half, fused, mode, cl);
     default: return {nullptr, 0};
   }
+}
+
+// One-time attribute setup per kernel (dynamic shared memory; cluster kernels may use
+// clusters above the portable 8 CTAs).
+cudaError_t configure(const KernelInfo& k, bool cl) {
+  static std::mutex mu;
+  static std::set<const void*> configured;
+  std::lock_guard<std::mutex> lk(mu);
+  if (configured.count(k.fn)) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+  if (e != cudaSuccess) return e;
+  if (cl) {
+    e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  configured.insert(k.fn);
+  return cudaSuccess;
 }
 
 int head_chunks(int group) { return group > 4 ? group / 4 : 1; }
@@ -706,25 +897,67 @@ int decode_max_splits(int64_t max_len, int hkv, int nz, int num_sms, int* min_sp
   return int(g < 1 ? 1 : g);
 }
 
-cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, int max_splits,
-                          int nz, cudaStream_t s) {
-  const int group = a.hq / a.hkv;
-  const KernelInfo k = pick(group, dtype == 0, fused, mode);
-  if (!k.fn) return cudaErrorInvalidValue;
-  static std::mutex mu;
-  static std::set<const void*> configured;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!configured.count(k.fn)) {
-      cudaError_t e =
-          cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
-      if (e != cudaSuccess) return e;
-      configured.insert(k.fn);
+int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fused,
+                          int num_sms) {
+  // One wave: the (layer, head chunk) rows times the cluster size fill the 3 CTA slots of every
+  // SM at most; at most 16 CTAs per cluster and one 16-key pass per CTA at least.  The size is
+  // then lowered until the device reports that all clusters are resident at once.
+  const int rows = hkv * head_chunks(group) * nz;
+  const int64_t slots = int64_t(num_sms) * 3;
+  int64_t c = slots / rows;
+  const int64_t by_len = (max_len + 15) / 16;
+  if (c > by_len) c = by_len;
+  if (c > kMaxCluster) c = kMaxCluster;
+  if (c < 2) return 1;
+  const KernelInfo k = pick(group, true, fused, kLayers, true);
+  if (!k.fn || configure(k, true) != cudaSuccess) return 1;
+  for (; c >= 2; --c) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(c), unsigned(hkv * head_chunks(group)), unsigned(nz));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = size_t(k.smem);
+    cudaLaunchAttribute at{};
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = unsigned(c);
+    at.val.clusterDim.y = 1;
+    at.val.clusterDim.z = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k.fn, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      continue;
     }
+    if (n >= rows) return int(c);
   }
+  return 1;
+}
+
+cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, int max_splits,
+                          int nz, cudaStream_t s, int cluster) {
+  const int group = a.hq / a.hkv;
+  const bool cl = cluster > 1;
+  if (cl && (cluster > kMaxCluster || cluster != max_splits)) return cudaErrorInvalidValue;
+  const KernelInfo k = pick(group, dtype == 0, fused, mode, cl);
+  if (!k.fn) return cudaErrorInvalidValue;
+  cudaError_t e = configure(k, cl);
+  if (e != cudaSuccess) return e;
   dim3 grid(max_splits, a.hkv * head_chunks(group), nz);
   void* args[] = {const_cast<DecodeArgs*>(&a)};
-  return cudaLaunchKernel(k.fn, grid, dim3(kThreads), args, size_t(k.smem), s);
+  if (!cl) return cudaLaunchKernel(k.fn, grid, dim3(kThreads), args, size_t(k.smem), s);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = size_t(k.smem);
+  cfg.stream = s;
+  cudaLaunchAttribute at{};
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = unsigned(cluster);
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, k.fn, args);
 }
 
 }  // namespace p2p

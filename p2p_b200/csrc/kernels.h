@@ -64,6 +64,7 @@ struct DecodeArgs {
   int32_t min_split;  // keys per split lower bound (multiple of 64)
   float* partials;    // [nz][hkv][max_splits][G][66]
   int32_t* counters;  // [nz][hkv], zero between launches
+  int32_t wait_deficit;  // test hook: extra bytes the cluster combine waits for (0 normally)
 };
 
 enum DecodeMode { kLayers = 0, kRagged = 1 };
@@ -71,8 +72,13 @@ enum DecodeMode { kLayers = 0, kRagged = 1 };
 // grid = (max_splits, hkv, nz).  Workspace sizes in bytes for that grid.
 size_t decode_partials_bytes(int max_splits, int hkv, int nz, int group);
 size_t decode_counters_bytes(int hkv, int nz);
+// cluster > 1: f16 kLayers only, max_splits == cluster (<= 8); the splits of one (layer,
+// head chunk) form one thread-block cluster and combine through distributed shared memory,
+// so partials/counters are not used.
 cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, int max_splits,
-                          int nz, cudaStream_t s);
+                          int nz, cudaStream_t s, int cluster = 0);
+// Cluster size for a decode step over nz layers (1 = use the workspace combine).
+int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fused, int num_sms);
 // Choose the split count for a sequence of up to max_len keys.
 int decode_max_splits(int64_t max_len, int hkv, int nz, int num_sms, int* min_split);
 
@@ -94,10 +100,12 @@ struct FlashArgs {
   int32_t pos0_host;
   float scale_log2;
   int32_t* err;          // device error word: bit 0 = position beyond the cache
+  int32_t wait_deficit;  // test hook: extra bytes the Q-tile wait expects (0 normally)
 };
 
 // Device error word bits.
 constexpr int kErrPosBeyondCache = 1;
+constexpr int kErrTimeout = 2;  // a bounded device-side wait ran out; that work was not written
 cudaError_t launch_flash(const FlashArgs& a, cudaStream_t s);
 
 }  // namespace p2p

@@ -48,7 +48,6 @@ constexpr int kStages = 5;  // K/V ring depth: TMA latency (~2 us under load) sp
 constexpr int kThreads = 320;  // 10 warps: 0-7 softmax (two warpgroups), 8 TMA, 9 MMA
 constexpr uint32_t kTileBytes = BM * D * 2;  // one Q, K or V tile: 16 KB
 constexpr uint32_t kTmemCols = 512;
-constexpr int kErrTimeout = 2;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (factor 256)
 
@@ -82,6 +81,7 @@ struct FlashParams {
   int32_t causal;
   int32_t n_qpairs;
   float scale_log2;
+  int32_t wait_deficit;  // test hook (0 normally): the Q-tile wait then runs out
 };
 
 // Bounded wait on an mbarrier phase; false when the limit passed or another role gave up.
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm_k);
       prefetch_tensormap(&tm_v);
       const int nq = rows1 > 0 ? 2 : 1;
-      mbar_arrive_expect_tx(&s.bar_q, kTileBytes * nq);
+      mbar_arrive_expect_tx(&s.bar_q, kTileBytes * nq + uint32_t(p.wait_deficit));
       for (int w = 0; w < nq; ++w)
         tma_load_2d(s.q[w], &tm_q, h * D, int32_t(int64_t(b) * p.bs_q + q_row0 + w * BM),
                     &s.bar_q);
@@ -453,6 +453,7 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
   p.causal = a.causal;
   p.n_qpairs = (a.s_q + 2 * BM - 1) / (2 * BM);
   p.scale_log2 = a.scale_log2;
+  p.wait_deficit = a.wait_deficit;
   const size_t smem = sizeof(Smem) + 1024;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;

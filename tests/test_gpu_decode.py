@@ -179,6 +179,32 @@ def test_decode_step_six_layers_ctx4096(ctx, oracle):
         assert_close(host(layers[l][4])[None], out_o, what=f"layer {l}")
 
 
+@pytest.mark.parametrize("hq,past", [(32, 0), (32, 5), (32, 100), (32, 3000), (64, 37)])
+def test_decode_step_device_position_in_large_cache(ctx, oracle, hq, past):
+    """Device-side position well inside a 4097-row cache: the split count follows the cache
+    size, so most splits of a (layer, head) get an empty key range and must contribute
+    nothing to the combine."""
+    import p2p_b200
+    hkv, cap, n_layers = 8, 4097, 2
+    rope = oracle.rope_table(cap)
+    prm = p2p_b200.Params(hq, hkv)
+    layers, want = [], []
+    for l in range(n_layers):
+        rng = np.random.default_rng(7000 + 10 * past + l)
+        qkv, nw, kc, vc = make_layer(rng, hq, hkv, past, cap)
+        _, kc_o, vc_o, out_o = oracle_decode(oracle, hq, hkv, qkv, nw, rope, kc, vc, past)
+        out = torch.zeros((hq * D,), dtype=torch.float16, device="cuda")
+        layers.append((dev(qkv[0]), dev(nw), dev(kc), dev(vc), out))
+        want.append((kc_o, vc_o, out_o))
+    ctx.meta_write(past, 1)
+    ctx.decode_step(prm, layers, dev(rope), cap, use_meta=True)
+    for l in range(n_layers):
+        kc_o, vc_o, out_o = want[l]
+        assert np.array_equal(bits(host(layers[l][2])), bits(kc_o))
+        assert np.array_equal(bits(host(layers[l][3])), bits(vc_o))
+        assert_close(host(layers[l][4])[None], out_o, what=f"layer {l} past {past}")
+
+
 def test_decode_fp32_storage(ctx, oracle):
     """The fp32 case: past 512 + 1 new, RoPE theta 1e6 on positions 0..512, no q/k norm."""
     import p2p_b200
