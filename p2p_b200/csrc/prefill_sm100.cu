@@ -114,8 +114,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qp = p.causal ? (p.n_qpairs - 1 - int(blockIdx.x)) : int(blockIdx.x);
-  const int h = blockIdx.y, b = blockIdx.z;
+  // Grid (heads, q pairs, images), launched in linear order: every head's q pair before the
+  // next q pair, and causal q pairs longest first (the last pair sees the most keys), so the
+  // block scheduler hands out the work longest-processing-time first.
+  const int qp = p.causal ? (p.n_qpairs - 1 - int(blockIdx.y)) : int(blockIdx.y);
+  const int h = blockIdx.x, b = blockIdx.z;
   const int kh = h / (p.hq / p.hkv);
   const int pos0 = p.causal ? (p.meta ? int(p.meta[0]) : p.pos0_host) : 0;
   const int q_row0 = qp * 2 * BM;
@@ -462,7 +465,8 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   });
   if (attr_err != cudaSuccess) return attr_err;
-  dim3 grid(p.n_qpairs, a.hq, a.batch);
+  if (p.n_qpairs > 65535) return cudaErrorInvalidValue;
+  dim3 grid(a.hq, p.n_qpairs, a.batch);
   void* args[] = {&tq, &tk, &tv, &p};
   return cudaLaunchKernel(reinterpret_cast<const void*>(&flash_fwd_kernel), grid,
                           dim3(kThreads), args, smem, stream);
