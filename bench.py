@@ -672,7 +672,7 @@ def main():
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(per_gpu_gbs / hbm_peak, 4), "peak_kind": peak_kind,
                          "frac_of_nominal_8tbs": round(per_gpu_gbs / 8000.0, 4),
-                         "traffic": tr, "kernel": "decode_kernel<__half,4,fused,layers>"},
+                         "traffic": tr, "kernel": "decode_mma_kernel<G=4,fused,layers,cluster>"},
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_sec * 1e6, 2)},
             "gpu_launches": args.steps,
