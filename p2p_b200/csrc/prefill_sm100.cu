@@ -6,7 +6,10 @@
 // q.k * scale, online softmax (running max / sum), P.V accumulated in f32, out = acc / sum in
 // f16 -- reorganised into 128 x 128 tiles on tcgen05 / TMEM / TMA:
 //
-//   CTA = one (image, q head, pair of 128-row q tiles); 10 warps.
+//   CTA = one (image, q head, pair of 128-row q tiles); 12 warps in three warpgroups.  The
+//   producer warpgroup (warps 8-11) hands registers to the two softmax warpgroups with
+//   setmaxnreg (104 / 192 per thread) so the 128-score rows and their 64 packed P pairs
+//   stay in registers.
 //   warp 8      TMA producer: the two Q tiles once, then K/V tiles of 128 keys (SWIZZLE_128B)
 //               into a 5-stage ring shared by both q tiles; mbarrier complete_tx; single-CTA loads.
 //   warp 9      allocates 512 TMEM columns; one lane issues tcgen05.mma (cta_group::1, f16):
@@ -17,9 +20,11 @@
 //               tensor core computes it while the softmax of tile j runs.
 //   warps 0-3   softmax warpgroup 0 (q tile 0), warps 4-7 warpgroup 1 (q tile 1): one thread
 //               per q row (= TMEM lane).  tcgen05.ld of the S row; mask only on tiles that
-//               cross the causal diagonal / the key end; exp2 with the scale folded into one
-//               packed FFMA2 and evaluated two at a time by MUFU.EX2 on f16x2 (the result is
-//               already the f16 P pair; the row sum adds the same rounded values in f32); P
+//               cross the causal diagonal / the key end; row max with 3-input max; exp2 with
+//               the scale folded into one packed FFMA2 and evaluated two at a time, mostly by
+//               MUFU.EX2 on f16x2 and for 6 of every 16 pairs by a cubic on the FMA pipe (the
+//               result is already the f16 P pair; the row sum adds the same rounded values);
+//               all of P(j) is computed before waiting for P(j-1).V to free the P buffer; P
 //               is stored into TMEM (tcgen05.st) and the P.V MMA takes its A operand from
 //               there, so P never touches shared memory.  O stays in TMEM; it is rescaled (tcgen05.ld/st) only when a
 //               row's max grows by more than 2^8 (lazy rescale: the final O / l is exact for
@@ -45,11 +50,22 @@ constexpr int BM = 128;  // q rows per tile (two tiles per CTA)
 constexpr int BN = 128;  // keys per tile
 constexpr int D = kHeadDim;
 constexpr int kStages = 5;  // K/V ring depth: TMA latency (~2 us under load) spans >1 tile
-constexpr int kThreads = 320;  // 10 warps: 0-7 softmax (two warpgroups), 8 TMA, 9 MMA
+// 12 warps (three warpgroups): 0-7 softmax (two warpgroups), 8 TMA, 9 MMA, 10-11 idle.  The
+// block launches with 168 registers per thread (the cap for 384 threads); the producer
+// warpgroup then gives registers back (104 each) and the softmax warpgroups take 192 each:
+// 8 * 32 * 192 + 4 * 32 * 104 = 62464 <= 384 * 168 = 64512, so the increase never waits.
+constexpr int kThreads = 384;
+constexpr int kSoftmaxRegs = 192;
+constexpr int kProducerRegs = 104;
+static_assert(8 * 32 * kSoftmaxRegs + 4 * 32 * kProducerRegs <= kThreads * 168, "register split");
 constexpr uint32_t kTileBytes = BM * D * 2;  // one Q, K or V tile: 16 KB
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (factor 256)
+#ifndef P2P_POLY_PAIRS
+#define P2P_POLY_PAIRS 6
+#endif
+constexpr int kPolyPairs = P2P_POLY_PAIRS;  // of every 16 exp pairs, these use the cubic
 
 // TMEM columns of q tile w: S at 256w (128 f32 columns), P at 256w + 128 (128 keys as 64
 // packed f16x2 columns), O at 256w + 192 (64 f32 columns).
@@ -161,6 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
+  if (warp >= 8) {
+  regs_dec<kProducerRegs>();  // the whole producer warpgroup, before its warps part ways
   if (warp == 8) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -268,8 +286,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&s.kv_empty[st]);
       }
     }
-  } else if (warp < 8) {
+  }
+  } else {
     // ------------------------------------------------------------------ softmax warpgroups
+    regs_inc<kSoftmaxRegs>();
     const int w = warp >> 2;           // q tile of this warpgroup
     const int r = threadIdx.x & 127;   // q row within the tile = TMEM lane
     const uint32_t lane_addr = tmem + (uint32_t((warp & 3) * 32) << 16);
@@ -304,33 +324,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (key0 + c * 32 + i >= key_lim) sv[c][i] = __float_as_uint(-INFINITY);
       }
-      // row max with 8 independent chains (a single 128-long fmax chain is latency-bound)
-      float m8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
+      // row max: four independent chains of 3-input max
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(sv[c][i]));
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int i = 0; i < 32; i += 2)
+          m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], __uint_as_float(sv[c][i]),
+                                   __uint_as_float(sv[c][i + 1]));
+      const float mx = fmax3(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
       // lazy rescale: keep the reference max unless this tile exceeds it by > 2^8
       const bool grow = (mx - m_raw) * sl2 > kRescaleLog2;
       const float alpha = grow ? fast_exp2((m_raw - mx) * sl2) : 1.0f;  // 0 on the first tile
       if (grow) m_raw = mx;
       const float neg = (m_raw == -INFINITY) ? 0.f : -m_raw * sl2;
-      // P buffer w is free (and O holds P(j-1).V) once P(j-1).V has completed
-      if (j > 0 && !wait_bar(s, &s.pv_done[w], (j - 1) & 1, p.err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // P(j) = exp2(s * scale_log2 - m * scale_log2) as packed f16 pairs into TMEM, 64 keys
-      // (32 columns) per store
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};  // 4 independent partial sums
+      // P(j) = exp2(s * scale_log2 - m * scale_log2) as 64 packed f16 pairs in registers, all
+      // computed before waiting for the P buffer: of every 16 pairs, kPolyPairs go through the
+      // FMA-pipe cubic and the rest through the MUFU, so that neither pipe alone bounds the tile.
+      uint32_t pk[2][32];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           const int c = half * 2 + cc;
@@ -339,12 +352,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             float x0, x1;  // s * scale_log2 - m * scale_log2 for two keys (one FFMA2)
             fma2(__uint_as_float(sv[c][2 * i]), __uint_as_float(sv[c][2 * i + 1]), sl2, neg, x0,
                  x1);
-            pk[cc * 16 + i] = ex2_f16x2(x0, x1);              // both exps as the f16 P pair
-            ps[i & 3] = add_f16x2_to_f32(pk[cc * 16 + i], ps[i & 3]);  // f32 row sum
+            pk[half][cc * 16 + i] = i < kPolyPairs ? ex2_poly_f16x2(x0, x1) : ex2_f16x2(x0, x1);
           }
         }
-        tmem_st32(lane_addr + col_p(w) + half * 32, pk);
       }
+      // row sum: f16x2 partial sums of 4 pairs, then two mixed-precision adds into f32
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int half = 0; half < 2; ++half)
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          const uint32_t* q4 = &pk[half][4 * g];
+          ps[g & 3] = add_f16x2_to_f32(hadd2(hadd2(q4[0], q4[1]), hadd2(q4[2], q4[3])), ps[g & 3]);
+        }
+      // P buffer w is free (and O holds P(j-1).V) once P(j-1).V has completed
+      if (j > 0 && !wait_bar(s, &s.pv_done[w], (j - 1) & 1, p.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      tmem_st32(lane_addr + col_p(w), pk[0]);
+      tmem_st32(lane_addr + col_p(w) + 32, pk[1]);
       tmem_st_wait();
       l_run = fmaf(l_run, alpha, (ps[0] + ps[1]) + (ps[2] + ps[3]));
       // rescale O (it holds P(j-1).V) before P(j).V accumulates into it; warp-uniform because
