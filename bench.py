@@ -254,17 +254,21 @@ class DecodeWorkload:
 
 
 def e2e_decode(wl, steps, warmup):
-    """The user-facing call path with host buffers: pinned H2D of the step's 6 qkv rows,
-    p2p_decode_step through the C ABI, D2H of the 6 output rows, host waits for the result."""
+    """The user-facing per-token call with host buffers: p2p_decode_step whose 6 qkv rows and 6
+    output rows live in page-locked host memory, so the kernel itself reads the step's inputs
+    from the host and writes its outputs back (no separate copy); the host then waits for the
+    result."""
     import torch
     stream = torch.cuda.current_stream()
     h_in = torch.randn(wl.qkv.shape, dtype=torch.float16).pin_memory()
     h_out = torch.empty(wl.out.shape, dtype=torch.float16).pin_memory()
+    plans = [wl.ctx.plan_decode_step(wl.prm, [(h_in[l], wl.nw[l], kc, vc, h_out[l])
+                                              for l, (kc, vc) in enumerate(c)],
+                                     wl.rope, wl.cap, use_meta=True)
+             for c in wl.copies]
 
     def one(i):
-        wl.qkv.copy_(h_in, non_blocking=True)
-        wl.step(i)
-        h_out.copy_(wl.out, non_blocking=True)
+        plans[i % len(plans)].run()
         stream.synchronize()
 
     for i in range(warmup):

@@ -129,7 +129,11 @@ p2p_status p2p_attn(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q, int
 /* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to
  * P2P_MAX_LAYERS attention layers in ONE launch: for each layer the new token's qkv row is
  * normed/rotated, its k/v are appended at row pos, and its Hq output rows are written.
- * Layers are independent (each layer's q comes from its own qkv row). */
+ * Layers are independent (each layer's q comes from its own qkv row).  The qkv and out rows
+ * may be device memory or page-locked host memory (cudaHostAlloc / cudaHostRegister): the
+ * kernel then reads the inputs and writes the outputs across the host link itself, with no
+ * separate copy, and the host reads the outputs after synchronizing the stream.  The caches,
+ * norm weights, rope table and meta buffer stay in device memory. */
 #define P2P_MAX_LAYERS 16
 typedef struct p2p_decode_layer {
   const void* qkv;    /* [Hq*D + 2*Hkv*D] row of the new token */

@@ -37,6 +37,7 @@
 // memory with st.async, which completes bytes on the owner's mbarrier.  The owner waits on
 // that mbarrier (bounded), combines and writes the output; every other CTA exits as soon as it
 // has pushed.  No workspace, no atomics, no global fences and no cluster barrier at the end.
+#include <map>
 #include <mutex>
 #include <set>
 
@@ -897,11 +898,41 @@ int decode_max_splits(int64_t max_len, int hkv, int nz, int num_sms, int* min_sp
   return int(g < 1 ? 1 : g);
 }
 
+// Clusters of `c` CTAs of kernel `k` the device can hold at once (cudaOccupancyMaxActiveClusters
+// does not depend on the grid size); asked once per (kernel, c) and remembered, since the
+// query costs host time and a decode step is launched once per token.
+int max_active_clusters(const KernelInfo& k, int c) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(k.fn, c);
+  const auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(c), 1, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = size_t(k.smem);
+  cudaLaunchAttribute at{};
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = unsigned(c);
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k.fn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache.emplace(key, n);
+  return n;
+}
+
 int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fused,
                           int num_sms) {
   // One wave: the (layer, head chunk) rows times the cluster size fill the 3 CTA slots of every
-  // SM at most; at most 16 CTAs per cluster and one 16-key pass per CTA at least.  The size is
-  // then lowered until the device reports that all clusters are resident at once.
+  // SM at most; at most kMaxCluster CTAs per cluster and one 16-key pass per CTA at least.  The
+  // size is then lowered until the device reports that all clusters are resident at once.
   const int rows = hkv * head_chunks(group) * nz;
   const int64_t slots = int64_t(num_sms) * 3;
   int64_t c = slots / rows;
@@ -911,25 +942,8 @@ int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fuse
   if (c < 2) return 1;
   const KernelInfo k = pick(group, true, fused, kLayers, true);
   if (!k.fn || configure(k, true) != cudaSuccess) return 1;
-  for (; c >= 2; --c) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(unsigned(c), unsigned(hkv * head_chunks(group)), unsigned(nz));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = size_t(k.smem);
-    cudaLaunchAttribute at{};
-    at.id = cudaLaunchAttributeClusterDimension;
-    at.val.clusterDim.x = unsigned(c);
-    at.val.clusterDim.y = 1;
-    at.val.clusterDim.z = 1;
-    cfg.attrs = &at;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, k.fn, &cfg) != cudaSuccess) {
-      cudaGetLastError();
-      continue;
-    }
-    if (n >= rows) return int(c);
-  }
+  for (; c >= 2; --c)
+    if (max_active_clusters(k, int(c)) >= rows) return int(c);
   return 1;
 }
 

@@ -205,6 +205,39 @@ def test_decode_step_device_position_in_large_cache(ctx, oracle, hq, past):
         assert_close(host(layers[l][4])[None], out_o, what=f"layer {l} past {past}")
 
 
+def test_decode_step_host_rows(ctx, oracle):
+    """qkv and out rows in page-locked host memory: the decode kernel reads the inputs and
+    writes the outputs across the host link itself; two steps with different inputs and
+    positions both match the oracle, and the caches get the new rows."""
+    import p2p_b200
+    hq, hkv, cap, n_layers = 32, 8, 700, 3
+    rope = oracle.rope_table(cap)
+    prm = p2p_b200.Params(hq, hkv)
+    rng = np.random.default_rng(4242)
+    row = (hq + 2 * hkv) * D
+    kcs = [rng.standard_normal((cap, hkv, D)).astype(np.float16) for _ in range(n_layers)]
+    vcs = [rng.standard_normal((cap, hkv, D)).astype(np.float16) for _ in range(n_layers)]
+    nws = [(1 + 0.1 * rng.standard_normal(2 * D)).astype(np.float16) for _ in range(n_layers)]
+    h_in = torch.zeros((n_layers, row), dtype=torch.float16).pin_memory()
+    h_out = torch.zeros((n_layers, hq * D), dtype=torch.float16).pin_memory()
+    layers = [(h_in[l], dev(nws[l]), dev(kcs[l]), dev(vcs[l]), h_out[l]) for l in range(n_layers)]
+    plan = ctx.plan_decode_step(prm, layers, dev(rope), cap, use_meta=True)
+    stream = torch.cuda.current_stream()
+    for past in (500, 501):
+        qkv = rng.standard_normal((n_layers, row)).astype(np.float16)
+        h_in.copy_(torch.from_numpy(qkv))
+        ctx.meta_write(past, 1, stream=stream)
+        plan.run(stream)
+        stream.synchronize()
+        ctx.sync()
+        for l in range(n_layers):
+            _, kc_o, vc_o, out_o = oracle_decode(oracle, hq, hkv, qkv[l:l + 1], nws[l], rope,
+                                                 kcs[l], vcs[l], past)
+            kcs[l], vcs[l] = kc_o, vc_o  # the next step sees this step's k/v rows
+            assert np.array_equal(bits(host(layers[l][2])[past]), bits(kc_o[past]))
+            assert_close(h_out[l].numpy()[None], out_o, what=f"host rows layer {l} past {past}")
+
+
 def test_decode_fp32_storage(ctx, oracle):
     """The fp32 case: past 512 + 1 new, RoPE theta 1e6 on positions 0..512, no q/k norm."""
     import p2p_b200
