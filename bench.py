@@ -383,6 +383,30 @@ def run_prefill_sharded(ctx, rank, world, s, steps, warmup):
     return timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
 
 
+def run_prefill_scatter(ctx, rank, world, s, steps, warmup):
+    """The same head-sharded prefill with the flash kernel writing its rows into every rank's
+    full [s][Hq*64] output over NVLink (CUDA IPC), then one single-element all-reduce ordering
+    the ranks, inside the timed region."""
+    import torch
+    from p2p_b200.sharding import ScatterHeadShardedPrefill
+    sp = ScatterHeadShardedPrefill(ctx, HQ, HKV, world, rank, max_tokens=s)
+    g = torch.Generator(device="cuda").manual_seed(33)
+    qkv_full = (0.5 * torch.randn((s, (HQ + 2 * HKV) * D), generator=g, device="cuda")).half()
+    qkv_l = qkv_full[:, sp.local_qkv_columns().cuda()].contiguous()
+    del qkv_full
+    rope = ctx.rope_table(s, D, 1e6)
+    kc = torch.zeros((s, sp.kvn, D), device="cuda", dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    q_buf = torch.zeros((s, sp.qn * D), device="cuda", dtype=torch.float16)
+
+    def step(i):
+        sp(qkv_l, None, rope, kc, vc, q_buf, 0, s)
+
+    ms = timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
+    sp.close()
+    return ms
+
+
 def run_vision_split(ctx, rank, world, steps, warmup):
     """The vision batch split by image over the ranks (no collective)."""
     import torch
@@ -619,6 +643,12 @@ def main():
                 side[f"prefill_head_sharded_s{s_tok}"] = {
                     "workload": f"causal prefill S={s_tok}, 32q/8kv split by kv-head group over "
                                 f"{world} GPUs + NCCL all-gather + [S][2048] assembly",
+                    "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
+                ms = max_over_ranks(run_prefill_scatter(ctx, rank, world, s_tok, 10, 3), world)
+                side[f"prefill_head_scatter_s{s_tok}"] = {
+                    "workload": f"causal prefill S={s_tok}, 32q/8kv split by kv-head group over "
+                                f"{world} GPUs, flash epilogue writes every rank's [S][2048] "
+                                f"output over NVLink (no all-gather)",
                     "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
             ms = max_over_ranks(run_vision_split(ctx, rank, world, 10, 3), world)
             side["vision_image_split"] = {

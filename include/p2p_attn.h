@@ -126,7 +126,36 @@ p2p_status p2p_attn(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q, int
                     int64_t ld_o, const uint32_t* meta_dev, int32_t pos0, int32_t m_tokens,
                     void* stream);
 
-/* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to
+/* Head-sharded causal prefill on several GPUs of one node (one process per GPU).  Each rank
+ * runs ATTN (kernels.js:268-319) for its own kv-head group -- prm counts the local heads, q
+ * and the caches hold only them -- and the kernel writes every output row straight into the
+ * full [M][ld_o] output buffer of every rank: outs[0] is this rank's own, outs[1..n_outs)
+ * other ranks' buffers opened with p2p_shared_open (the rows cross NVLink as the kernel's own
+ * stores), local head h at column (out_head0 + h) * D of each.  This replaces ATTN followed by
+ * an all-gather of the per-rank slices and their reassembly.  The call only orders this
+ * rank's writes; before a rank reads its buffer (or any rank writes the buffers again) the
+ * ranks must order themselves, e.g. with any collective on the stream after this call. */
+#define P2P_MAX_SCATTER_OUTS 8
+p2p_status p2p_attn_scatter(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q,
+                            int64_t ld_q, const void* k_cache, const void* v_cache,
+                            int64_t kv_cap_tokens, void* const* outs, int32_t n_outs,
+                            int64_t ld_o, int32_t out_head0, const uint32_t* meta_dev,
+                            int32_t pos0, int32_t m_tokens, void* stream);
+
+/* Device buffers shared between the processes of one node (CUDA IPC): p2p_shared_alloc
+ * allocates `bytes` on the context's device and returns an opaque handle that another
+ * process passes to p2p_shared_open to map the same memory (its GPU then reads and writes it
+ * over NVLink).  Close every mapping (p2p_shared_close) before the owner frees the buffer
+ * (p2p_shared_free); both wait for the device first. */
+#define P2P_IPC_HANDLE_BYTES 64
+p2p_status p2p_shared_alloc(p2p_ctx* ctx, size_t bytes, void** ptr,
+                            unsigned char handle[P2P_IPC_HANDLE_BYTES]);
+p2p_status p2p_shared_free(p2p_ctx* ctx, void* ptr);
+p2p_status p2p_shared_open(p2p_ctx* ctx, const unsigned char handle[P2P_IPC_HANDLE_BYTES],
+                           void** ptr);
+p2p_status p2p_shared_close(p2p_ctx* ctx, void* ptr);
+
+/* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to/* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to
  * P2P_MAX_LAYERS attention layers in ONE launch: for each layer the new token's qkv row is
  * normed/rotated, its k/v are appended at row pos, and its Hq output rows are written.
  * Layers are independent (each layer's q comes from its own qkv row).  The qkv and out rows

@@ -24,6 +24,7 @@ P2P_ERR_UNSUPPORTED = 7
 P2P_F16 = 0
 P2P_F32 = 1
 MAX_LAYERS = 16
+P2P_IPC_HANDLE_BYTES = 64
 
 
 class P2PError(RuntimeError):
@@ -96,6 +97,12 @@ PROTOTYPES = {
     "p2p_attn_bidir": (_st, [_v, _pp, _v, _v, _v, _v, _i64, _i32, _i32, _v]),
     "p2p_attn_decode_ragged_noalloc": (
         _st, [_v, _pp, _v, _i64, _v, _v, _v, _v, _v, _v, _i32, _i32, _i32, _v, _i64, _v]),
+    "p2p_attn_scatter": (
+        _st, [_v, _pp, _v, _i64, _v, _v, _i64, C.POINTER(_v), _i32, _i64, _i32, _v, _i32, _i32, _v]),
+    "p2p_shared_alloc": (_st, [_v, C.c_size_t, C.POINTER(_v), C.c_char_p]),
+    "p2p_shared_free": (_st, [_v, _v]),
+    "p2p_shared_open": (_st, [_v, C.c_char_p, C.POINTER(_v)]),
+    "p2p_shared_close": (_st, [_v, _v]),
     "p2p_debug_set_alloc_limit": (_st, [_i64]),
     "p2p_debug_set_wait_deficit": (_st, [_i32]),
 }

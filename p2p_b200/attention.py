@@ -114,6 +114,39 @@ class Context:
             _ptr(k_cache), _ptr(v_cache), k_cache.shape[0], self.meta_ptr if use_meta else None,
             pos0, m, _stream(stream)))
 
+    def attn_scatter(self, prm: Params, q: torch.Tensor, k_cache: torch.Tensor,
+                     v_cache: torch.Tensor, outs: Sequence[int], ld_o: int, out_head0: int, *,
+                     pos0: int = 0, m_tokens: Optional[int] = None, use_meta: bool = False,
+                     stream=None):
+        """p2p_attn_scatter: causal prefill over this rank's heads, every output row written
+        into each buffer of `outs` (device addresses: this rank's own first, then the other
+        ranks' opened with shared_open) at column (out_head0 + h) * 64."""
+        m = q.shape[0] if m_tokens is None else m_tokens
+        arr = (C.c_void_p * len(outs))(*[int(o) for o in outs])
+        self._chk(lib.p2p_attn_scatter(
+            self.h, C.byref(prm.c()), _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache),
+            k_cache.shape[0], arr, len(outs), ld_o, out_head0,
+            self.meta_ptr if use_meta else None, pos0, m, _stream(stream)))
+
+    def shared_alloc(self, nbytes: int):
+        """p2p_shared_alloc: (device address, IPC handle bytes) of a new node-shared buffer."""
+        ptr = C.c_void_p()
+        handle = C.create_string_buffer(_lib.P2P_IPC_HANDLE_BYTES)
+        self._chk(lib.p2p_shared_alloc(self.h, nbytes, C.byref(ptr), handle))
+        return ptr.value, handle.raw
+
+    def shared_open(self, handle: bytes) -> int:
+        """p2p_shared_open: this process's address of another process's shared buffer."""
+        ptr = C.c_void_p()
+        self._chk(lib.p2p_shared_open(self.h, handle, C.byref(ptr)))
+        return ptr.value
+
+    def shared_close(self, ptr: int):
+        self._chk(lib.p2p_shared_close(self.h, C.c_void_p(ptr)))
+
+    def shared_free(self, ptr: int):
+        self._chk(lib.p2p_shared_free(self.h, C.c_void_p(ptr)))
+
     def attn(self, prm: Params, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
              out: torch.Tensor, *, pos0: int = 0, m_tokens: Optional[int] = None,
              use_meta: bool = False, stream=None):

@@ -39,6 +39,7 @@ struct p2p_ctx {
   int32_t* counters = nullptr;
   size_t counters_bytes = 0;
   std::map<std::tuple<int, int, double, int>, void*> rope;
+  std::map<void*, size_t> shared;  // p2p_shared_alloc buffers and their sizes
   std::string err;
 };
 
@@ -242,6 +243,46 @@ p2p_status run_decode(p2p_ctx* ctx, const p2p_attn_params* prm, p2p::DecodeArgs&
   return P2P_OK;
 }
 
+// The tcgen05 flash kernel on a causal prompt chunk: rows pos0 .. pos0+M-1 of q against
+// cache keys 0 .. pos0+M-1; outs[0] is this GPU's output, outs[1..] other buffers of the same
+// layout (other GPUs') that receive the same rows; head h lands at column (out_head0 + h)*D.
+p2p_status run_causal_flash(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q,
+                            int64_t ld_q, const void* k_cache, const void* v_cache,
+                            int64_t kv_cap_tokens, void* const* outs, int n_outs, int64_t ld_o,
+                            int out_head0, const uint32_t* meta_dev, int32_t pos0,
+                            int32_t m_tokens, cudaStream_t s) {
+  p2p::FlashArgs f{};
+  f.q = q;
+  f.k = k_cache;
+  f.v = v_cache;
+  f.out = outs[0];
+  for (int t = 1; t < n_outs; ++t) f.extra_out[t - 1] = outs[t];
+  f.n_extra_out = n_outs - 1;
+  f.out_head0 = out_head0;
+  f.ld_q = ld_q;
+  f.ld_kv = int64_t(prm->num_kv_heads) * prm->head_dim;
+  f.ld_o = ld_o;
+  f.q_rows_total = m_tokens;
+  f.kv_rows_total = kv_cap_tokens;
+  f.batch_stride_q_rows = 0;
+  f.batch_stride_kv_rows = 0;
+  f.batch = 1;
+  f.s_q = m_tokens;
+  f.s_kv = 0;
+  f.hq = prm->num_heads;
+  f.hkv = prm->num_kv_heads;
+  f.causal = 1;
+  f.meta = meta_dev;
+  f.pos0_host = pos0;
+  f.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
+  f.err = ctx->dev_err;
+  f.wait_deficit = g_wait_deficit.load();
+  cudaError_t e = p2p::launch_flash(f, s);
+  if (e == cudaErrorNotSupported) return fail(ctx, P2P_ERR_UNSUPPORTED, "prefill kernel");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill launch");
+  return P2P_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -309,6 +350,7 @@ p2p_status p2p_ctx_destroy(p2p_ctx* ctx) {
   DeviceGuard g(ctx->device);
   cudaDeviceSynchronize();
   for (auto& kv : ctx->rope) cudaFree(kv.second);
+  for (auto& kv : ctx->shared) dev_free(kv.first, kv.second);
   dev_free(ctx->meta, 16);
   dev_free(ctx->dev_err, sizeof(int32_t));
   dev_free(ctx->partials, ctx->partials_bytes);
@@ -584,32 +626,92 @@ p2p_status p2p_attn(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q, int
   }
   if ((ld_q % 8) || (ld_o % 8) || !aligned16(q) || !aligned16(out))
     return fail(ctx, P2P_ERR_INVALID_ARG, "attn prefill: q/out must be 16-byte aligned rows");
-  p2p::FlashArgs f{};
-  f.q = q;
-  f.k = k_cache;
-  f.v = v_cache;
-  f.out = out;
-  f.ld_q = ld_q;
-  f.ld_kv = int64_t(prm->num_kv_heads) * prm->head_dim;
-  f.ld_o = ld_o;
-  f.q_rows_total = m_tokens;
-  f.kv_rows_total = kv_cap_tokens;
-  f.batch_stride_q_rows = 0;
-  f.batch_stride_kv_rows = 0;
-  f.batch = 1;
-  f.s_q = m_tokens;
-  f.s_kv = 0;
-  f.hq = prm->num_heads;
-  f.hkv = prm->num_kv_heads;
-  f.causal = 1;
-  f.meta = meta_dev;
-  f.pos0_host = pos0;
-  f.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
-  f.err = ctx->dev_err;
-  f.wait_deficit = g_wait_deficit.load();
-  cudaError_t e = p2p::launch_flash(f, s);
-  if (e == cudaErrorNotSupported) return fail(ctx, P2P_ERR_UNSUPPORTED, "prefill kernel");
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill launch");
+  return run_causal_flash(ctx, prm, q, ld_q, k_cache, v_cache, kv_cap_tokens, &out, 1, ld_o, 0,
+                          meta_dev, pos0, m_tokens, s);
+}
+
+static_assert(P2P_MAX_SCATTER_OUTS == p2p::kMaxFlashOuts, "one flash launch writes every output");
+
+p2p_status p2p_attn_scatter(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q,
+                            int64_t ld_q, const void* k_cache, const void* v_cache,
+                            int64_t kv_cap_tokens, void* const* outs, int32_t n_outs,
+                            int64_t ld_o, int32_t out_head0, const uint32_t* meta_dev,
+                            int32_t pos0, int32_t m_tokens, void* stream) {
+  p2p_status st = check_params(ctx, prm, false);
+  if (st != P2P_OK) return st;
+  const int64_t qw = int64_t(prm->num_heads) * prm->head_dim;
+  if (!q || !k_cache || !v_cache || !outs || n_outs < 1 || n_outs > P2P_MAX_SCATTER_OUTS)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn_scatter: NULL buffer or %d outputs (1..%d)",
+                n_outs, P2P_MAX_SCATTER_OUTS);
+  for (int t = 0; t < n_outs; ++t)
+    if (!outs[t] || !aligned16(outs[t]))
+      return fail(ctx, P2P_ERR_INVALID_ARG, "attn_scatter: output %d is NULL or misaligned", t);
+  if (m_tokens < 0 || ld_q < qw || out_head0 < 0 || ld_o < (int64_t(out_head0) * prm->head_dim + qw) ||
+      kv_cap_tokens <= 0 || (!meta_dev && pos0 < 0) || (ld_q % 8) || (ld_o % 8) || !aligned16(q))
+    return fail(ctx, P2P_ERR_INVALID_ARG,
+                "attn_scatter: M %d ld_q %lld ld_o %lld out_head0 %d cap %lld pos0 %d", m_tokens,
+                (long long)ld_q, (long long)ld_o, out_head0, (long long)kv_cap_tokens, pos0);
+  if (!meta_dev && int64_t(pos0) + m_tokens > kv_cap_tokens)
+    return fail(ctx, P2P_ERR_KV_FULL, "attn_scatter: pos0 %d + M %d > cache rows %lld", pos0,
+                m_tokens, (long long)kv_cap_tokens);
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn_scatter: cache buffers must be 16-byte aligned");
+  if (m_tokens == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  return run_causal_flash(ctx, prm, q, ld_q, k_cache, v_cache, kv_cap_tokens, outs, n_outs, ld_o,
+                          out_head0, meta_dev, pos0, m_tokens, pick_stream(ctx, stream));
+}
+
+p2p_status p2p_shared_alloc(p2p_ctx* ctx, size_t bytes, void** ptr,
+                            unsigned char handle[P2P_IPC_HANDLE_BYTES]) {
+  if (!ctx || !ptr || !handle || bytes == 0) return P2P_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  DeviceGuard g(ctx->device);
+  void* p = nullptr;
+  if (dev_alloc(&p, bytes) != cudaSuccess) return fail(ctx, P2P_ERR_OOM, "shared buffer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    dev_free(p, bytes);
+    return cuda_fail(ctx, e, "cudaIpcGetMemHandle");
+  }
+  static_assert(sizeof(h) <= P2P_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memset(handle, 0, P2P_IPC_HANDLE_BYTES);
+  std::memcpy(handle, &h, sizeof(h));
+  ctx->shared[p] = bytes;
+  *ptr = p;
+  return P2P_OK;
+}
+
+p2p_status p2p_shared_free(p2p_ctx* ctx, void* ptr) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  const auto it = ctx->shared.find(ptr);
+  if (it == ctx->shared.end()) return fail(ctx, P2P_ERR_INVALID_ARG, "shared_free: unknown buffer");
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  dev_free(it->first, it->second);
+  ctx->shared.erase(it);
+  return P2P_OK;
+}
+
+p2p_status p2p_shared_open(p2p_ctx* ctx, const unsigned char handle[P2P_IPC_HANDLE_BYTES],
+                           void** ptr) {
+  if (!ctx || !handle || !ptr) return P2P_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  DeviceGuard g(ctx->device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaIpcOpenMemHandle");
+  return P2P_OK;
+}
+
+p2p_status p2p_shared_close(p2p_ctx* ctx, void* ptr) {
+  if (!ctx || !ptr) return P2P_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaIpcCloseMemHandle");
   return P2P_OK;
 }
 

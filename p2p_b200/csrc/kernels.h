@@ -83,11 +83,15 @@ int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fuse
 int decode_max_splits(int64_t max_len, int hkv, int nz, int num_sms, int* min_split);
 
 // ---- prefill_sm100.cu ----------------------------------------------------------------------
+constexpr int kMaxFlashOuts = 8;  // output buffers one flash launch writes (one per rank)
 struct FlashArgs {
   const void* q;  // [B][Sq][ld_q] rows, head h at column h*64
   const void* k;  // [B][Skv][ld_kv] rows, kv head at column kh*64
   const void* v;
-  void* out;      // [B][Sq][ld_o]
+  void* out;      // [B][Sq][ld_o]; head h of this call at column (out_head0 + h)*64
+  void* extra_out[kMaxFlashOuts - 1];  // more buffers of out's layout that get the same rows
+  int32_t n_extra_out;                 // (other GPUs' outputs, written over NVLink)
+  int32_t out_head0;
   int64_t ld_q, ld_kv, ld_o;
   int64_t q_rows_total, kv_rows_total;  // rows of the q / kv 2-D views (tensor-map extents)
   int64_t batch_stride_q_rows, batch_stride_kv_rows;  // rows between images

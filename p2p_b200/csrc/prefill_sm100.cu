@@ -85,7 +85,9 @@ struct __align__(1024) Smem {
 };
 
 struct FlashParams {
-  __half* out;
+  __half* out[kMaxFlashOuts];  // [0] this GPU's output; the others are peers' (NVLink stores)
+  int32_t n_out;
+  int32_t out_head0;           // head h is written at column (out_head0 + h) * 64
   int64_t ld_o;
   int64_t bs_q, bs_kv;  // rows between images
   int64_t kv_rows_total;
@@ -405,15 +407,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int rows = w == 0 ? rows0 : rows1;
       if (r < rows) {
         const float inv = 1.0f / l_run;
-        __half* dst = p.out + (int64_t(b) * p.bs_q + q_first + r) * p.ld_o + int64_t(h) * D;
+        uint4 row[D / 8];
 #pragma unroll
         for (int i = 0; i < D; i += 8) {
           const int c = i >> 5, e = i & 31;
-          *reinterpret_cast<uint4*>(dst + i) = make_uint4(
+          row[i / 8] = make_uint4(
               pack_half2(__uint_as_float(ov[c][e]) * inv, __uint_as_float(ov[c][e + 1]) * inv),
               pack_half2(__uint_as_float(ov[c][e + 2]) * inv, __uint_as_float(ov[c][e + 3]) * inv),
               pack_half2(__uint_as_float(ov[c][e + 4]) * inv, __uint_as_float(ov[c][e + 5]) * inv),
               pack_half2(__uint_as_float(ov[c][e + 6]) * inv, __uint_as_float(ov[c][e + 7]) * inv));
+        }
+        const int64_t off =
+            (int64_t(b) * p.bs_q + q_first + r) * p.ld_o + int64_t(p.out_head0 + h) * D;
+        // this GPU's output first, then every peer's (head-sharded prefill: the rows reach
+        // the other GPUs over NVLink here, instead of through a separate all-gather)
+        for (int t = 0; t < p.n_out; ++t) {
+          uint4* dst = reinterpret_cast<uint4*>(p.out[t] + off);
+#pragma unroll
+          for (int i = 0; i < D / 8; ++i) dst[i] = row[i];
         }
       }
     }
@@ -469,7 +480,11 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
       !make_map(&tv, a.v, kvw, a.ld_kv, a.kv_rows_total))
     return cudaErrorInvalidValue;
   FlashParams p{};
-  p.out = static_cast<__half*>(a.out);
+  if (a.n_extra_out < 0 || a.n_extra_out > kMaxFlashOuts - 1) return cudaErrorInvalidValue;
+  p.out[0] = static_cast<__half*>(a.out);
+  for (int t = 0; t < a.n_extra_out; ++t) p.out[1 + t] = static_cast<__half*>(a.extra_out[t]);
+  p.n_out = 1 + a.n_extra_out;
+  p.out_head0 = a.out_head0;
   p.ld_o = a.ld_o;
   p.bs_q = a.batch_stride_q_rows;
   p.bs_kv = a.batch_stride_kv_rows;

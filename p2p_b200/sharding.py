@@ -5,8 +5,9 @@ Where the work shards naturally:
     count) gives every rank a near-equal share of KV bytes to stream; no collective on the
     data path.
   * long-context prefill -- KV-head groups: rank g owns kv heads [g*Hkv/G, (g+1)*Hkv/G) and
-    their query heads, computes out[:, heads_g] and its KV-cache slice; one all-gather over
-    NVLink assembles the [S][Hq*D] output.
+    their query heads, computes out[:, heads_g] and its KV-cache slice; either one NCCL
+    all-gather assembles the [S][Hq*D] output (HeadShardedPrefill), or the flash kernel writes
+    its rows straight into every rank's full output over NVLink (ScatterHeadShardedPrefill).
   * vision -- independent images.
   * single-sequence decode does not shard (8.4 MB per layer is less than the cost of a
     cross-GPU exchange): replicas only.
@@ -101,3 +102,59 @@ class HeadShardedPrefill:
         else:
             out_full.copy_(out_local)
         return out_full
+
+
+class ScatterHeadShardedPrefill(HeadShardedPrefill):
+    """HeadShardedPrefill without the all-gather: the flash kernel of every rank writes each of
+    its output rows straight into the full [max_tokens][Hq*64] output buffer of every rank (its
+    own, and the other ranks' through CUDA IPC mappings, so the rows cross NVLink as the
+    kernel's own stores, overlapped with its compute).  One all-reduce of a single element then
+    orders the ranks, after which every rank's buffer holds all heads.
+
+    The buffers are reused by every call: a rank must be done reading one result before any
+    rank starts the next call (in a model, the next layer's collective orders that)."""
+
+    def __init__(self, ctx, num_heads: int, num_kv_heads: int, world: int, rank: int,
+                 max_tokens: int, group=None):
+        import torch
+        import torch.distributed as dist
+        from .attention import _from_device_ptr
+        super().__init__(ctx, num_heads, num_kv_heads, world, rank, group)
+        self.max_tokens = max_tokens
+        self.ld_o = num_heads * 64
+        nbytes = max_tokens * self.ld_o * 2
+        self.own, handle = ctx.shared_alloc(nbytes)
+        handles = [None] * world
+        if world > 1:
+            dist.all_gather_object(handles, handle, group=group)
+        else:
+            handles[0] = handle
+        self.peers = [ctx.shared_open(handles[r]) for r in range(world) if r != rank]
+        self.outs = [self.own] + self.peers
+        self.out_full = _from_device_ptr(self.own, nbytes, ctx.device).view(torch.float16).view(
+            max_tokens, self.ld_o)
+        self.flag = torch.zeros(1, dtype=torch.float32, device=f"cuda:{ctx.device}")
+
+    def __call__(self, qkv_local, norm_w, rope, k_cache, v_cache, q_buf, pos0: int,
+                 m_tokens: int, stream=None):
+        import torch.distributed as dist
+        if m_tokens > self.max_tokens:
+            raise ValueError(f"{m_tokens} tokens > max_tokens {self.max_tokens}")
+        self.ctx.qk_prep(self.prm, qkv_local, norm_w, rope, q_buf, k_cache, v_cache, pos0=pos0,
+                         m_tokens=m_tokens, stream=stream)
+        self.ctx.attn_scatter(self.prm, q_buf, k_cache, v_cache, self.outs, self.ld_o, self.q0,
+                              pos0=pos0, m_tokens=m_tokens, stream=stream)
+        if self.world > 1:
+            dist.all_reduce(self.flag, group=self.group)  # every rank's rows have landed
+        return self.out_full[:m_tokens]
+
+    def close(self):
+        import torch.distributed as dist
+        for p in self.peers:
+            self.ctx.shared_close(p)
+        self.peers = []
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no rank still maps this rank's buffer
+        if self.own:
+            self.ctx.shared_free(self.own)
+            self.own = None

@@ -1,7 +1,8 @@
 """Multi-GPU paths on real GPUs (skipped with fewer than 2 visible GPUs).
 
 Two NCCL ranks, one process per GPU, rendezvous on 127.0.0.1:
-  * causal prefill split by KV-head group + all-gather vs the oracle on the full heads;
+  * causal prefill split by KV-head group + all-gather vs the oracle on the full heads, and
+    the same with the flash kernel scattering its rows into every rank's output (CUDA IPC);
   * ragged decode split by sequence (LPT by tokens, no collective) vs the oracle.
 """
 import os
@@ -68,6 +69,18 @@ def _worker(rank, world, port, q):
         ok["prefill"] = bool((err <= 2e-3 + 1e-2 * np.abs(want.astype(np.float64))).all())
         ok["prefill_kv_slice"] = bool(np.array_equal(
             kc.cpu().numpy().view(np.uint16), ko[:, sp.kv0:sp.kv0 + sp.kvn].view(np.uint16)))
+        # the same prefill with the flash kernel writing its rows into every rank's output
+        # over NVLink (CUDA IPC mappings) instead of an all-gather; twice in a row
+        from p2p_b200.sharding import ScatterHeadShardedPrefill
+        ssp = ScatterHeadShardedPrefill(ctx, hq, hkv, world, rank, max_tokens=m)
+        for it in range(2):
+            kc.zero_()
+            vc.zero_()
+            full = ssp(qkv_l, dev(nw), dev(rope), kc, vc, q_buf, 0, m)
+            torch.cuda.synchronize()
+            g3 = full.cpu().numpy().astype(np.float64)
+            ok[f"scatter_{it}"] = bool((np.abs(g3 - want) <= 2e-3 + 1e-2 * np.abs(want.astype(np.float64))).all())
+        ssp.close()
         # ragged decode split by sequence
         past = np.array([100, 2000, 37, 700, 1500, 9], np.int32)
         mine = lpt_partition(list(past + 1), world)[rank]

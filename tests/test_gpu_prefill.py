@@ -170,3 +170,30 @@ def test_vision_siglip2_batch16_sampled(ctx, oracle):
         want = np.zeros((1, s, 768), np.float16)
         oracle.vision_attn(12, D, host(q)[i:i + 1], host(k)[i:i + 1], host(v)[i:i + 1], want)
         assert_close(got[i:i + 1], want, what=f"vision image {i}")
+
+
+def test_attn_scatter_two_outputs_head_halves(ctx, oracle):
+    """p2p_attn_scatter on one GPU: the two halves of the heads (as two ranks of a head-sharded
+    prefill would own them) each write their rows into two full-layout buffers at their head
+    columns; both buffers must then equal attention over all heads."""
+    import p2p_b200
+    hq, hkv, m = 32, 8, 300
+    rng = np.random.default_rng(515)
+    q = (0.5 * rng.standard_normal((m, hq * D))).astype(np.float16)
+    kc = (0.5 * rng.standard_normal((m, hkv, D))).astype(np.float16)
+    vc = (0.5 * rng.standard_normal((m, hkv, D))).astype(np.float16)
+    want = np.zeros((m, hq * D), np.float16)
+    oracle.attn(hq, hkv, D, q, kc, vc, want, 0, m)
+    a = torch.zeros((m, hq * D), dtype=torch.float16, device="cuda")
+    b = torch.zeros_like(a)
+    half_q, half_kv = hq // 2, hkv // 2
+    for part in (0, 1):
+        q_p = dev(q[:, part * half_q * D:(part + 1) * half_q * D])
+        kc_p = dev(kc[:, part * half_kv:(part + 1) * half_kv])
+        vc_p = dev(vc[:, part * half_kv:(part + 1) * half_kv])
+        ctx.attn_scatter(p2p_b200.Params(half_q, half_kv), q_p, kc_p, vc_p,
+                         [a.data_ptr(), b.data_ptr()], hq * D, part * half_q, pos0=0,
+                         m_tokens=m)
+    ctx.sync()
+    assert_close(host(a), want, what="scatter output 0")
+    assert np.array_equal(bits(host(a)), bits(host(b)))
