@@ -197,3 +197,25 @@ def test_attn_scatter_two_outputs_head_halves(ctx, oracle):
     ctx.sync()
     assert_close(host(a), want, what="scatter output 0")
     assert np.array_equal(bits(host(a)), bits(host(b)))
+
+
+def test_prefill_device_position_beyond_cache_is_refused(ctx):
+    """A prompt chunk whose device-side position runs past the cache rows: the q rows whose
+    keys the cache does not hold (here the second pair of 128-row tiles) are not written, and
+    p2p_sync reports P2P_ERR_KV_FULL (the reference's 'kv_full'); the context stays usable."""
+    import p2p_b200
+    hq, hkv, m, cap = 32, 8, 300, 400
+    q = torch.ones((m, hq * D), dtype=torch.float16, device="cuda")
+    kc = torch.zeros((cap, hkv, D), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    out = torch.full((m, hq * D), 7.0, dtype=torch.float16, device="cuda")
+    prm = p2p_b200.Params(hq, hkv)
+    ctx.meta_write(cap - m + 1, m)  # rows 256.. need keys up to cap + 1
+    ctx.attn(prm, q, kc, vc, out, m_tokens=m, use_meta=True)
+    with pytest.raises(p2p_b200.KvFullError):
+        ctx.sync()
+    assert bool((out[256:] == 7.0).all())
+    ctx.meta_write(cap - m, m)
+    ctx.attn(prm, q, kc, vc, out, m_tokens=m, use_meta=True)
+    ctx.sync()
+    assert bool(torch.isfinite(out.float()).all())
