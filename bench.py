@@ -407,6 +407,28 @@ def run_prefill_scatter(ctx, rank, world, s, steps, warmup):
     return ms
 
 
+def run_prefill_multicast(ctx, rank, world, s, steps, warmup):
+    """The same head-sharded prefill with the flash epilogue storing each row once to the NVLink
+    multicast address of a symmetric-memory buffer (NVSwitch replicates it into every rank's
+    output), then one single-element all-reduce, inside the timed region."""
+    import torch
+    from p2p_b200.sharding import MulticastHeadShardedPrefill
+    sp = MulticastHeadShardedPrefill(ctx, HQ, HKV, world, rank, max_tokens=s)
+    g = torch.Generator(device="cuda").manual_seed(33)
+    qkv_full = (0.5 * torch.randn((s, (HQ + 2 * HKV) * D), generator=g, device="cuda")).half()
+    qkv_l = qkv_full[:, sp.local_qkv_columns().cuda()].contiguous()
+    del qkv_full
+    rope = ctx.rope_table(s, D, 1e6)
+    kc = torch.zeros((s, sp.kvn, D), device="cuda", dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    q_buf = torch.zeros((s, sp.qn * D), device="cuda", dtype=torch.float16)
+
+    def step(i):
+        sp(qkv_l, None, rope, kc, vc, q_buf, 0, s)
+
+    return timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
+
+
 def run_vision_split(ctx, rank, world, steps, warmup):
     """The vision batch split by image over the ranks (no collective)."""
     import torch
@@ -650,6 +672,17 @@ def main():
                                 f"{world} GPUs, flash epilogue writes every rank's [S][2048] "
                                 f"output over NVLink (no all-gather)",
                     "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
+                key = f"prefill_head_multicast_s{s_tok}"
+                try:
+                    ms = max_over_ranks(run_prefill_multicast(ctx, rank, world, s_tok, 10, 3),
+                                        world)
+                    side[key] = {
+                        "workload": f"causal prefill S={s_tok}, 32q/8kv split by kv-head group "
+                                    f"over {world} GPUs, flash epilogue stores every row once as "
+                                    f"NVLink multicast (NVSwitch writes every rank's output)",
+                        "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
+                except RuntimeError as e:  # same on every rank: no collective was entered
+                    side[key] = {"unavailable": str(e).splitlines()[0][:200]}
             ms = max_over_ranks(run_vision_split(ctx, rank, world, 10, 3), world)
             side["vision_image_split"] = {
                 "workload": f"vision B=16 S=1024 12 heads split by image over {world} GPUs",

@@ -142,6 +142,16 @@ p2p_status p2p_attn_scatter(p2p_ctx* ctx, const p2p_attn_params* prm, const void
                             int64_t ld_o, int32_t out_head0, const uint32_t* meta_dev,
                             int32_t pos0, int32_t m_tokens, void* stream);
 
+/* As p2p_attn_scatter, but the output rows go out once, as NVLink multicast stores
+ * (multimem.st) to mc_out, the multicast address of a buffer bound on every rank of the node
+ * (e.g. a symmetric-memory allocation with multicast support): NVSwitch writes each row into
+ * every rank's [M][ld_o] buffer, so a GPU sends its rows once instead of once per peer. */
+p2p_status p2p_attn_multicast(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q,
+                              int64_t ld_q, const void* k_cache, const void* v_cache,
+                              int64_t kv_cap_tokens, void* mc_out, int64_t ld_o,
+                              int32_t out_head0, const uint32_t* meta_dev, int32_t pos0,
+                              int32_t m_tokens, void* stream);
+
 /* Device buffers shared between the processes of one node (CUDA IPC): p2p_shared_alloc
  * allocates `bytes` on the context's device and returns an opaque handle that another
  * process passes to p2p_shared_open to map the same memory (its GPU then reads and writes it

@@ -99,6 +99,8 @@ PROTOTYPES = {
         _st, [_v, _pp, _v, _i64, _v, _v, _v, _v, _v, _v, _i32, _i32, _i32, _v, _i64, _v]),
     "p2p_attn_scatter": (
         _st, [_v, _pp, _v, _i64, _v, _v, _i64, C.POINTER(_v), _i32, _i64, _i32, _v, _i32, _i32, _v]),
+    "p2p_attn_multicast": (
+        _st, [_v, _pp, _v, _i64, _v, _v, _i64, _v, _i64, _i32, _v, _i32, _i32, _v]),
     "p2p_shared_alloc": (_st, [_v, C.c_size_t, C.POINTER(_v), C.c_char_p]),
     "p2p_shared_free": (_st, [_v, _v]),
     "p2p_shared_open": (_st, [_v, C.c_char_p, C.POINTER(_v)]),

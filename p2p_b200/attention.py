@@ -128,6 +128,18 @@ class Context:
             k_cache.shape[0], arr, len(outs), ld_o, out_head0,
             self.meta_ptr if use_meta else None, pos0, m, _stream(stream)))
 
+    def attn_multicast(self, prm: Params, q: torch.Tensor, k_cache: torch.Tensor,
+                       v_cache: torch.Tensor, mc_out: int, ld_o: int, out_head0: int, *,
+                       pos0: int = 0, m_tokens: Optional[int] = None, use_meta: bool = False,
+                       stream=None):
+        """p2p_attn_multicast: as attn_scatter, with the rows written once to the NVLink
+        multicast address mc_out (NVSwitch replicates them into every rank's buffer)."""
+        m = q.shape[0] if m_tokens is None else m_tokens
+        self._chk(lib.p2p_attn_multicast(
+            self.h, C.byref(prm.c()), _ptr(q), q.stride(0), _ptr(k_cache), _ptr(v_cache),
+            k_cache.shape[0], C.c_void_p(mc_out), ld_o, out_head0,
+            self.meta_ptr if use_meta else None, pos0, m, _stream(stream)))
+
     def shared_alloc(self, nbytes: int):
         """p2p_shared_alloc: (device address, IPC handle bytes) of a new node-shared buffer."""
         ptr = C.c_void_p()

@@ -250,8 +250,9 @@ p2p_status run_causal_flash(p2p_ctx* ctx, const p2p_attn_params* prm, const void
                             int64_t ld_q, const void* k_cache, const void* v_cache,
                             int64_t kv_cap_tokens, void* const* outs, int n_outs, int64_t ld_o,
                             int out_head0, const uint32_t* meta_dev, int32_t pos0,
-                            int32_t m_tokens, cudaStream_t s) {
+                            int32_t m_tokens, cudaStream_t s, void* mc_out = nullptr) {
   p2p::FlashArgs f{};
+  f.mc_out = mc_out;
   f.q = q;
   f.k = k_cache;
   f.v = v_cache;
@@ -660,6 +661,33 @@ p2p_status p2p_attn_scatter(p2p_ctx* ctx, const p2p_attn_params* prm, const void
   DeviceGuard g(ctx->device);
   return run_causal_flash(ctx, prm, q, ld_q, k_cache, v_cache, kv_cap_tokens, outs, n_outs, ld_o,
                           out_head0, meta_dev, pos0, m_tokens, pick_stream(ctx, stream));
+}
+
+p2p_status p2p_attn_multicast(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q,
+                              int64_t ld_q, const void* k_cache, const void* v_cache,
+                              int64_t kv_cap_tokens, void* mc_out, int64_t ld_o,
+                              int32_t out_head0, const uint32_t* meta_dev, int32_t pos0,
+                              int32_t m_tokens, void* stream) {
+  p2p_status st = check_params(ctx, prm, false);
+  if (st != P2P_OK) return st;
+  const int64_t qw = int64_t(prm->num_heads) * prm->head_dim;
+  if (!q || !k_cache || !v_cache || !mc_out || !aligned16(mc_out))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn_multicast: NULL or misaligned buffer");
+  if (m_tokens < 0 || ld_q < qw || out_head0 < 0 || ld_o < (int64_t(out_head0) * prm->head_dim + qw) ||
+      kv_cap_tokens <= 0 || (!meta_dev && pos0 < 0) || (ld_q % 8) || (ld_o % 8) || !aligned16(q))
+    return fail(ctx, P2P_ERR_INVALID_ARG,
+                "attn_multicast: M %d ld_q %lld ld_o %lld out_head0 %d cap %lld pos0 %d", m_tokens,
+                (long long)ld_q, (long long)ld_o, out_head0, (long long)kv_cap_tokens, pos0);
+  if (!meta_dev && int64_t(pos0) + m_tokens > kv_cap_tokens)
+    return fail(ctx, P2P_ERR_KV_FULL, "attn_multicast: pos0 %d + M %d > cache rows %lld", pos0,
+                m_tokens, (long long)kv_cap_tokens);
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "attn_multicast: cache buffers must be 16-byte aligned");
+  if (m_tokens == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  void* none = mc_out;  // outs[0] is unused when the multicast address is given
+  return run_causal_flash(ctx, prm, q, ld_q, k_cache, v_cache, kv_cap_tokens, &none, 1, ld_o,
+                          out_head0, meta_dev, pos0, m_tokens, pick_stream(ctx, stream), mc_out);
 }
 
 p2p_status p2p_shared_alloc(p2p_ctx* ctx, size_t bytes, void** ptr,

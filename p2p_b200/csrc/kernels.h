@@ -92,6 +92,7 @@ struct FlashArgs {
   void* extra_out[kMaxFlashOuts - 1];  // more buffers of out's layout that get the same rows
   int32_t n_extra_out;                 // (other GPUs' outputs, written over NVLink)
   int32_t out_head0;
+  void* mc_out;  // non-null: NVLink multicast address of every GPU's output (out unused)
   int64_t ld_q, ld_kv, ld_o;
   int64_t q_rows_total, kv_rows_total;  // rows of the q / kv 2-D views (tensor-map extents)
   int64_t batch_stride_q_rows, batch_stride_kv_rows;  // rows between images

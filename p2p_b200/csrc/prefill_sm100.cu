@@ -88,6 +88,7 @@ struct FlashParams {
   __half* out[kMaxFlashOuts];  // [0] this GPU's output; the others are peers' (NVLink stores)
   int32_t n_out;
   int32_t out_head0;           // head h is written at column (out_head0 + h) * 64
+  __half* mc_out;              // non-null: multicast address; one store reaches every GPU
   int64_t ld_o;
   int64_t bs_q, bs_kv;  // rows between images
   int64_t kv_rows_total;
@@ -419,12 +420,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int64_t off =
             (int64_t(b) * p.bs_q + q_first + r) * p.ld_o + int64_t(p.out_head0 + h) * D;
-        // this GPU's output first, then every peer's (head-sharded prefill: the rows reach
-        // the other GPUs over NVLink here, instead of through a separate all-gather)
-        for (int t = 0; t < p.n_out; ++t) {
-          uint4* dst = reinterpret_cast<uint4*>(p.out[t] + off);
+        if (p.mc_out) {
+          // head-sharded prefill with NVLink multicast: each store leaves this GPU once and
+          // NVSwitch writes it into every GPU's output buffer
+          uint4* dst = reinterpret_cast<uint4*>(p.mc_out + off);
 #pragma unroll
-          for (int i = 0; i < D / 8; ++i) dst[i] = row[i];
+          for (int i = 0; i < D / 8; ++i) multimem_st16(dst + i, row[i]);
+        } else {
+          // this GPU's output first, then every peer's (head-sharded prefill: the rows reach
+          // the other GPUs over NVLink here, instead of through a separate all-gather)
+          for (int t = 0; t < p.n_out; ++t) {
+            uint4* dst = reinterpret_cast<uint4*>(p.out[t] + off);
+#pragma unroll
+            for (int i = 0; i < D / 8; ++i) dst[i] = row[i];
+          }
         }
       }
     }
@@ -485,6 +494,7 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
   for (int t = 0; t < a.n_extra_out; ++t) p.out[1 + t] = static_cast<__half*>(a.extra_out[t]);
   p.n_out = 1 + a.n_extra_out;
   p.out_head0 = a.out_head0;
+  p.mc_out = static_cast<__half*>(a.mc_out);
   p.ld_o = a.ld_o;
   p.bs_q = a.batch_stride_q_rows;
   p.bs_kv = a.batch_stride_kv_rows;

@@ -238,6 +238,14 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
+// 16 bytes to an NVLink multicast address: NVSwitch writes them into the buffer of every GPU
+// bound to the multicast object.
+__device__ __forceinline__ void multimem_st16(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
 // acc + f32(low half) + f32(high half), without separate conversions (mixed-precision adds).
 __device__ __forceinline__ float add_f16x2_to_f32(uint32_t h2, float acc) {
   const unsigned short lo = static_cast<unsigned short>(h2 & 0xffffu);

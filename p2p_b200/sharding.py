@@ -7,7 +7,9 @@ Where the work shards naturally:
   * long-context prefill -- KV-head groups: rank g owns kv heads [g*Hkv/G, (g+1)*Hkv/G) and
     their query heads, computes out[:, heads_g] and its KV-cache slice; either one NCCL
     all-gather assembles the [S][Hq*D] output (HeadShardedPrefill), or the flash kernel writes
-    its rows straight into every rank's full output over NVLink (ScatterHeadShardedPrefill).
+    its rows straight into every rank's full output over NVLink, either once per peer
+    (ScatterHeadShardedPrefill) or once as NVLink multicast stores that NVSwitch replicates
+    (MulticastHeadShardedPrefill).
   * vision -- independent images.
   * single-sequence decode does not shard (8.4 MB per layer is less than the cost of a
     cross-GPU exchange): replicas only.
@@ -158,3 +160,41 @@ class ScatterHeadShardedPrefill(HeadShardedPrefill):
         if self.own:
             self.ctx.shared_free(self.own)
             self.own = None
+
+
+class MulticastHeadShardedPrefill(HeadShardedPrefill):
+    """HeadShardedPrefill whose flash epilogue stores every output row once, to the NVLink
+    multicast address of a symmetric-memory buffer bound on all ranks: NVSwitch writes it into
+    every rank's full [max_tokens][Hq*64] output, so a GPU sends its slice once instead of once
+    per peer (the scatter variant's cost grows with the number of GPUs).  One all-reduce of a
+    single element then orders the ranks.  Needs NVLink multicast (NVSwitch); raises if the
+    node has none.  The same buffer reuse rule as ScatterHeadShardedPrefill applies."""
+
+    def __init__(self, ctx, num_heads: int, num_kv_heads: int, world: int, rank: int,
+                 max_tokens: int, group=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        super().__init__(ctx, num_heads, num_kv_heads, world, rank, group)
+        self.max_tokens = max_tokens
+        self.ld_o = num_heads * 64
+        self.out_full = symm_mem.empty((max_tokens, self.ld_o), dtype=torch.float16,
+                                       device=f"cuda:{ctx.device}")
+        self.handle = symm_mem.rendezvous(self.out_full, group or dist.group.WORLD)
+        self.mc = int(self.handle.multicast_ptr)
+        if not self.mc:
+            raise RuntimeError("no NVLink multicast support for this group")
+        self.flag = torch.zeros(1, dtype=torch.float32, device=f"cuda:{ctx.device}")
+
+    def __call__(self, qkv_local, norm_w, rope, k_cache, v_cache, q_buf, pos0: int,
+                 m_tokens: int, stream=None):
+        import torch.distributed as dist
+        if m_tokens > self.max_tokens:
+            raise ValueError(f"{m_tokens} tokens > max_tokens {self.max_tokens}")
+        self.ctx.qk_prep(self.prm, qkv_local, norm_w, rope, q_buf, k_cache, v_cache, pos0=pos0,
+                         m_tokens=m_tokens, stream=stream)
+        self.ctx.attn_multicast(self.prm, q_buf, k_cache, v_cache, self.mc, self.ld_o, self.q0,
+                                pos0=pos0, m_tokens=m_tokens, stream=stream)
+        if self.world > 1:
+            dist.all_reduce(self.flag, group=self.group)  # every rank's rows have landed
+        return self.out_full[:m_tokens]

@@ -81,6 +81,22 @@ def _worker(rank, world, port, q):
             g3 = full.cpu().numpy().astype(np.float64)
             ok[f"scatter_{it}"] = bool((np.abs(g3 - want) <= 2e-3 + 1e-2 * np.abs(want.astype(np.float64))).all())
         ssp.close()
+        # the same with every row stored once to an NVLink multicast address (NVSwitch
+        # writes it into both ranks' outputs), where the node supports multicast
+        from p2p_b200.sharding import MulticastHeadShardedPrefill
+        try:
+            msp = MulticastHeadShardedPrefill(ctx, hq, hkv, world, rank, max_tokens=m)
+        except RuntimeError:
+            msp = None
+        if msp is not None:
+            for it in range(2):
+                kc.zero_()
+                vc.zero_()
+                full = msp(qkv_l, dev(nw), dev(rope), kc, vc, q_buf, 0, m)
+                torch.cuda.synchronize()
+                g4 = full.cpu().numpy().astype(np.float64)
+                ok[f"multicast_{it}"] = bool((np.abs(g4 - want) <= 2e-3 + 1e-2 * np.abs(want.astype(np.float64))).all())
+            del msp
         # ragged decode split by sequence
         past = np.array([100, 2000, 37, 700, 1500, 9], np.int32)
         mine = lpt_partition(list(past + 1), world)[rank]
