@@ -768,6 +768,13 @@ p2p_status p2p_decode_step(p2p_ctx* ctx, const p2p_attn_params* prm, int32_t n_l
   a.pos_host = pos;
   a.kv_cap = kv_cap_tokens;
   DeviceGuard g(ctx->device);
+  // qkv rows in page-locked host memory: let one CTA of each cluster read them (the others get
+  // the rotated q through distributed shared memory) instead of every split crossing the link
+  cudaPointerAttributes pa{};
+  if (cudaPointerGetAttributes(&pa, layers[0].qkv) == cudaSuccess)
+    a.q_bcast = pa.type == cudaMemoryTypeHost ? 1 : 0;
+  else
+    cudaGetLastError();
   const int64_t max_len = meta_dev ? kv_cap_tokens : int64_t(pos) + 1;
   return run_decode(ctx, prm, a, p2p::kLayers, true, n_layers, max_len,
                     pick_stream(ctx, stream));

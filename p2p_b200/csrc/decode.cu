@@ -100,7 +100,8 @@ __device__ __forceinline__ Seq<T> resolve(const DecodeArgs& a, int z) {
 template <class T, int GC, bool FUSED>
 __device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T>& sq, int kh, int hc,
                                          int head0, bool has_new, float qscale,
-                                         float (*q_s)[kHeadDim], float* knew_s, float* vnew_s) {
+                                         float (*q_s)[kHeadDim], float* knew_s, float* vnew_s,
+                                         bool do_q = true) {
   constexpr int D = kHeadDim;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (FUSED) {
@@ -108,8 +109,8 @@ __device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T>& sq, 
     const T* rope = static_cast<const T*>(a.rope) + int64_t(sq.past) * D;
     const float cs = to_f32(rope[lane]);
     const float sn = to_f32(rope[32 + lane]);
-    const int units = GC + (has_new ? 2 : 0);
-    for (int u = warp; u < units; u += kWarps) {
+    for (int u = warp; u < GC + 2; u += kWarps) {
+      if (u < GC ? !do_q : !has_new) continue;
       if (u < GC) {  // QK_PREP q unit (kernels.js:255-263), f16 rounding of the stored q
         const int64_t off = int64_t(head0 + u) * D;
         float r0, r1;
@@ -142,7 +143,7 @@ __device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T>& sq, 
         vnew_s[lane + 32] = to_f32(x1);
       }
     }
-  } else {
+  } else if (do_q) {
     for (int i = tid; i < GC * D; i += kThreads)
       q_s[i / D][i % D] = to_f32(sq.qrow[int64_t(head0) * D + i]) * qscale;
   }
@@ -276,7 +277,8 @@ __device__ __forceinline__ void finish_push(const DecodeArgs& a, T* out_h, int s
                                             const float (*red_m)[GC], const float (*red_l)[GC],
                                             const float (*red_acc)[GC][kHeadDim],
                                             float (*stage_s)[kPushStride],
-                                            float (*recv_s)[kPushStride], uint64_t* recv_bar) {
+                                            float (*recv_s)[kPushStride], uint64_t* recv_bar,
+                                            bool start_waited) {
   constexpr int D = kHeadDim;
   const int tid = threadIdx.x;
   const bool active = split < nsplit;
@@ -303,7 +305,7 @@ __device__ __forceinline__ void finish_push(const DecodeArgs& a, T* out_h, int s
     }
     __syncthreads();
   }
-  cluster_wait();  // every rank's receive mbarrier is initialised
+  if (!start_waited) cluster_wait();  // every rank's receive mbarrier is initialised
   if (!active) return;
   for (int i = tid; i < GC * kPushChunks; i += kThreads) {
     const int g = i / kPushChunks, c = i % kPushChunks;
@@ -427,11 +429,15 @@ __global__ void __launch_bounds__(kThreads, 3)
   __shared__ __align__(16) float stage_s[CL ? GC : 1][kPushStride];
   __shared__ __align__(16) float recv_s[CL ? kRecvSlots : 1][kPushStride];
   __shared__ __align__(8) uint64_t recv_bar;
+  __shared__ __align__(8) uint64_t q_bar;
   if constexpr (CL) {
-    if (tid == 0) recv_bar_init(&recv_bar);
-    cluster_arrive_relaxed();  // matched by cluster_wait() in finish_push
+    if (tid == 0) {
+      recv_bar_init(&recv_bar);
+      recv_bar_init(&q_bar);
+    }
+    cluster_arrive_relaxed();  // matched by one cluster_wait(): after the prologue or at finish
   }
-  __shared__ float q_s[GC][D];
+  __shared__ __align__(16) float q_s[GC][D];
   __shared__ float knew_s[D];
   __shared__ float vnew_s[D];
   __shared__ float red_m[kWarps][GC];
@@ -462,7 +468,37 @@ __global__ void __launch_bounds__(kThreads, 3)
 #pragma unroll
   for (int t = 0; t < kStages - 1; ++t) issue_tile(t);
 
-  prologue<T, GC, FUSED>(a, sq, kh, hc, head0, has_new, 1.0f, q_s, knew_s, vnew_s);
+  // Cluster form with the qkv rows in host memory: the query rows are the same for every split
+  // of a (layer, head chunk), so rank 0 alone reads them across the host link and rotates
+  // them, and pushes the result into every peer's q_s (st.async, completing on the peer's
+  // q_bar); the first K/V tiles are already in flight meanwhile.
+  const bool q_bcast = CL && a.q_bcast;
+  prologue<T, GC, FUSED>(a, sq, kh, hc, head0, has_new, 1.0f, q_s, knew_s, vnew_s,
+                         !q_bcast || split == 0);
+  if (q_bcast) {
+    cluster_wait();  // every rank's q_bar and recv_bar are initialised
+    constexpr int kQChunks = GC * D * 4 / 16;  // 16-byte pieces of q_s
+    if (split == 0) {
+      __syncthreads();  // q_s complete
+      for (int i = tid; i < (ngrid - 1) * kQChunks; i += kThreads) {
+        const uint32_t peer = uint32_t(1 + i / kQChunks);
+        const int c = i % kQChunks;
+        const uint4 v = reinterpret_cast<const uint4*>(&q_s[0][0])[c];
+        st_async16(map_rank(smem_addr(&q_s[0][0]) + 16u * c, peer), v,
+                   map_rank(smem_addr(&q_bar), peer));
+      }
+    } else {
+      if (tid == 0) recv_bar_expect(&q_bar, uint32_t(GC * D * 4));
+      if (!recv_bar_try_wait(&q_bar)) {
+        const uint64_t t0 = now_ns();
+        bool ok = true;
+        while (ok && !recv_bar_try_wait(&q_bar)) ok = now_ns() - t0 <= kWaitLimitNs;
+        // Rank 0 never delivered: report it and carry on with whatever q_s holds, so that
+        // this CTA still takes its part in the combine (no peer writes into a CTA that left).
+        if (!ok && tid == 0) atomicOr(a.err, kErrTimeout);
+      }
+    }
+  }
   __syncthreads();
 
   // Q^T as the B operand (k = dims, n = heads): lane holds head n = lane/4 (zero when
@@ -584,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   __syncthreads();
   if constexpr (CL) {
     finish_push<T, GC>(a, sq.orow + int64_t(head0) * D, split, nsplit, red_m, red_l, red_acc,
-                       stage_s, recv_s, &recv_bar);
+                       stage_s, recv_s, &recv_bar, q_bcast);
   } else {
     finish<T, GC>(a, sq.orow + int64_t(head0) * D, z * gridDim.y + blockIdx.y, split, nsplit,
                   ngrid, red_m, red_l, red_acc, &s_last);

@@ -65,6 +65,8 @@ struct DecodeArgs {
   float* partials;    // [nz][hkv][max_splits][G][66]
   int32_t* counters;  // [nz][hkv], zero between launches
   int32_t wait_deficit;  // test hook: extra bytes the cluster combine waits for (0 normally)
+  int32_t q_bcast;       // cluster form: rank 0 alone reads the qkv rows (host memory) and
+                         // hands the rotated q to its peers
 };
 
 enum DecodeMode { kLayers = 0, kRagged = 1 };
