@@ -685,8 +685,8 @@ p2p_status p2p_attn_multicast(p2p_ctx* ctx, const p2p_attn_params* prm, const vo
     return fail(ctx, P2P_ERR_INVALID_ARG, "attn_multicast: cache buffers must be 16-byte aligned");
   if (m_tokens == 0) return P2P_OK;
   DeviceGuard g(ctx->device);
-  void* none = mc_out;  // outs[0] is unused when the multicast address is given
-  return run_causal_flash(ctx, prm, q, ld_q, k_cache, v_cache, kv_cap_tokens, &none, 1, ld_o,
+  // the kernel stores through mc_out alone; it also fills the launcher's one output slot
+  return run_causal_flash(ctx, prm, q, ld_q, k_cache, v_cache, kv_cap_tokens, &mc_out, 1, ld_o,
                           out_head0, meta_dev, pos0, m_tokens, pick_stream(ctx, stream), mc_out);
 }
 
