@@ -12,7 +12,8 @@
 //   stay in registers.
 //   warp 8      TMA producer: the two Q tiles once, then K/V tiles of 128 keys (SWIZZLE_128B)
 //               into a 5-stage ring shared by both q tiles; mbarrier complete_tx; single-CTA loads.
-//   warp 9      allocates 512 TMEM columns; one lane issues tcgen05.mma (cta_group::1, f16):
+//   warp 9      allocates 512 TMEM columns and issues tcgen05.mma (cta_group::1, f16) from the
+//               converged warp, one elected lane per MMA group:
 //                 S_w(j)  = Q_w K_j^T -> TMEM S_w   (M128 N128 K64)
 //                 O_w    += P_w(j) V_j -> TMEM O_w  (M128 N64 K128, A = P from TMEM, V an
 //                                                  MN-major shared-memory operand)
@@ -218,11 +219,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
-    // One thread.  All shared-memory descriptors are built once; a k-step only adds to the
-    // 14-bit start-address field (16-byte units: +2 per 32-byte K16 step of a 128B-swizzled
-    // K-major tile, +128 per 16-row step of the MN-major V tile), which cannot carry out of
-    // the field because shared addresses stay below 228 KB.
-    if (lane == 0) {
+    // The whole warp runs this loop with warp-uniform descriptors; lane 0 alone polls the
+    // mbarriers and broadcasts the outcome, and one elected lane issues each MMA group and
+    // its commit.  (Issuing from a one-lane branch instead lets the softmax warps of the same
+    // SM sub-partition starve the issuer of issue slots, and the tensor pipe, which queues
+    // very few MMAs, idles.)  All shared-memory descriptors are built once; a k-step only
+    // adds to the 14-bit start-address field (16-byte units: +2 per 32-byte K16 step of a
+    // 128B-swizzled K-major tile, +128 per 16-row step of the MN-major V tile), which cannot
+    // carry out of the field because shared addresses stay below 228 KB.
+    {
       constexpr uint32_t idesc_s = idesc_f16_f32(BM, BN, 0, 0);
       constexpr uint32_t idesc_pv = idesc_f16_f32(BM, D, 0, 1);
       // consecutive tiles (Q0/Q1, ring stages) are 16 KB apart: 1024 address units
@@ -231,21 +236,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t kdesc0 = smem_desc_sw128(smem_u32(s.k[0]), 16, 1024);
       const uint64_t vdesc0 = smem_desc_sw128(smem_u32(s.v[0]), 0, 1024);
       auto issue_s = [&](int w, int st) {  // S_w = Q_w K_st^T
-        const uint64_t qd = qdesc0 + uint64_t(w) * 1024, kd = kdesc0 + uint64_t(st) * 1024;
+        if (elect_one()) {
+          const uint64_t qd = qdesc0 + uint64_t(w) * 1024, kd = kdesc0 + uint64_t(st) * 1024;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_f16_ss(tmem + col_s(w), qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0);
-        mma_commit(&s.s_full[w]);
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_f16_ss(tmem + col_s(w), qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0);
+          mma_commit(&s.s_full[w]);
+        }
+        __syncwarp();
       };
       auto issue_pv = [&](int w, int st, bool acc) {  // O_w += P_w V_st
-        const uint64_t vd = vdesc0 + uint64_t(st) * 1024;
+        if (elect_one()) {
+          const uint64_t vd = vdesc0 + uint64_t(st) * 1024;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P
-          mma_f16_ts(tmem + col_o(w), tmem + col_p(w) + kk * 8, vd + 128 * kk, idesc_pv,
-                     (acc || kk > 0) ? 1u : 0u);
-        mma_commit(&s.pv_done[w]);
+          for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns of P
+            mma_f16_ts(tmem + col_o(w), tmem + col_p(w) + kk * 8, vd + 128 * kk, idesc_pv,
+                       (acc || kk > 0) ? 1u : 0u);
+          mma_commit(&s.pv_done[w]);
+        }
+        __syncwarp();
       };
-      bool ok = wait_bar(s, &s.bar_q, 0, p.err) && wait_bar(s, &s.k_full[0], 0, p.err);
+      auto wait_warp = [&](uint64_t* bar, uint32_t parity) {
+        bool r = true;
+        if (lane == 0) r = wait_bar(s, bar, parity, p.err);
+        return __shfl_sync(0xffffffffu, r ? 1 : 0, 0) != 0;
+      };
+      bool ok = wait_warp(&s.bar_q, 0) && wait_warp(&s.k_full[0], 0);
       if (ok) {
         tc_fence_after();
         if (n_kv0 > 0) issue_s(0, 0);
@@ -256,37 +272,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         // next tile's scores, as soon as each warpgroup has read its S buffer
         if (j + 1 < n_max) {
           const int st1 = (j + 1) % kStages;
-          if (!wait_bar(s, &s.k_full[st1], ((j + 1) / kStages) & 1, p.err)) break;
+          if (!wait_warp(&s.k_full[st1], ((j + 1) / kStages) & 1)) break;
           if (j + 1 < n_kv0) {
-            if (!wait_bar(s, &s.s_free[0], j & 1, p.err)) break;
+            if (!wait_warp(&s.s_free[0], j & 1)) break;
             tc_fence_after();
             issue_s(0, st1);
           }
           if (j + 1 < n_kv1) {
-            if (!wait_bar(s, &s.s_free[1], j & 1, p.err)) break;
+            if (!wait_warp(&s.s_free[1], j & 1)) break;
             tc_fence_after();
             issue_s(1, st1);
           }
         }
-        if (!wait_bar(s, &s.v_full[st], (j / kStages) & 1, p.err)) break;
+        if (!wait_warp(&s.v_full[st], (j / kStages) & 1)) break;
         if (j == n_max - 1 && last_valid < BN) {
           // Rows past the last valid key may hold anything (the cache is not cleared); P is
           // 0 there, but 0 * NaN is NaN, so those V rows are zeroed before the P.V MMA.
           uint4* vrow = reinterpret_cast<uint4*>(s.v[st]);
-          for (int i = last_valid * 8; i < BN * 8; ++i) vrow[i] = make_uint4(0, 0, 0, 0);
+          for (int i = last_valid * 8 + lane; i < BN * 8; i += 32) vrow[i] = make_uint4(0, 0, 0, 0);
           fence_proxy_async_smem();
+          __syncwarp();
         }
         if (j < n_kv0) {
-          if (!wait_bar(s, &s.p_full[0], j & 1, p.err)) break;
+          if (!wait_warp(&s.p_full[0], j & 1)) break;
           tc_fence_after();
           issue_pv(0, st, j > 0);
         }
         if (j < n_kv1) {
-          if (!wait_bar(s, &s.p_full[1], j & 1, p.err)) break;
+          if (!wait_warp(&s.p_full[1], j & 1)) break;
           tc_fence_after();
           issue_pv(1, st, j > 0);
         }
-        mma_commit(&s.kv_empty[st]);
+        if (elect_one()) mma_commit(&s.kv_empty[st]);
+        __syncwarp();
       }
     }
   }

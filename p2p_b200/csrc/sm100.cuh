@@ -176,6 +176,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// One lane of the (converged) warp is elected: true there, false in the other 31.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(e));
+  return e != 0;
+}
 // Per-warpgroup register budget changes (all warps of the warpgroup execute them).  The sum
 // over warpgroups must stay within the registers the CTA was launched with.
 template <int N>
