@@ -34,6 +34,8 @@ struct p2p_ctx {
   cudaStream_t stream = nullptr;
   uint32_t* meta = nullptr;
   int32_t* dev_err = nullptr;  // kernels set bits here (kErrPosBeyondCache); read by p2p_sync
+  int32_t* host_err = nullptr;      // mapped page-locked word p2p_sync reads dev_err into
+  int32_t* host_err_dev = nullptr;  // the same word's device address
   float* partials = nullptr;
   size_t partials_bytes = 0;
   int32_t* counters = nullptr;
@@ -342,6 +344,18 @@ p2p_status p2p_ctx_create(int device, p2p_ctx** out) {
   }
   cudaMemset(e, 0, sizeof(int32_t));
   ctx->dev_err = static_cast<int32_t*>(e);
+  // p2p_sync has a one-thread kernel move the error word into this mapped page-locked word on
+  // the caller's stream; without it (allocation refused) p2p_sync falls back to a copy
+  void* h = nullptr;
+  void* hd = nullptr;
+  if (cudaHostAlloc(&h, sizeof(int32_t), cudaHostAllocMapped) == cudaSuccess &&
+      cudaHostGetDevicePointer(&hd, h, 0) == cudaSuccess) {
+    ctx->host_err = static_cast<int32_t*>(h);
+    ctx->host_err_dev = static_cast<int32_t*>(hd);
+  } else {
+    if (h) cudaFreeHost(h);
+    cudaGetLastError();
+  }
   *out = ctx;
   return P2P_OK;
 }
@@ -354,6 +368,7 @@ p2p_status p2p_ctx_destroy(p2p_ctx* ctx) {
   for (auto& kv : ctx->shared) dev_free(kv.first, kv.second);
   dev_free(ctx->meta, 16);
   dev_free(ctx->dev_err, sizeof(int32_t));
+  if (ctx->host_err) cudaFreeHost(ctx->host_err);
   dev_free(ctx->partials, ctx->partials_bytes);
   dev_free(ctx->counters, ctx->counters_bytes);
   cudaStreamDestroy(ctx->stream);
@@ -365,16 +380,38 @@ const char* p2p_last_error(const p2p_ctx* ctx) { return ctx ? ctx->err.c_str() :
 
 void* p2p_ctx_stream(p2p_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
 
+namespace {
+__global__ void take_error_word(int32_t* dev_err, int32_t* host_err) {
+  *static_cast<volatile int32_t*>(host_err) = atomicExch(dev_err, 0);
+}
+}  // namespace
+
 p2p_status p2p_sync(p2p_ctx* ctx, void* stream) {
   if (!ctx) return P2P_ERR_INVALID_ARG;
   DeviceGuard g(ctx->device);
-  cudaError_t e = cudaStreamSynchronize(pick_stream(ctx, stream));
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+  cudaStream_t s = pick_stream(ctx, stream);
   int32_t flags = 0;
-  e = cudaMemcpy(&flags, ctx->dev_err, sizeof flags, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "reading the device error word");
+  cudaError_t e;
+  if (ctx->host_err_dev) {
+    // behind the stream's work, one thread swaps the error word to 0 and stores what it held
+    // in mapped host memory: one stream synchronization, no device-wide one, no copy engine
+    take_error_word<<<1, 1, 0, s>>>(ctx->dev_err, ctx->host_err_dev);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "reading the device error word");
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+    flags = *static_cast<volatile int32_t*>(ctx->host_err);
+  } else {
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+    e = cudaMemcpy(&flags, ctx->dev_err, sizeof flags, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "reading the device error word");
+  }
   if (flags) {
-    cudaMemset(ctx->dev_err, 0, sizeof flags);
+    if (!ctx->host_err_dev) {
+      cudaMemsetAsync(ctx->dev_err, 0, sizeof flags, s);
+      cudaStreamSynchronize(s);
+    }
     if (flags & p2p::kErrPosBeyondCache)
       return fail(ctx, P2P_ERR_KV_FULL,
                   "a kernel was given a device-side position beyond its KV cache; that work "
