@@ -108,6 +108,7 @@ struct FlashArgs {
   float scale_log2;
   int32_t* err;          // device error word: bit 0 = position beyond the cache
   int32_t wait_deficit;  // test hook: extra bytes the Q-tile wait expects (0 normally)
+  int32_t num_sms;       // non-causal: > 0 lets the last partial wave run as one-tile CTAs
 };
 
 // Device error word bits.

@@ -102,6 +102,10 @@ struct FlashParams {
   int32_t n_qpairs;
   float scale_log2;
   int32_t wait_deficit;  // test hook (0 normally): the Q-tile wait then runs out
+  // Non-causal 1-D grid (lin != 0): CTA i < n_pair covers item i (a pair of q tiles); CTA
+  // n_pair + t covers one 128-row q tile (t & 1) of item n_pair + t / 2.  Items are numbered
+  // head-fastest, then q pair, then image.
+  int32_t lin, n_pair;
 };
 
 // Bounded wait on an mbarrier phase; false when the limit passed or another role gave up.
@@ -137,14 +141,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Grid (heads, q pairs, images), launched in linear order: every head's q pair before the
   // next q pair, and causal q pairs longest first (the last pair sees the most keys), so the
   // block scheduler hands out the work longest-processing-time first.
-  const int qp = p.causal ? (p.n_qpairs - 1 - int(blockIdx.y)) : int(blockIdx.y);
-  const int h = blockIdx.x, b = blockIdx.z;
+  int qp, h, b, q_row0;
+  bool single = false;
+  if (p.lin) {
+    const int bx = int(blockIdx.x);
+    single = bx >= p.n_pair;
+    const int item = single ? p.n_pair + ((bx - p.n_pair) >> 1) : bx;
+    h = item % p.hq;
+    qp = (item / p.hq) % p.n_qpairs;
+    b = item / (p.hq * p.n_qpairs);
+    q_row0 = qp * 2 * BM + (single ? ((bx - p.n_pair) & 1) * BM : 0);
+  } else {
+    qp = p.causal ? (p.n_qpairs - 1 - int(blockIdx.y)) : int(blockIdx.y);
+    h = blockIdx.x;
+    b = blockIdx.z;
+    q_row0 = qp * 2 * BM;
+  }
   const int kh = h / (p.hq / p.hkv);
   const int pos0 = p.causal ? (p.meta ? int(p.meta[0]) : p.pos0_host) : 0;
-  const int q_row0 = qp * 2 * BM;
   // valid q rows of the two tiles and the keys each needs (causal: 0 .. pos0 + last row)
   const int rows0 = min(BM, p.s_q - q_row0);
-  const int rows1 = max(0, min(BM, p.s_q - q_row0 - BM));
+  if (rows0 <= 0) return;  // single mode: the second tile of a pair whose q rows end earlier
+  const int rows1 = single ? 0 : max(0, min(BM, p.s_q - q_row0 - BM));
   const int64_t kend0 = p.causal ? int64_t(pos0) + q_row0 + rows0 : int64_t(p.s_kv);
   const int64_t kend1 =
       rows1 == 0 ? 0 : (p.causal ? int64_t(pos0) + q_row0 + BM + rows1 : int64_t(p.s_kv));
@@ -536,11 +554,27 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   });
   if (attr_err != cudaSuccess) return attr_err;
-  if (p.n_qpairs > 65535) return cudaErrorInvalidValue;
-  dim3 grid(a.hq, p.n_qpairs, a.batch);
   void* args[] = {&tq, &tk, &tv, &p};
-  return cudaLaunchKernel(reinterpret_cast<const void*>(&flash_fwd_kernel), grid,
-                          dim3(kThreads), args, smem, stream);
+  auto launch = [&](dim3 grid) {
+    return cudaLaunchKernel(reinterpret_cast<const void*>(&flash_fwd_kernel), grid,
+                            dim3(kThreads), args, smem, stream);
+  };
+  // Non-causal (all items equal): when the items do not fill the last wave of one CTA per SM,
+  // the last R pairs run as 2R one-tile CTAs at the end of the same grid (the block scheduler
+  // hands them out last, to the SMs that free up first).  A one-tile CTA has its softmax
+  // warpgroup alone on the XU pipe and finishes sooner than a pair, so the last wave shortens
+  // (this needs 2R <= SMs).
+  if (!a.causal && a.num_sms > 0) {
+    const int64_t n_items = int64_t(a.hq) * p.n_qpairs * a.batch;
+    const int64_t tail = n_items % a.num_sms;
+    if (tail > 0 && 2 * tail <= a.num_sms && n_items + tail <= INT32_MAX) {
+      p.lin = 1;
+      p.n_pair = int32_t(n_items - tail);
+      return launch(dim3(unsigned(n_items + tail)));
+    }
+  }
+  if (p.n_qpairs > 65535) return cudaErrorInvalidValue;
+  return launch(dim3(a.hq, p.n_qpairs, a.batch));
 }
 
 }  // namespace p2p
