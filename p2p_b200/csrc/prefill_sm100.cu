@@ -23,7 +23,7 @@
 //               per q row (= TMEM lane).  tcgen05.ld of the S row; mask only on tiles that
 //               cross the causal diagonal / the key end; row max with 3-input max; exp2 with
 //               the scale folded into one packed FFMA2 and evaluated two at a time, mostly by
-//               MUFU.EX2 on f16x2 and for 6 of every 16 pairs by a cubic on the FMA pipe (the
+//               MUFU.EX2 on f16x2 and for 5 of every 16 pairs by a cubic on the FMA pipe (the
 //               result is already the f16 P pair; the row sum adds the same rounded values);
 //               all of P(j) is computed before waiting for P(j-1).V to free the P buffer; P
 //               is stored into TMEM (tcgen05.st) and the P.V MMA takes its A operand from
@@ -64,7 +64,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (factor 256)
 #ifndef P2P_POLY_PAIRS
-#define P2P_POLY_PAIRS 6
+#define P2P_POLY_PAIRS 5
 #endif
 constexpr int kPolyPairs = P2P_POLY_PAIRS;  // of every 16 exp pairs, these use the cubic
 
