@@ -1,9 +1,18 @@
 // qk_prep.cu -- QK_PREP (src/scripts/lfm-engine/kernels.js:216-266) for sm_100a.
 //
-// One warp per (head unit, token): units [0,Hq) are q heads, [Hq,Hq+Hkv) k heads,
-// [Hq+Hkv,Hq+2Hkv) v heads, exactly the shader's unit numbering generalised from 16/8.
-// Lane l owns elements l and l+32 (the rotate-half partners), so RoPE needs no exchange and
-// the RMS sum is a 5-level butterfly that reproduces the shader's tree sum bit for bit.
+// Units [0,Hq) are q heads, [Hq,Hq+Hkv) k heads, [Hq+Hkv,Hq+2Hkv) v heads, exactly the shader's
+// unit numbering generalised from 16/8.  Two kernels:
+//  * qk_prep_rows_kernel (16-byte aligned buffers, the normal case): one THREAD per (q or k
+//    head, token) row.  It loads the row's 64 elements with 16-byte loads, sums the squares in
+//    the shader's tree order (pairs 32 apart, then 16, 8, 4, 2, 1: the same IEEE additions, so
+//    the result is bit-identical), and computes inverseSqrt, the f16-rounded norm and the
+//    rotate-half RoPE per element pair (i, i + 32), storing 16 bytes at a time.  The per-row
+//    scalar work (divide, square root, reciprocal) is paid once per row instead of once per
+//    row by a whole warp, which made the one-warp-per-row form instruction-bound (~130 warp
+//    instructions per row, 8 % of DRAM bandwidth).  v heads are copied by further threads.
+//  * qk_prep_kernel (any alignment): one warp per (head unit, token); lane l owns elements l
+//    and l+32 (the rotate-half partners), so RoPE needs no exchange and the RMS sum is a
+//    5-level butterfly that reproduces the shader's tree sum bit for bit.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -51,11 +60,185 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   dst[lane + 32] = from_f32<T>(r1);
 }
 
+
+// 64 elements of one row in registers; element e as f32.
+template <class T>
+struct Row64;
+template <>
+struct Row64<__half> {
+  uint32_t w[32];  // w[k] = elements 2k, 2k+1
+  __device__ __forceinline__ void load(const __half* p) {
+    const uint4* s = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 v = s[i];
+      w[4 * i] = v.x;
+      w[4 * i + 1] = v.y;
+      w[4 * i + 2] = v.z;
+      w[4 * i + 3] = v.w;
+    }
+  }
+  __device__ __forceinline__ float get(int e) const {
+    const __half2 h = *reinterpret_cast<const __half2*>(&w[e >> 1]);
+    return (e & 1) ? __high2float(h) : __low2float(h);
+  }
+};
+template <>
+struct Row64<float> {
+  float f[64];
+  __device__ __forceinline__ void load(const float* p) {
+    const float4* s = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 v = s[i];
+      f[4 * i] = v.x;
+      f[4 * i + 1] = v.y;
+      f[4 * i + 2] = v.z;
+      f[4 * i + 3] = v.w;
+    }
+  }
+  __device__ __forceinline__ float get(int e) const { return f[e]; }
+};
+
+// 8 consecutive elements stored with one 16-byte store (f16) or two (f32).
+__device__ __forceinline__ void store8(__half* p, const float (&x)[8]) {
+  uint4 v;
+  __half2 h;
+  h = __floats2half2_rn(x[0], x[1]); v.x = *reinterpret_cast<uint32_t*>(&h);
+  h = __floats2half2_rn(x[2], x[3]); v.y = *reinterpret_cast<uint32_t*>(&h);
+  h = __floats2half2_rn(x[4], x[5]); v.z = *reinterpret_cast<uint32_t*>(&h);
+  h = __floats2half2_rn(x[6], x[7]); v.w = *reinterpret_cast<uint32_t*>(&h);
+  *reinterpret_cast<uint4*>(p) = v;
+}
+__device__ __forceinline__ void store8(float* p, const float (&x)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
+}
+
+constexpr int kRowsPerBlock = 128;
+
+// Threads [0, M*(Hq+Hkv)) of the grid take the q and k rows (token-major, unit-minor, so a
+// warp reads consecutive 128-byte rows); threads beyond take the v rows, 16 bytes each.
+template <class T>
+__global__ void __launch_bounds__(kRowsPerBlock)
+    qk_prep_rows_kernel(const QkPrepArgs a) {
+  constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte access
+  __shared__ float nw_s[2 * kHeadDim];
+  const bool has_norm = a.norm_w != nullptr;
+  if (has_norm)
+    for (int i = threadIdx.x; i < 2 * kHeadDim; i += blockDim.x)
+      nw_s[i] = to_f32(static_cast<const T*>(a.norm_w)[i]);
+  __syncthreads();
+  const int64_t pos0 = int64_t(a.meta ? a.meta[0] : uint32_t(a.pos0));
+  const int qk_units = a.hq + a.hkv;
+  const int64_t n_qk = int64_t(a.m_tokens) * qk_units;
+  const int64_t kv_stride = int64_t(a.hkv) * kHeadDim;
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const T* qkv = static_cast<const T*>(a.qkv);
+  if (idx >= n_qk) {
+    // v heads (kernels.js:237-241): copied unchanged, one 16-byte piece per thread
+    constexpr int kPieces = kHeadDim / kVec;
+    const int64_t v = idx - n_qk;
+    if (v >= int64_t(a.m_tokens) * a.hkv * kPieces) return;
+    const int piece = int(v % kPieces);
+    const int kh = int((v / kPieces) % a.hkv);
+    const int m = int(v / (int64_t(kPieces) * a.hkv));
+    const int64_t pos = pos0 + m;
+    if (pos >= a.kv_cap) {  // the cache cannot hold this row: touch nothing, report it
+      atomicOr(a.err, kErrPosBeyondCache);
+      return;
+    }
+    const T* src = qkv + int64_t(m) * a.ld_qkv + int64_t(qk_units + kh) * kHeadDim + piece * kVec;
+    T* dst = static_cast<T*>(a.v_cache) + pos * kv_stride + kh * kHeadDim + piece * kVec;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    return;
+  }
+  const int unit = int(idx % qk_units);
+  const int m = int(idx / qk_units);
+  const int64_t pos = pos0 + m;
+  if (pos >= a.kv_cap) {
+    atomicOr(a.err, kErrPosBeyondCache);
+    return;
+  }
+  const bool isq = unit < a.hq;
+  Row64<T> x;
+  x.load(qkv + int64_t(m) * a.ld_qkv + int64_t(unit) * kHeadDim);
+  float inv = 1.0f;
+  if (has_norm) {
+    // the shader's tree: t[i] = v[i]^2 + v[i+32]^2, then pairs 16, 8, 4, 2, 1 apart
+    float t[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      t[i] = __fadd_rn(__fmul_rn(x.get(i), x.get(i)), __fmul_rn(x.get(i + 32), x.get(i + 32)));
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1)
+#pragma unroll
+      for (int i = 0; i < s; ++i) t[i] = __fadd_rn(t[i], t[i + s]);
+    inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(t[0], 64.0f), a.eps));
+  }
+  const float* w = nw_s + (isq ? 0 : kHeadDim);
+  const T* rope = static_cast<const T*>(a.rope) + pos * kHeadDim;
+  T* dst = isq ? static_cast<T*>(a.q_out) + int64_t(m) * a.ld_q + int64_t(unit) * kHeadDim
+               : static_cast<T*>(a.k_cache) + pos * kv_stride + int64_t(unit - a.hq) * kHeadDim;
+#pragma unroll
+  for (int c = 0; c < 32; c += 8) {  // element pairs (i, i + 32), i = c .. c + 7
+    float cs[8], sn[8], lo[8], hi[8];
+    // rope row: cos at [0, 32), sin at [32, 64)
+#pragma unroll
+    for (int k = 0; k < 8; k += kVec) {
+      if constexpr (sizeof(T) == 2) {
+        const uint4 vc = *reinterpret_cast<const uint4*>(rope + c + k);
+        const uint4 vs = *reinterpret_cast<const uint4*>(rope + 32 + c + k);
+        const uint32_t uc[4] = {vc.x, vc.y, vc.z, vc.w}, us[4] = {vs.x, vs.y, vs.z, vs.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const __half2 hc = *reinterpret_cast<const __half2*>(&uc[q]);
+          const __half2 hs = *reinterpret_cast<const __half2*>(&us[q]);
+          cs[k + 2 * q] = __low2float(hc);
+          cs[k + 2 * q + 1] = __high2float(hc);
+          sn[k + 2 * q] = __low2float(hs);
+          sn[k + 2 * q + 1] = __high2float(hs);
+        }
+      } else {
+        const float4 vc = *reinterpret_cast<const float4*>(rope + c + k);
+        const float4 vs = *reinterpret_cast<const float4*>(rope + 32 + c + k);
+        cs[k] = to_f32(vc.x); cs[k + 1] = to_f32(vc.y); cs[k + 2] = to_f32(vc.z); cs[k + 3] = to_f32(vc.w);
+        sn[k] = to_f32(vs.x); sn[k + 1] = to_f32(vs.y); sn[k + 2] = to_f32(vs.z); sn[k + 3] = to_f32(vs.w);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = c + k;
+      float n0 = x.get(i), n1 = x.get(i + 32);
+      if (has_norm) {
+        n0 = round_st<T>(__fmul_rn(__fmul_rn(n0, inv), w[i]));
+        n1 = round_st<T>(__fmul_rn(__fmul_rn(n1, inv), w[i + 32]));
+      }
+      lo[k] = __fsub_rn(__fmul_rn(n0, cs[k]), __fmul_rn(n1, sn[k]));
+      hi[k] = __fadd_rn(__fmul_rn(n1, cs[k]), __fmul_rn(n0, sn[k]));
+    }
+    store8(dst + c, lo);
+    store8(dst + 32 + c, hi);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_qk_prep(const QkPrepArgs& a, int dtype, cudaStream_t s) {
   if (a.m_tokens <= 0) return cudaSuccess;
   const int units = a.hq + 2 * a.hkv;
+  const size_t es = dtype == 0 ? 2 : 4;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (al16(a.qkv) && al16(a.q_out) && al16(a.k_cache) && al16(a.v_cache) && al16(a.rope) &&
+      (a.ld_qkv * es) % 16 == 0 && (a.ld_q * es) % 16 == 0) {
+    const int64_t threads = int64_t(a.m_tokens) * (a.hq + a.hkv) +
+                            int64_t(a.m_tokens) * a.hkv * int64_t(kHeadDim * es / 16);
+    const int64_t blocks = (threads + kRowsPerBlock - 1) / kRowsPerBlock;
+    if (blocks > INT32_MAX) return cudaErrorInvalidValue;
+    if (dtype == 0) qk_prep_rows_kernel<__half><<<unsigned(blocks), kRowsPerBlock, 0, s>>>(a);
+    else qk_prep_rows_kernel<float><<<unsigned(blocks), kRowsPerBlock, 0, s>>>(a);
+    return cudaGetLastError();
+  }
   dim3 grid(ceil_div(units, kWarpsPerBlock), a.m_tokens);
   if (dtype == 0) qk_prep_kernel<__half><<<grid, kWarpsPerBlock * 32, 0, s>>>(a);
   else qk_prep_kernel<float><<<grid, kWarpsPerBlock * 32, 0, s>>>(a);
