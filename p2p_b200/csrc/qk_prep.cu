@@ -3,7 +3,8 @@
 // Units [0,Hq) are q heads, [Hq,Hq+Hkv) k heads, [Hq+Hkv,Hq+2Hkv) v heads, exactly the shader's
 // unit numbering generalised from 16/8.  Two kernels:
 //  * qk_prep_rows_kernel (16-byte aligned buffers, the normal case): one THREAD per (q or k
-//    head, token) row.  It loads the row's 64 elements with 16-byte loads, sums the squares in
+//    head, token) row.  A warp stages its 32 rows through shared memory with row-contiguous
+//    16-byte loads; each thread then sums the squares of its row in
 //    the shader's tree order (pairs 32 apart, then 16, 8, 4, 2, 1: the same IEEE additions, so
 //    the result is bit-identical), and computes inverseSqrt, the f16-rounded norm and the
 //    rotate-half RoPE per element pair (i, i + 32), storing 16 bytes at a time.  The per-row
@@ -115,30 +116,37 @@ __device__ __forceinline__ void store8(float* p, const float (&x)[8]) {
   reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
 }
 
-constexpr int kRowsPerBlock = 128;
+constexpr int kRowsPerBlock = 128;  // 4 warps; one q/k row per thread
 
-// Threads [0, M*(Hq+Hkv)) of the grid take the q and k rows (token-major, unit-minor, so a
-// warp reads consecutive 128-byte rows); threads beyond take the v rows, 16 bytes each.
+// Threads [0, round_up(M*(Hq+Hkv), 32)) take the q and k rows, one per thread, token-major and
+// unit-minor; threads beyond take the v rows, 16 bytes each.  A warp's 32 rows are staged
+// through shared memory (row stride padded by 16 bytes, so the per-thread 16-byte reads and
+// writes are conflict-free): global loads and stores then cover whole 128-byte rows per 8
+// lanes instead of 32 different rows per instruction.
 template <class T>
 __global__ void __launch_bounds__(kRowsPerBlock)
     qk_prep_rows_kernel(const QkPrepArgs a) {
-  constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte access
+  constexpr int kVec = 16 / sizeof(T);             // elements per 16-byte access
+  constexpr int kPieces = kHeadDim / kVec;         // 16-byte pieces per row
+  constexpr int kStride = kHeadDim * sizeof(T) + 16;  // staged row stride in bytes
   __shared__ float nw_s[2 * kHeadDim];
+  __shared__ __align__(16) uint8_t stage[kRowsPerBlock / 32][32][kStride];
   const bool has_norm = a.norm_w != nullptr;
   if (has_norm)
     for (int i = threadIdx.x; i < 2 * kHeadDim; i += blockDim.x)
       nw_s[i] = to_f32(static_cast<const T*>(a.norm_w)[i]);
   __syncthreads();
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int64_t pos0 = int64_t(a.meta ? a.meta[0] : uint32_t(a.pos0));
   const int qk_units = a.hq + a.hkv;
   const int64_t n_qk = int64_t(a.m_tokens) * qk_units;
+  const int64_t n_qk_pad = (n_qk + 31) & ~int64_t(31);
   const int64_t kv_stride = int64_t(a.hkv) * kHeadDim;
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const T* qkv = static_cast<const T*>(a.qkv);
-  if (idx >= n_qk) {
+  if (idx >= n_qk_pad) {
     // v heads (kernels.js:237-241): copied unchanged, one 16-byte piece per thread
-    constexpr int kPieces = kHeadDim / kVec;
-    const int64_t v = idx - n_qk;
+    const int64_t v = idx - n_qk_pad;
     if (v >= int64_t(a.m_tokens) * a.hkv * kPieces) return;
     const int piece = int(v % kPieces);
     const int kh = int((v / kPieces) % a.hkv);
@@ -153,72 +161,100 @@ __global__ void __launch_bounds__(kRowsPerBlock)
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
     return;
   }
-  const int unit = int(idx % qk_units);
-  const int m = int(idx / qk_units);
+  // the whole warp is in the q/k range from here on (n_qk_pad is a multiple of 32); each lane
+  // decodes its own row once, and the staged copies take row r's values from lane r
+  const int64_t row0 = idx - lane;  // first row of this warp
+  const int64_t row = row0 + lane;
+  const int unit = int(row % qk_units);
+  const int m = int(row / qk_units);
   const int64_t pos = pos0 + m;
-  if (pos >= a.kv_cap) {
-    atomicOr(a.err, kErrPosBeyondCache);
-    return;
+  const bool mine = row < n_qk;
+  const bool ok = mine && pos < a.kv_cap;
+  if (mine && !ok) atomicOr(a.err, kErrPosBeyondCache);  // the cache cannot hold this row
+  // staged load: flat piece f = i * 32 + lane -> row f / kPieces, piece f % kPieces
+#pragma unroll
+  for (int i = 0; i < kPieces; ++i) {
+    const int f = i * 32 + lane, r = f / kPieces, pc = f % kPieces;
+    const int mr = __shfl_sync(0xffffffffu, m, r), ur = __shfl_sync(0xffffffffu, unit, r);
+    if (__shfl_sync(0xffffffffu, ok ? 1 : 0, r))
+      *reinterpret_cast<uint4*>(&stage[wib][r][pc * 16]) = *reinterpret_cast<const uint4*>(
+          qkv + int64_t(mr) * a.ld_qkv + int64_t(ur) * kHeadDim + pc * kVec);
   }
-  const bool isq = unit < a.hq;
-  Row64<T> x;
-  x.load(qkv + int64_t(m) * a.ld_qkv + int64_t(unit) * kHeadDim);
-  float inv = 1.0f;
-  if (has_norm) {
-    // the shader's tree: t[i] = v[i]^2 + v[i+32]^2, then pairs 16, 8, 4, 2, 1 apart
-    float t[32];
+  __syncwarp();
+  if (ok) {
+    const bool isq = unit < a.hq;
+    Row64<T> x;
+    x.load(reinterpret_cast<const T*>(&stage[wib][lane][0]));
+    float inv = 1.0f;
+    if (has_norm) {
+      // the shader's tree: t[i] = v[i]^2 + v[i+32]^2, then pairs 16, 8, 4, 2, 1 apart
+      float t[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      t[i] = __fadd_rn(__fmul_rn(x.get(i), x.get(i)), __fmul_rn(x.get(i + 32), x.get(i + 32)));
+      for (int i = 0; i < 32; ++i)
+        t[i] = __fadd_rn(__fmul_rn(x.get(i), x.get(i)), __fmul_rn(x.get(i + 32), x.get(i + 32)));
 #pragma unroll
-    for (int s = 16; s > 0; s >>= 1)
+      for (int s = 16; s > 0; s >>= 1)
 #pragma unroll
-      for (int i = 0; i < s; ++i) t[i] = __fadd_rn(t[i], t[i + s]);
-    inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(t[0], 64.0f), a.eps));
-  }
-  const float* w = nw_s + (isq ? 0 : kHeadDim);
-  const T* rope = static_cast<const T*>(a.rope) + pos * kHeadDim;
-  T* dst = isq ? static_cast<T*>(a.q_out) + int64_t(m) * a.ld_q + int64_t(unit) * kHeadDim
-               : static_cast<T*>(a.k_cache) + pos * kv_stride + int64_t(unit - a.hq) * kHeadDim;
+        for (int i = 0; i < s; ++i) t[i] = __fadd_rn(t[i], t[i + s]);
+      inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(t[0], 64.0f), a.eps));
+    }
+    const float* w = nw_s + (isq ? 0 : kHeadDim);
+    const T* rope = static_cast<const T*>(a.rope) + pos * kHeadDim;
+    T* out = reinterpret_cast<T*>(&stage[wib][lane][0]);  // results replace the staged row
 #pragma unroll
-  for (int c = 0; c < 32; c += 8) {  // element pairs (i, i + 32), i = c .. c + 7
-    float cs[8], sn[8], lo[8], hi[8];
-    // rope row: cos at [0, 32), sin at [32, 64)
+    for (int c = 0; c < 32; c += 8) {  // element pairs (i, i + 32), i = c .. c + 7
+      float cs[8], sn[8], lo[8], hi[8];
+      // rope row: cos at [0, 32), sin at [32, 64)
 #pragma unroll
-    for (int k = 0; k < 8; k += kVec) {
-      if constexpr (sizeof(T) == 2) {
-        const uint4 vc = *reinterpret_cast<const uint4*>(rope + c + k);
-        const uint4 vs = *reinterpret_cast<const uint4*>(rope + 32 + c + k);
-        const uint32_t uc[4] = {vc.x, vc.y, vc.z, vc.w}, us[4] = {vs.x, vs.y, vs.z, vs.w};
+      for (int k = 0; k < 8; k += kVec) {
+        if constexpr (sizeof(T) == 2) {
+          const uint4 vc = *reinterpret_cast<const uint4*>(rope + c + k);
+          const uint4 vs = *reinterpret_cast<const uint4*>(rope + 32 + c + k);
+          const uint32_t uc[4] = {vc.x, vc.y, vc.z, vc.w}, us[4] = {vs.x, vs.y, vs.z, vs.w};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const __half2 hc = *reinterpret_cast<const __half2*>(&uc[q]);
-          const __half2 hs = *reinterpret_cast<const __half2*>(&us[q]);
-          cs[k + 2 * q] = __low2float(hc);
-          cs[k + 2 * q + 1] = __high2float(hc);
-          sn[k + 2 * q] = __low2float(hs);
-          sn[k + 2 * q + 1] = __high2float(hs);
+          for (int q = 0; q < 4; ++q) {
+            const __half2 hc = *reinterpret_cast<const __half2*>(&uc[q]);
+            const __half2 hs = *reinterpret_cast<const __half2*>(&us[q]);
+            cs[k + 2 * q] = __low2float(hc);
+            cs[k + 2 * q + 1] = __high2float(hc);
+            sn[k + 2 * q] = __low2float(hs);
+            sn[k + 2 * q + 1] = __high2float(hs);
+          }
+        } else {
+          const float4 vc = *reinterpret_cast<const float4*>(rope + c + k);
+          const float4 vs = *reinterpret_cast<const float4*>(rope + 32 + c + k);
+          cs[k] = to_f32(vc.x); cs[k + 1] = to_f32(vc.y); cs[k + 2] = to_f32(vc.z); cs[k + 3] = to_f32(vc.w);
+          sn[k] = to_f32(vs.x); sn[k + 1] = to_f32(vs.y); sn[k + 2] = to_f32(vs.z); sn[k + 3] = to_f32(vs.w);
         }
-      } else {
-        const float4 vc = *reinterpret_cast<const float4*>(rope + c + k);
-        const float4 vs = *reinterpret_cast<const float4*>(rope + 32 + c + k);
-        cs[k] = to_f32(vc.x); cs[k + 1] = to_f32(vc.y); cs[k + 2] = to_f32(vc.z); cs[k + 3] = to_f32(vc.w);
-        sn[k] = to_f32(vs.x); sn[k + 1] = to_f32(vs.y); sn[k + 2] = to_f32(vs.z); sn[k + 3] = to_f32(vs.w);
       }
-    }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int i = c + k;
-      float n0 = x.get(i), n1 = x.get(i + 32);
-      if (has_norm) {
-        n0 = round_st<T>(__fmul_rn(__fmul_rn(n0, inv), w[i]));
-        n1 = round_st<T>(__fmul_rn(__fmul_rn(n1, inv), w[i + 32]));
+      for (int k = 0; k < 8; ++k) {
+        const int i = c + k;
+        float n0 = x.get(i), n1 = x.get(i + 32);
+        if (has_norm) {
+          n0 = round_st<T>(__fmul_rn(__fmul_rn(n0, inv), w[i]));
+          n1 = round_st<T>(__fmul_rn(__fmul_rn(n1, inv), w[i + 32]));
+        }
+        lo[k] = __fsub_rn(__fmul_rn(n0, cs[k]), __fmul_rn(n1, sn[k]));
+        hi[k] = __fadd_rn(__fmul_rn(n1, cs[k]), __fmul_rn(n0, sn[k]));
       }
-      lo[k] = __fsub_rn(__fmul_rn(n0, cs[k]), __fmul_rn(n1, sn[k]));
-      hi[k] = __fadd_rn(__fmul_rn(n1, cs[k]), __fmul_rn(n0, sn[k]));
+      store8(out + c, lo);
+      store8(out + 32 + c, hi);
     }
-    store8(dst + c, lo);
-    store8(dst + 32 + c, hi);
+  }
+  __syncwarp();
+  // staged store: q rows to q_out[m][unit], k rows to the cache row `pos`
+#pragma unroll
+  for (int i = 0; i < kPieces; ++i) {
+    const int f = i * 32 + lane, r = f / kPieces, pc = f % kPieces;
+    const int mr = __shfl_sync(0xffffffffu, m, r), ur = __shfl_sync(0xffffffffu, unit, r);
+    if (__shfl_sync(0xffffffffu, ok ? 1 : 0, r)) {
+      T* dst = ur < a.hq ? static_cast<T*>(a.q_out) + int64_t(mr) * a.ld_q + int64_t(ur) * kHeadDim
+                         : static_cast<T*>(a.k_cache) + (pos0 + mr) * kv_stride +
+                               int64_t(ur - a.hq) * kHeadDim;
+      *reinterpret_cast<uint4*>(dst + pc * kVec) =
+          *reinterpret_cast<const uint4*>(&stage[wib][r][pc * 16]);
+    }
   }
 }
 
@@ -231,7 +267,8 @@ cudaError_t launch_qk_prep(const QkPrepArgs& a, int dtype, cudaStream_t s) {
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (al16(a.qkv) && al16(a.q_out) && al16(a.k_cache) && al16(a.v_cache) && al16(a.rope) &&
       (a.ld_qkv * es) % 16 == 0 && (a.ld_q * es) % 16 == 0) {
-    const int64_t threads = int64_t(a.m_tokens) * (a.hq + a.hkv) +
+    const int64_t n_qk = int64_t(a.m_tokens) * (a.hq + a.hkv);
+    const int64_t threads = ((n_qk + 31) & ~int64_t(31)) +
                             int64_t(a.m_tokens) * a.hkv * int64_t(kHeadDim * es / 16);
     const int64_t blocks = (threads + kRowsPerBlock - 1) / kRowsPerBlock;
     if (blocks > INT32_MAX) return cudaErrorInvalidValue;
