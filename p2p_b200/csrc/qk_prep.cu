@@ -145,12 +145,14 @@ __global__ void __launch_bounds__(kRowsPerBlock)
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const T* qkv = static_cast<const T*>(a.qkv);
   if (idx >= n_qk_pad) {
-    // v heads (kernels.js:237-241): copied unchanged, one 16-byte piece per thread
-    const int64_t v = idx - n_qk_pad;
-    if (v >= int64_t(a.m_tokens) * a.hkv * kPieces) return;
+    // v heads (kernels.js:237-241): copied unchanged, one 16-byte piece per thread (32-bit
+    // index arithmetic: the host launches this kernel only for fewer than 2^31 threads)
+    const uint32_t v = uint32_t(idx - n_qk_pad);
+    if (v >= uint32_t(a.m_tokens) * uint32_t(a.hkv) * kPieces) return;
     const int piece = int(v % kPieces);
-    const int kh = int((v / kPieces) % a.hkv);
-    const int m = int(v / (int64_t(kPieces) * a.hkv));
+    const uint32_t vr = v / kPieces;
+    const int kh = int(vr % uint32_t(a.hkv));
+    const int m = int(vr / uint32_t(a.hkv));
     const int64_t pos = pos0 + m;
     if (pos >= a.kv_cap) {  // the cache cannot hold this row: touch nothing, report it
       atomicOr(a.err, kErrPosBeyondCache);
@@ -165,8 +167,8 @@ __global__ void __launch_bounds__(kRowsPerBlock)
   // decodes its own row once, and the staged copies take row r's values from lane r
   const int64_t row0 = idx - lane;  // first row of this warp
   const int64_t row = row0 + lane;
-  const int unit = int(row % qk_units);
-  const int m = int(row / qk_units);
+  const int unit = int(uint32_t(row) % uint32_t(qk_units));
+  const int m = int(uint32_t(row) / uint32_t(qk_units));
   const int64_t pos = pos0 + m;
   const bool mine = row < n_qk;
   const bool ok = mine && pos < a.kv_cap;
@@ -265,13 +267,13 @@ cudaError_t launch_qk_prep(const QkPrepArgs& a, int dtype, cudaStream_t s) {
   const int units = a.hq + 2 * a.hkv;
   const size_t es = dtype == 0 ? 2 : 4;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const int64_t n_qk = int64_t(a.m_tokens) * (a.hq + a.hkv);
+  const int64_t threads = ((n_qk + 31) & ~int64_t(31)) +
+                          int64_t(a.m_tokens) * a.hkv * int64_t(kHeadDim * es / 16);
   if (al16(a.qkv) && al16(a.q_out) && al16(a.k_cache) && al16(a.v_cache) && al16(a.rope) &&
-      (a.ld_qkv * es) % 16 == 0 && (a.ld_q * es) % 16 == 0) {
-    const int64_t n_qk = int64_t(a.m_tokens) * (a.hq + a.hkv);
-    const int64_t threads = ((n_qk + 31) & ~int64_t(31)) +
-                            int64_t(a.m_tokens) * a.hkv * int64_t(kHeadDim * es / 16);
+      (a.ld_qkv * es) % 16 == 0 && (a.ld_q * es) % 16 == 0 &&
+      threads + kRowsPerBlock <= INT32_MAX) {
     const int64_t blocks = (threads + kRowsPerBlock - 1) / kRowsPerBlock;
-    if (blocks > INT32_MAX) return cudaErrorInvalidValue;
     if (dtype == 0) qk_prep_rows_kernel<__half><<<unsigned(blocks), kRowsPerBlock, 0, s>>>(a);
     else qk_prep_rows_kernel<float><<<unsigned(blocks), kRowsPerBlock, 0, s>>>(a);
     return cudaGetLastError();
