@@ -79,6 +79,34 @@ def test_qk_prep_bit_exact(ctx, oracle, hq, hkv, pos0, m, norm):
     assert np.array_equal(bits(host(vc_g)), bits(vc_o))
 
 
+@pytest.mark.parametrize("norm", [True, False])
+def test_qk_prep_unaligned_rows_bit_exact(ctx, oracle, norm):
+    """Row strides that are not a multiple of 16 bytes (qkv and q rows one element longer than
+    their data) take the warp-per-row kernel instead of the thread-per-row one; same bits."""
+    import p2p_b200
+    hq, hkv, pos0, m = 32, 8, 21, 6
+    rng = np.random.default_rng(4242 + norm)
+    cap = pos0 + m
+    w_in, w_q = (hq + 2 * hkv) * D, hq * D
+    qkv = rng.standard_normal((m, w_in)).astype(np.float16)
+    nw = (1 + 0.1 * rng.standard_normal(2 * D)).astype(np.float16) if norm else None
+    rope_np = oracle.rope_table(cap)
+    kc = rng.standard_normal((cap, hkv, D)).astype(np.float16)
+    vc = rng.standard_normal((cap, hkv, D)).astype(np.float16)
+    q_o = np.zeros((m, w_q), np.float16)
+    kc_o, vc_o = kc.copy(), vc.copy()
+    oracle.qk_prep(hq, hkv, D, qkv, nw, rope_np, q_o, kc_o, vc_o, pos0, m)
+    qkv_pad = torch.zeros((m, w_in + 1), dtype=torch.float16, device="cuda")
+    qkv_pad[:, :w_in] = dev(qkv)
+    q_pad = torch.zeros((m, w_q + 1), dtype=torch.float16, device="cuda")
+    kc_g, vc_g = dev(kc), dev(vc)
+    ctx.qk_prep(p2p_b200.Params(hq, hkv), qkv_pad[:, :w_in], None if nw is None else dev(nw),
+                dev(rope_np), q_pad[:, :w_q], kc_g, vc_g, pos0=pos0, m_tokens=m)
+    assert np.array_equal(bits(host(q_pad[:, :w_q].contiguous())), bits(q_o))
+    assert np.array_equal(bits(host(kc_g)), bits(kc_o))
+    assert np.array_equal(bits(host(vc_g)), bits(vc_o))
+
+
 def test_library_rope_table_equals_oracle(ctx, oracle):
     import p2p_b200  # noqa: F401
     p = ctx.rope_table(40000, D, 1e6)
