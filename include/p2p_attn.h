@@ -10,6 +10,8 @@
  *   VISION_ATTN  src/scripts/lfm-engine/vision-kernels.js:176-258 -> p2p_attn_bidir
  *   ropeTable    src/scripts/lfm-engine/engine.js:60-71      -> p2p_rope_table
  *   meta buffer  src/scripts/lfm-engine/engine.js:144,388,422 -> p2p_meta / p2p_meta_write
+ *   ARGMAX       src/scripts/lfm-engine/kernels.js:362-399   -> p2p_argmax_step (the greedy
+ *                token and the device-side advance of the meta buffer's position and step)
  *   KV cache     src/scripts/lfm-engine/engine.js:152-165 (alloc), :274-304 (growth)
  *                                                            -> p2p_kv_*
  *
@@ -90,6 +92,17 @@ p2p_status p2p_rope_table(p2p_ctx* ctx, int32_t max_ctx, int32_t head_dim, doubl
 p2p_status p2p_meta(p2p_ctx* ctx, uint32_t** dev_meta);
 p2p_status p2p_meta_write(p2p_ctx* ctx, uint32_t pos0, uint32_t m_tokens, uint32_t step,
                           void* stream);
+
+/* kernels.js:362-399 (ARGMAX, dispatched at engine.js:239-240, 265-266 with the bindings
+ * logits, tok, mt, outTok): the greedy token over `vocab` f16 logits -- the smallest index
+ * among the maxima of the values above -3e38 (NaN never wins), else 0 -- is stored in tok[0]
+ * and out_tok[meta[2]], then meta[2] (step) and meta[0] (position) advance by one, all on the
+ * device, so the next decode step reads its position from the meta buffer without a host
+ * write.  meta_dev NULL uses the context's meta buffer.  When meta[2] >= out_tok_cap the
+ * token is not stored in out_tok and p2p_sync reports P2P_ERR_INVALID_ARG. */
+p2p_status p2p_argmax_step(p2p_ctx* ctx, const void* logits, int32_t vocab, uint32_t* tok,
+                           uint32_t* out_tok, int64_t out_tok_cap, uint32_t* meta_dev,
+                           void* stream);
 
 /* engine.js:152-165: one K and one V buffer [cap][Hkv][D] per attention layer. */
 p2p_status p2p_kv_create(p2p_ctx* ctx, int32_t n_layers, int32_t num_kv_heads,

@@ -364,4 +364,42 @@ int p2p_or_set_threads(int n) {
 #endif
 }
 
+
+// kernels.js:362-399 (ARGMAX), dispatched as one workgroup of 256 (engine.js:239-240, 265-266):
+// invocation t scans logits[t], logits[t+256], ... keeping the first strictly larger value
+// (seeded -3e38 and index 0); the workgroup tree over 128, 64, ..., 1 keeps the larger value,
+// ties to the smaller index; invocation 0 stores the token in tok[0] and outTok[mt[2]] and
+// advances mt[2] (step) and mt[0] (position) by one.
+void p2p_or_argmax_h(const uint16_t* logits, uint32_t v, uint32_t* tok, uint32_t* mt,
+                     uint32_t* out_tok) {
+  float bv[256];
+  uint32_t bi[256];
+  for (uint32_t t = 0; t < 256u; ++t) {
+    float best = -3.0e38f;
+    uint32_t bidx = 0u;
+    for (uint32_t i = t; i < v; i += 256u) {
+      const float x = p2p_or_f16_to_f32(logits[i]);
+      if (x > best) {
+        best = x;
+        bidx = i;
+      }
+    }
+    bv[t] = best;
+    bi[t] = bidx;
+  }
+  for (uint32_t s = 128u; s > 0u; s >>= 1u)
+    for (uint32_t t = 0; t < s; ++t) {
+      const float ov = bv[t + s];
+      const uint32_t oi = bi[t + s];
+      if (ov > bv[t] || (ov == bv[t] && oi < bi[t])) {
+        bv[t] = ov;
+        bi[t] = oi;
+      }
+    }
+  tok[0] = bi[0];
+  out_tok[mt[2]] = bi[0];
+  mt[2] = mt[2] + 1u;
+  mt[0] = mt[0] + 1u;
+}
+
 }  // extern "C"

@@ -11,6 +11,8 @@
  *   - QK_PREP            src/scripts/lfm-engine/kernels.js:216-266
  *   - ATTN               src/scripts/lfm-engine/kernels.js:268-319
  *   - VISION_ATTN        src/scripts/lfm-engine/vision-kernels.js:176-258
+ *   - ARGMAX             src/scripts/lfm-engine/kernels.js:362-399 (greedy token + the
+ *                        device-side advance of the meta buffer's position and step)
  * generalised from the reference's hard-coded 16 q heads / 8 kv heads / head_dim 64 /
  * row strides 2048, 1024, 768 to runtime (Hq, Hkv, D, strides).  For Hq=16, Hkv=8, D=64 it
  * performs the reference's operations in the reference's order.
@@ -90,6 +92,12 @@ void p2p_or_vision_attn_h(int nh, int d, float scale, int batch, int s_tokens,
 void p2p_or_attn_exact(int hq, int hkv, int d, double scale, const uint16_t* q, int64_t ld_q,
                        const uint16_t* kc, const uint16_t* vc, double* out, int64_t ld_o,
                        int pos0, int m_tokens);
+
+/* kernels.js:362-399: greedy argmax over v f16 logits (ties to the smaller index; values not
+ * above -3e38 and NaN never win, index 0 if none does), stored in tok[0] and out_tok[mt[2]],
+ * then mt[2] (step) and mt[0] (position) advance by one. */
+void p2p_or_argmax_h(const uint16_t* logits, uint32_t v, uint32_t* tok, uint32_t* mt,
+                     uint32_t* out_tok);
 
 /* OpenMP threads the parallel loops may use (0 = library default). Returns the count used. */
 int p2p_or_set_threads(int n);

@@ -59,6 +59,7 @@ def lib():
         L.p2p_or_attn_ragged_h.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _p, _i, _p, _i64]
         L.p2p_or_vision_attn_h.argtypes = [_i, _i, _f, _i, _i, _p, _p, _p, _p, _i64]
         L.p2p_or_attn_exact.argtypes = [_i, _i, _i, _d, _p, _i64, _p, _p, _p, _i64, _i, _i]
+        L.p2p_or_argmax_h.argtypes = [_p, C.c_uint32, _p, _p, _p]
         L.p2p_or_set_threads.restype = _i
         L.p2p_or_set_threads.argtypes = [_i]
         _LIB = L
@@ -77,7 +78,7 @@ def ref():
         if not path.exists():
             raise FileNotFoundError(f"{path} not built (needs the reference sources)")
         L = C.CDLL(str(path))
-        for name in ("QK_PREP", "ATTN", "VISION_ATTN"):
+        for name in ("QK_PREP", "ATTN", "VISION_ATTN", "ARGMAX"):
             fn = getattr(L, f"ref_{name}")
             fn.restype = _i
             fn.argtypes = [_p, _p, C.c_uint32, C.c_uint32, C.c_uint32]
@@ -144,6 +145,12 @@ def vision_attn(nh, d, q, k, v, out, scale=0.125):
     lib().p2p_or_vision_attn_h(nh, d, scale, b, s, _ptr(q), _ptr(k), _ptr(v), _ptr(out), ld)
 
 
+def argmax(logits, tok, meta, out_tok):
+    """kernels.js:362-399 in place on tok / meta / out_tok (uint32 arrays); logits float16."""
+    logits = np.ascontiguousarray(logits, dtype=np.float16)
+    lib().p2p_or_argmax_h(_ptr(logits), logits.size, _ptr(tok), _ptr(meta), _ptr(out_tok))
+
+
 def attn_exact(hq, hkv, d, q, kc, vc, pos0, m_tokens, scale=0.125):
     out = np.empty((m_tokens, hq * d), np.float64)
     lib().p2p_or_attn_exact(hq, hkv, d, scale, _ptr(q), q.shape[-1], _ptr(kc), _ptr(vc),
@@ -182,6 +189,15 @@ def ref_vision_attn(q, k, v, out, s_tokens=1024, num_heads=12, scale=0.125):
     rc = ref().ref_VISION_ATTN(b, ov, num_heads, s_tokens, 1)
     if rc != 0:
         raise RuntimeError("VISION_ATTN: non-uniform barrier")
+
+
+def ref_argmax(logits, tok, meta, out_tok):
+    """ARGMAX dispatched as engine.js:265-266 does: one workgroup, V = len(logits)."""
+    b = _bind(logits, tok, meta, out_tok)
+    ov = (C.c_double * 1)(float(logits.size))
+    rc = ref().ref_ARGMAX(b, ov, 1, 1, 1)
+    if rc != 0:
+        raise RuntimeError("ARGMAX: non-uniform barrier")
 
 
 def threads_env() -> int:

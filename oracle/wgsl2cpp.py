@@ -1,4 +1,5 @@
-"""Translate the reference's attention WGSL shaders into C++ for host execution.
+"""Translate the reference's attention WGSL shaders (and ARGMAX, which advances the meta
+buffer) into C++ for host execution.
 
 TEST INFRASTRUCTURE ONLY.  The reference keeps its GPU code as WGSL template strings inside
 JavaScript modules (src/scripts/lfm-engine/kernels.js, vision-kernels.js) and runs them
@@ -25,6 +26,7 @@ SHADERS = [
     ("src/scripts/lfm-engine/kernels.js", "QK_PREP"),
     ("src/scripts/lfm-engine/kernels.js", "ATTN"),
     ("src/scripts/lfm-engine/vision-kernels.js", "VISION_ATTN"),
+    ("src/scripts/lfm-engine/kernels.js", "ARGMAX"),
 ]
 
 TYPES = {"f32": "float", "f16": "wgsl::h16", "u32": "uint32_t", "i32": "int32_t"}

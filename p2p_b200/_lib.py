@@ -83,6 +83,7 @@ PROTOTYPES = {
     "p2p_rope_table": (_st, [_v, _i32, _i32, C.c_double, _i32, C.POINTER(_v)]),
     "p2p_meta": (_st, [_v, C.POINTER(_v)]),
     "p2p_meta_write": (_st, [_v, _u32, _u32, _u32, _v]),
+    "p2p_argmax_step": (_st, [_v, _v, _i32, _v, _v, _i64, _v, _v]),
     "p2p_kv_create": (_st, [_v, _i32, _i32, _i32, _i64, _i32, C.POINTER(_v)]),
     "p2p_kv_destroy": (_st, [_v]),
     "p2p_kv_ensure_capacity": (_st, [_v, _i64, _i64, _i64, _v]),

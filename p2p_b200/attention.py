@@ -99,6 +99,15 @@ class Context:
     def meta_write(self, pos0: int, m_tokens: int, step: int = 0, stream=None):
         self._chk(lib.p2p_meta_write(self.h, pos0, m_tokens, step, _stream(stream)))
 
+    def argmax_step(self, logits: torch.Tensor, tok: torch.Tensor, out_tok: torch.Tensor,
+                    meta: Optional[torch.Tensor] = None, stream=None):
+        """kernels.js:362-399 (ARGMAX): greedy token of `logits` (f16, vocab elements) into
+        tok[0] and out_tok[step]; then step and position advance in the meta buffer (the
+        context's own unless `meta`, a uint32[4] device tensor, is given), on the device."""
+        self._chk(lib.p2p_argmax_step(self.h, _ptr(logits), logits.numel(), _ptr(tok),
+                                      _ptr(out_tok), out_tok.numel(),
+                                      _ptr(meta) if meta is not None else None, _stream(stream)))
+
     def sync(self, stream=None):
         self._chk(lib.p2p_sync(self.h, _stream(stream)))
 

@@ -419,6 +419,10 @@ p2p_status p2p_sync(p2p_ctx* ctx, void* stream) {
     if (flags & p2p::kErrTimeout)
       return fail(ctx, P2P_ERR_TIMEOUT,
                   "a kernel's bounded wait on another CTA ran out; its output was not written");
+    if (flags & p2p::kErrOutTokFull)
+      return fail(ctx, P2P_ERR_INVALID_ARG,
+                  "argmax_step: the step index in the meta buffer reached out_tok's capacity; "
+                  "that token was not stored (tok and the meta buffer were still updated)");
   }
   return P2P_OK;
 }
@@ -502,6 +506,21 @@ p2p_status p2p_meta_write(p2p_ctx* ctx, uint32_t pos0, uint32_t m_tokens, uint32
   cudaError_t e =
       cudaMemcpyAsync(ctx->meta, v, sizeof v, cudaMemcpyHostToDevice, pick_stream(ctx, stream));
   if (e != cudaSuccess) return cuda_fail(ctx, e, "meta write");
+  return P2P_OK;
+}
+
+p2p_status p2p_argmax_step(p2p_ctx* ctx, const void* logits, int32_t vocab, uint32_t* tok,
+                           uint32_t* out_tok, int64_t out_tok_cap, uint32_t* meta_dev,
+                           void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  if (!logits || !tok || !out_tok || vocab <= 0 || out_tok_cap <= 0)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "argmax_step: NULL buffer, vocab %d or out_tok_cap %lld",
+                vocab, (long long)out_tok_cap);
+  DeviceGuard g(ctx->device);
+  cudaError_t e = p2p::launch_argmax_step(logits, vocab, tok, out_tok, out_tok_cap,
+                                          meta_dev ? meta_dev : ctx->meta, ctx->dev_err,
+                                          pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "argmax launch");
   return P2P_OK;
 }
 

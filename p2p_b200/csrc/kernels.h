@@ -25,6 +25,9 @@ struct QkPrepArgs {
   int32_t* err;          // device error word: bit 0 = position beyond the cache
 };
 cudaError_t launch_qk_prep(const QkPrepArgs& a, int dtype, cudaStream_t s);
+cudaError_t launch_argmax_step(const void* logits, int32_t vocab, uint32_t* tok,
+                               uint32_t* out_tok, int64_t out_cap, uint32_t* meta, int32_t* err,
+                               cudaStream_t s);
 
 // ---- decode.cu ------------------------------------------------------------------------------
 constexpr int kMaxLayers = 16;
@@ -114,6 +117,7 @@ struct FlashArgs {
 // Device error word bits.
 constexpr int kErrPosBeyondCache = 1;
 constexpr int kErrTimeout = 2;  // a bounded device-side wait ran out; that work was not written
+constexpr int kErrOutTokFull = 4;  // argmax_step: the step index reached out_tok's capacity
 cudaError_t launch_flash(const FlashArgs& a, cudaStream_t s);
 
 }  // namespace p2p

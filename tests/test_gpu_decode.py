@@ -107,6 +107,52 @@ def test_qk_prep_unaligned_rows_bit_exact(ctx, oracle, norm):
     assert np.array_equal(bits(host(vc_g)), bits(vc_o))
 
 
+@pytest.mark.parametrize("vocab,offset", [(65536, 0), (1001, 0), (65536, 1)])
+def test_argmax_step_two_calls_match_oracle(ctx, oracle, vocab, offset):
+    """p2p_argmax_step (kernels.js:362-399) twice in a row on the context's meta buffer: same
+    tokens as the oracle (ties and NaNs included), out_tok filled at steps 7 and 8, position
+    and step advanced on the device.  offset 1 makes the logits unaligned (element path)."""
+    from p2p_b200.attention import _from_device_ptr
+    rng = np.random.default_rng(vocab + offset)
+    meta_o = np.array([300, 1, 7, 0], np.uint32)
+    out_o = np.zeros(16, np.uint32)
+    tok_o = np.zeros(1, np.uint32)
+    ctx.meta_write(300, 1, 7)
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out_tok = torch.zeros(16, dtype=torch.int32, device="cuda")
+    for call in range(2):
+        lg = rng.standard_normal(vocab).astype(np.float16)
+        lg[rng.integers(0, vocab, 3)] = lg.max()  # ties at the maximum
+        lg[rng.integers(0, vocab, 3)] = np.nan
+        buf = torch.zeros(vocab + offset, dtype=torch.float16, device="cuda")
+        buf[offset:] = dev(lg)
+        ctx.argmax_step(buf[offset:], tok, out_tok)
+        ctx.sync()
+        oracle.argmax(lg, tok_o, meta_o, out_o)
+        assert int(host(tok)[0]) == int(tok_o[0])
+    meta = _from_device_ptr(ctx.meta_ptr.value if hasattr(ctx.meta_ptr, "value") else ctx.meta_ptr,
+                            16, 0).view(torch.int32)
+    assert host(meta).astype(np.uint32).tolist() == meta_o.tolist() == [302, 1, 9, 0]
+    assert np.array_equal(host(out_tok).astype(np.uint32), out_o)
+
+
+def test_argmax_step_full_token_buffer_is_reported(ctx):
+    """The step index at out_tok's capacity: the token is not stored there, tok and the meta
+    buffer still advance, and p2p_sync reports P2P_ERR_INVALID_ARG."""
+    import p2p_b200
+    ctx.meta_write(10, 1, 4)
+    lg = torch.zeros(64, dtype=torch.float16, device="cuda")
+    lg[9] = 1.0
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out_tok = torch.full((4,), -1, dtype=torch.int32, device="cuda")
+    ctx.argmax_step(lg, tok, out_tok)
+    with pytest.raises(p2p_b200.P2PError) as e:
+        ctx.sync()
+    assert e.value.status == p2p_b200.P2P_ERR_INVALID_ARG
+    assert int(host(tok)[0]) == 9 and host(out_tok).tolist() == [-1, -1, -1, -1]
+    ctx.sync()  # the error bit was cleared by the previous sync
+
+
 def test_library_rope_table_equals_oracle(ctx, oracle):
     import p2p_b200  # noqa: F401
     p = ctx.rope_table(40000, D, 1e6)

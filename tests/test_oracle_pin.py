@@ -93,6 +93,59 @@ def test_restatement_matches_reference_vision_shader(oracle, s_tokens, seed):
     assert np.array_equal(_bits(oa), _bits(ob))
 
 
+def _argmax_cases():
+    """Logits for ARGMAX: random, ties at the maximum, all -inf, NaNs mixed in; vocab sizes
+    65536 (the model's), one that is not a multiple of 8, and 1."""
+    rng = np.random.default_rng(31)
+    out = []
+    for v in (65536, 1001, 1):
+        lg = rng.standard_normal(v).astype(np.float16)
+        out.append(lg)
+        t = lg.copy()
+        t[rng.integers(0, v, 5)] = t.max()
+        out.append(t)
+        out.append(np.full(v, -np.inf, np.float16))
+        t = lg.copy()
+        t[::7] = np.nan
+        out.append(t)
+    return out
+
+
+def argmax_rule(lg):
+    """The shaders' result in closed form: the smallest index among the maxima of the values
+    above -3e38 (NaN never wins), else 0."""
+    x = lg.astype(np.float32)
+    ok = ~np.isnan(x) & (x > -3e38)
+    if not ok.any():
+        return 0
+    return int(np.flatnonzero(ok & (x == x[ok].max()))[0])
+
+
+def test_argmax_restatement_rule(oracle):
+    """kernels.js:362-399 restated: token, out_tok[step] and the advance of step and position."""
+    for lg in _argmax_cases():
+        tok = np.zeros(1, np.uint32)
+        meta = np.array([100, 1, 3, 0], np.uint32)
+        out_tok = np.zeros(8, np.uint32)
+        oracle.argmax(lg, tok, meta, out_tok)
+        assert tok[0] == argmax_rule(lg) and out_tok[3] == tok[0]
+        assert list(meta) == [101, 1, 4, 0]
+
+
+@ref_only
+def test_argmax_restatement_matches_reference_shader(oracle):
+    for lg in _argmax_cases():
+        res = []
+        for fn in (oracle.ref_argmax, oracle.argmax):
+            tok = np.zeros(4, np.uint32)
+            meta = np.array([4096, 1, 5, 0], np.uint32)
+            out_tok = np.zeros(16, np.uint32)
+            fn(lg, tok, meta, out_tok)
+            res.append((tok.copy(), meta.copy(), out_tok.copy()))
+        for a, b in zip(*res):
+            assert np.array_equal(a, b)
+
+
 def _load_decoder(golden_dir, name):
     z = np.load(golden_dir / f"{name}.npz")
     pos0, m = int(z["meta"][0]), int(z["meta"][1])
