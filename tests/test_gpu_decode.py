@@ -136,6 +136,62 @@ def test_argmax_step_two_calls_match_oracle(ctx, oracle, vocab, offset):
     assert np.array_equal(host(out_tok).astype(np.uint32), out_o)
 
 
+def test_decode_loop_in_one_cuda_graph_advances_positions_on_device(ctx, oracle):
+    """Three decode steps, each followed by p2p_argmax_step, captured in one CUDA graph and
+    replayed once: every decode step reads its position from the meta buffer that the previous
+    argmax advanced on the device (no host write between steps, as in the reference's
+    multi-step decode), so the steps land at positions past, past+1, past+2."""
+    import p2p_b200
+    from p2p_b200.attention import _from_device_ptr
+    hq, hkv, cap, past, n_steps, vocab = 32, 8, 600, 400, 3, 1024
+    rope = oracle.rope_table(cap)
+    prm = p2p_b200.Params(hq, hkv)
+    rng = np.random.default_rng(2718)
+    qkv, nw, kc, vc = make_layer(rng, hq, hkv, past, cap)
+    steps = [rng.standard_normal((1, (hq + 2 * hkv) * D)).astype(np.float16)
+             for _ in range(n_steps)]
+    logits = [rng.standard_normal(vocab).astype(np.float16) for _ in range(n_steps)]
+    rope_g, nw_g = dev(rope), dev(nw)
+    kc_g, vc_g = dev(kc), dev(vc)
+    q_rows = [dev(x[0]) for x in steps]
+    outs = [torch.zeros((hq * D,), dtype=torch.float16, device="cuda") for _ in range(n_steps)]
+    lg = [dev(x) for x in logits]
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out_tok = torch.zeros(8, dtype=torch.int32, device="cuda")
+    # first launches of each kernel outside the capture, on scratch buffers
+    ctx.meta_write(past, 1, 0)
+    scratch = (dev(steps[0][0]), nw_g, dev(kc), dev(vc), torch.zeros_like(outs[0]))
+    ctx.decode_step(prm, [scratch], rope_g, cap, use_meta=True)
+    ctx.argmax_step(lg[0], tok, out_tok)
+    ctx.sync()
+    ctx.meta_write(past, 1, 0)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for s in range(n_steps):
+            ctx.decode_step(prm, [(q_rows[s], nw_g, kc_g, vc_g, outs[s])], rope_g, cap,
+                            use_meta=True)
+            ctx.argmax_step(lg[s], tok, out_tok)
+    g.replay()
+    torch.cuda.synchronize()
+    ctx.sync()
+    kc_o, vc_o = kc.copy(), vc.copy()
+    tok_o = np.zeros(1, np.uint32)
+    meta_o = np.array([past, 1, 0, 0], np.uint32)
+    out_o = np.zeros(8, np.uint32)
+    for s in range(n_steps):
+        _, kc_o, vc_o, want = oracle_decode(oracle, hq, hkv, steps[s], nw, rope, kc_o, vc_o,
+                                            past + s)
+        assert_close(host(outs[s])[None], want, what=f"graph step {s} at position {past + s}")
+        oracle.argmax(logits[s], tok_o, meta_o, out_o)
+    assert np.array_equal(bits(host(kc_g)), bits(kc_o))
+    assert np.array_equal(bits(host(vc_g)), bits(vc_o))
+    assert np.array_equal(host(out_tok).astype(np.uint32), out_o)
+    meta = _from_device_ptr(ctx.meta_ptr.value, 16, 0).view(torch.int32)
+    assert host(meta).astype(np.uint32).tolist() == meta_o.tolist() == [past + 3, 1, 3, 0]
+    del g
+
+
 def test_argmax_step_full_token_buffer_is_reported(ctx):
     """The step index at out_tok's capacity: the token is not stored there, tok and the meta
     buffer still advance, and p2p_sync reports P2P_ERR_INVALID_ARG."""
