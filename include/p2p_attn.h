@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define P2P_ATTN_ABI_VERSION 1
+#define P2P_ATTN_ABI_VERSION 2
 
 typedef enum p2p_status {
   P2P_OK = 0,
@@ -178,7 +178,7 @@ p2p_status p2p_shared_open(p2p_ctx* ctx, const unsigned char handle[P2P_IPC_HAND
                            void** ptr);
 p2p_status p2p_shared_close(p2p_ctx* ctx, void* ptr);
 
-/* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to/* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to
+/* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to
  * P2P_MAX_LAYERS attention layers in ONE launch: for each layer the new token's qkv row is
  * normed/rotated, its k/v are appended at row pos, and its Hq output rows are written.
  * Layers are independent (each layer's q comes from its own qkv row).  The qkv and out rows
@@ -200,17 +200,21 @@ p2p_status p2p_decode_step(p2p_ctx* ctx, const p2p_attn_params* prm, int32_t n_l
                            void* stream);
 
 /* Batched decode over nseq independent sequences sharing one cache buffer pair
- * [rows][Hkv][D]: sequence i owns rows offsets[i] .. offsets[i]+past[i] and its new token
+ * [kv_rows][Hkv][D]: sequence i owns rows offsets[i] .. offsets[i]+past[i] and its new token
  * goes to row offsets[i]+past[i].  With fused_prep != 0, qkv rows [nseq][ld_qkv] are
  * normed/rotated and the new k/v appended (as p2p_decode_step); with fused_prep == 0, qkv
  * holds already-rotated q rows [nseq][ld_qkv] and the new k/v must already be in the cache.
- * offsets and past are device int32 arrays; max_past bounds past[i] for grid sizing only
- * (a longer sequence is still handled correctly, with longer splits). */
+ * offsets and past are device int32 arrays.  max_past is the largest past[i] allowed: it sizes
+ * the grid, and the rope table must hold at least max_past + 1 rows.  The kernel checks every
+ * sequence before touching it: one with a negative entry, past[i] > max_past or
+ * offsets[i] + past[i] >= kv_rows is skipped (its output rows are not written) and the next
+ * p2p_sync returns P2P_ERR_KV_FULL; the other sequences are computed normally. */
 p2p_status p2p_attn_decode_ragged(p2p_ctx* ctx, const p2p_attn_params* prm, const void* qkv,
                                   int64_t ld_qkv, const void* norm_w, const void* rope,
-                                  void* k_cache, void* v_cache, const int32_t* offsets,
-                                  const int32_t* past, int32_t nseq, int32_t max_past,
-                                  int32_t fused_prep, void* out, int64_t ld_o, void* stream);
+                                  void* k_cache, void* v_cache, int64_t kv_rows,
+                                  const int32_t* offsets, const int32_t* past, int32_t nseq,
+                                  int32_t max_past, int32_t fused_prep, void* out, int64_t ld_o,
+                                  void* stream);
 
 /* vision-kernels.js:176-258 (VISION_ATTN, dispatched (NUM_HEADS, S) at vision.js:271-276),
  * batched: out[b] = softmax(scale * q[b] k[b]^T) v[b] per head, no mask, tcgen05 kernel.
@@ -226,16 +230,19 @@ p2p_status p2p_attn_bidir(p2p_ctx* ctx, const p2p_attn_params* prm, const void* 
  * scratch lives in a fixed array of P2P_NOALLOC_SCRATCH_BYTES inside the library, which every
  * GPU that loads the library holds until the process exits.  A request whose scratch
  * (nseq x kv heads x splits x up to 4 heads x 66 floats, plus counters) exceeds it returns
- * P2P_ERR_INVALID_ARG with the sizes in p2p_last_error().  The first call on a device looks
- * up the array's device address (and may load the library's device code), so make that call
- * before capturing anything into a CUDA graph.  All calls share the array: calls that overlap
- * on the GPU (other streams, other contexts on the same device) race and must be ordered by
- * the caller. */
+ * P2P_ERR_INVALID_ARG with the sizes in p2p_last_error().  p2p_ctx_create looks up the
+ * array's device address on its device (loading the module that holds it, which is when the
+ * array takes its place in device memory), so the array is in place before the host reserves
+ * its pool if the context is created first; the calls themselves then allocate nothing.
+ * Sequences are checked as for p2p_attn_decode_ragged (kv_rows, max_past).  All calls share
+ * the array: calls that overlap on the GPU (other streams, other contexts on the same device)
+ * race and must be ordered by the caller. */
 #define P2P_NOALLOC_SCRATCH_BYTES (32u << 20)
 p2p_status p2p_attn_decode_ragged_noalloc(p2p_ctx* ctx, const p2p_attn_params* prm,
                                           const void* qkv, int64_t ld_qkv, const void* norm_w,
                                           const void* rope, void* k_cache, void* v_cache,
-                                          const int32_t* offsets, const int32_t* past,
+                                          int64_t kv_rows, const int32_t* offsets,
+                                          const int32_t* past,
                                           int32_t nseq, int32_t max_past, int32_t fused_prep,
                                           void* out, int64_t ld_o, void* stream);
 

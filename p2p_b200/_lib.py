@@ -94,10 +94,10 @@ PROTOTYPES = {
     "p2p_attn": (_st, [_v, _pp, _v, _i64, _v, _v, _i64, _v, _i64, _v, _i32, _i32, _v]),
     "p2p_decode_step": (_st, [_v, _pp, _i32, C.POINTER(DecodeLayer), _v, _i64, _v, _i32, _v]),
     "p2p_attn_decode_ragged": (
-        _st, [_v, _pp, _v, _i64, _v, _v, _v, _v, _v, _v, _i32, _i32, _i32, _v, _i64, _v]),
+        _st, [_v, _pp, _v, _i64, _v, _v, _v, _v, _i64, _v, _v, _i32, _i32, _i32, _v, _i64, _v]),
     "p2p_attn_bidir": (_st, [_v, _pp, _v, _v, _v, _v, _i64, _i32, _i32, _v]),
     "p2p_attn_decode_ragged_noalloc": (
-        _st, [_v, _pp, _v, _i64, _v, _v, _v, _v, _v, _v, _i32, _i32, _i32, _v, _i64, _v]),
+        _st, [_v, _pp, _v, _i64, _v, _v, _v, _v, _i64, _v, _v, _i32, _i32, _i32, _v, _i64, _v]),
     "p2p_attn_scatter": (
         _st, [_v, _pp, _v, _i64, _v, _v, _i64, C.POINTER(_v), _i32, _i64, _i32, _v, _i32, _i32, _v]),
     "p2p_attn_multicast": (

@@ -197,26 +197,32 @@ class Context:
     def attn_decode_ragged(self, prm: Params, qkv: torch.Tensor, norm_w, rope,
                            k_cache: torch.Tensor, v_cache: torch.Tensor, offsets: torch.Tensor,
                            past: torch.Tensor, out: torch.Tensor, *, max_past: int,
-                           fused_prep: bool = True, stream=None):
+                           fused_prep: bool = True, kv_rows: Optional[int] = None, stream=None):
+        """Sequence i owns cache rows offsets[i] .. offsets[i] + past[i]; kv_rows (default: the
+        cache tensor's first dimension) bounds them.  A sequence outside the cache, or with
+        past[i] > max_past, is skipped on the device and the next sync() raises KvFullError."""
         assert offsets.dtype == torch.int32 and past.dtype == torch.int32
+        rows = k_cache.shape[0] if kv_rows is None else kv_rows
         self._chk(lib.p2p_attn_decode_ragged(
             self.h, C.byref(prm.c()), _ptr(qkv), qkv.stride(0), _ptr(norm_w),
             rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(k_cache), _ptr(v_cache),
-            _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep), _ptr(out),
-            out.stride(0), _stream(stream)))
+            rows, _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep),
+            _ptr(out), out.stride(0), _stream(stream)))
 
     def attn_decode_ragged_noalloc(self, prm: Params, qkv: torch.Tensor, norm_w, rope,
                                    k_cache: torch.Tensor, v_cache: torch.Tensor,
                                    offsets: torch.Tensor, past: torch.Tensor, out: torch.Tensor,
-                                   *, max_past: int, fused_prep: bool = True, stream=None):
+                                   *, max_past: int, fused_prep: bool = True,
+                                   kv_rows: Optional[int] = None, stream=None):
         """attn_decode_ragged without any device allocation: the split scratch is the
         library's fixed array of P2P_NOALLOC_SCRATCH_BYTES (see include/p2p_attn.h)."""
         assert offsets.dtype == torch.int32 and past.dtype == torch.int32
+        rows = k_cache.shape[0] if kv_rows is None else kv_rows
         self._chk(lib.p2p_attn_decode_ragged_noalloc(
             self.h, C.byref(prm.c()), _ptr(qkv), qkv.stride(0), _ptr(norm_w),
             rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(k_cache), _ptr(v_cache),
-            _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep), _ptr(out),
-            out.stride(0), _stream(stream)))
+            rows, _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep),
+            _ptr(out), out.stride(0), _stream(stream)))
 
     def attn_bidir(self, prm: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    out: torch.Tensor, stream=None):

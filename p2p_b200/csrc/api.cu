@@ -26,6 +26,7 @@
 #pragma GCC visibility push(default)
 #include "../../include/p2p_attn.h"
 #pragma GCC visibility pop
+#include "host_internal.h"
 #include "kernels.h"
 
 struct p2p_ctx {
@@ -355,6 +356,14 @@ p2p_status p2p_ctx_create(int device, p2p_ctx** out) {
   } else {
     if (h) cudaFreeHost(h);
     cudaGetLastError();
+  }
+  // Place the no-alloc entry point's fixed scratch array on this device now, at start-up,
+  // rather than at that entry point's first call (after which a host may have given the rest
+  // of the device's memory to its own pool).
+  if (p2p::noalloc_prepare(device) != cudaSuccess) {
+    cudaGetLastError();
+    p2p_ctx_destroy(ctx);
+    return P2P_ERR_CUDA;
   }
   *out = ctx;
   return P2P_OK;
@@ -838,32 +847,17 @@ p2p_status p2p_decode_step(p2p_ctx* ctx, const p2p_attn_params* prm, int32_t n_l
 
 p2p_status p2p_attn_decode_ragged(p2p_ctx* ctx, const p2p_attn_params* prm, const void* qkv,
                                   int64_t ld_qkv, const void* norm_w, const void* rope,
-                                  void* k_cache, void* v_cache, const int32_t* offsets,
-                                  const int32_t* past, int32_t nseq, int32_t max_past,
-                                  int32_t fused_prep, void* out, int64_t ld_o, void* stream) {
-  p2p_status st = check_params(ctx, prm, true);
-  if (st != P2P_OK) return st;
-  const int64_t qw = int64_t(prm->num_heads) * prm->head_dim;
-  const int64_t row = qw + 2 * int64_t(prm->num_kv_heads) * prm->head_dim;
-  if (!qkv || !k_cache || !v_cache || !offsets || !past || !out || (fused_prep && !rope))
-    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_ragged: NULL buffer");
-  if (nseq < 0 || nseq > 65535 || max_past < 0 || ld_o < qw || ld_qkv < (fused_prep ? row : qw))
-    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_ragged: nseq %d max_past %d ld_qkv %lld ld_o %lld",
-                nseq, max_past, (long long)ld_qkv, (long long)ld_o);
-  if (!aligned16(k_cache) || !aligned16(v_cache))
-    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_ragged: cache buffers must be 16-byte aligned");
-  if (nseq == 0) return P2P_OK;
+                                  void* k_cache, void* v_cache, int64_t kv_rows,
+                                  const int32_t* offsets, const int32_t* past, int32_t nseq,
+                                  int32_t max_past, int32_t fused_prep, void* out, int64_t ld_o,
+                                  void* stream) {
+  p2p_status st = p2p::check_ragged(ctx, prm, qkv, ld_qkv, rope, k_cache, v_cache, kv_rows,
+                                    offsets, past, nseq, max_past, fused_prep, out, ld_o,
+                                    "decode_ragged");
+  if (st != P2P_OK || nseq == 0) return st;
   p2p::DecodeArgs a{};
-  a.qkv = qkv;
-  a.ld_qkv = ld_qkv;
-  a.norm_w = norm_w;
-  a.k_cache = k_cache;
-  a.v_cache = v_cache;
-  a.offsets = offsets;
-  a.past = past;
-  a.out = out;
-  a.ld_o = ld_o;
-  a.rope = rope;
+  p2p::fill_ragged(a, qkv, ld_qkv, norm_w, rope, k_cache, v_cache, kv_rows, offsets, past,
+                   max_past, out, ld_o);
   DeviceGuard g(ctx->device);
   return run_decode(ctx, prm, a, p2p::kRagged, fused_prep != 0, nseq, int64_t(max_past) + 1,
                     pick_stream(ctx, stream));
@@ -923,4 +917,53 @@ float eff_scale_log2(const p2p_attn_params* prm) {
   return eff_scale(prm) * 1.4426950408889634f;
 }
 float eff_eps_of(const p2p_attn_params* prm) { return eff_eps(prm); }
+int forced_decode_splits() { return forced_splits(); }
+int32_t* ctx_dev_err(const p2p_ctx* ctx) { return ctx->dev_err; }
+int32_t debug_wait_deficit() { return g_wait_deficit.load(); }
+
+p2p_status check_ragged(p2p_ctx* ctx, const p2p_attn_params* prm, const void* qkv,
+                        int64_t ld_qkv, const void* rope, const void* k_cache,
+                        const void* v_cache, int64_t kv_rows, const int32_t* offsets,
+                        const int32_t* past, int32_t nseq, int32_t max_past, int32_t fused_prep,
+                        const void* out, int64_t ld_o, const char* who) {
+  p2p_status st = check_params(ctx, prm, true);
+  if (st != P2P_OK) return st;
+  const int64_t qw = int64_t(prm->num_heads) * prm->head_dim;
+  const int64_t row = qw + 2 * int64_t(prm->num_kv_heads) * prm->head_dim;
+  if (!qkv || !k_cache || !v_cache || !offsets || !past || !out || (fused_prep && !rope))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "%s: NULL buffer", who);
+  if (nseq < 0 || nseq > 65535 || max_past < 0 || kv_rows <= 0 || ld_o < qw ||
+      ld_qkv < (fused_prep ? row : qw))
+    return fail(ctx, P2P_ERR_INVALID_ARG,
+                "%s: nseq %d max_past %d kv_rows %lld ld_qkv %lld ld_o %lld", who, nseq,
+                max_past, (long long)kv_rows, (long long)ld_qkv, (long long)ld_o);
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "%s: cache buffers must be 16-byte aligned", who);
+  if (fused_prep) {
+    // a rope table this context built knows its rows: it must cover positions 0..max_past
+    for (const auto& kv : ctx->rope)
+      if (kv.second == rope && std::get<0>(kv.first) <= max_past)
+        return fail(ctx, P2P_ERR_INVALID_ARG, "%s: rope table of %d rows, max_past %d", who,
+                    std::get<0>(kv.first), max_past);
+  }
+  return P2P_OK;
+}
+
+void fill_ragged(DecodeArgs& a, const void* qkv, int64_t ld_qkv, const void* norm_w,
+                 const void* rope, void* k_cache, void* v_cache, int64_t kv_rows,
+                 const int32_t* offsets, const int32_t* past, int32_t max_past, void* out,
+                 int64_t ld_o) {
+  a.qkv = qkv;
+  a.ld_qkv = ld_qkv;
+  a.norm_w = norm_w;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.kv_cap = kv_rows;
+  a.offsets = offsets;
+  a.past = past;
+  a.max_past = max_past;
+  a.out = out;
+  a.ld_o = ld_o;
+  a.rope = rope;
+}
 }  // namespace p2p

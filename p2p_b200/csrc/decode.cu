@@ -94,6 +94,25 @@ __device__ __forceinline__ Seq<T> resolve(const DecodeArgs& a, int z) {
   return q;
 }
 
+// Whether sequence z must be refused before any of its rows is touched: a decode-step
+// position at or beyond the cache (kLayers), or a ragged entry that is negative, longer than
+// max_past (the rope table's bound) or reaching past the cache's kv_cap rows (kRagged).  One
+// CTA per sequence records the refusal in the device error word, which p2p_sync reports.
+template <int MODE>
+__device__ __forceinline__ bool refused(const DecodeArgs& a, int z) {
+  bool bad;
+  if (MODE == kLayers) {
+    const int pos = a.meta ? int(a.meta[0]) : a.pos_host;
+    bad = pos < 0 || int64_t(pos) >= a.kv_cap;
+  } else {
+    const int off = a.offsets[z], past = a.past[z];
+    bad = off < 0 || past < 0 || past > a.max_past || int64_t(off) + past >= a.kv_cap;
+  }
+  if (bad && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
+    atomicOr(a.err, kErrPosBeyondCache);
+  return bad;
+}
+
 // Rotated query heads head0..head0+GC-1 into q_s (times `qscale`), and for the split that
 // holds the new token its normed/rotated k and raw v (QK_PREP's k and v units) into
 // knew_s/vnew_s and, by head chunk 0, into cache row `past`.  Unfused: q is read as given.
@@ -410,11 +429,8 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int kh = blockIdx.y / NHC, hc = blockIdx.y % NHC;
   const int head0 = kh * G + hc * GC;
   const int ngrid = gridDim.x;
+  if (refused<MODE>(a, z)) return;  // rows beyond the cache: touch nothing
   const Seq<T> sq = resolve<T, MODE>(a, z);
-  if (MODE == kLayers && int64_t(sq.past) >= a.kv_cap) {  // refuse rows beyond the cache
-    if (tid == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
-    return;
-  }
   const int len = sq.past + 1;  // keys 0..past, key `past` is the new token
   const int split_len = max(a.min_split, (ceil_div(len, ngrid) + 15) & ~15);
   const int nsplit = ceil_div(len, split_len);
@@ -704,11 +720,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int kh = blockIdx.y / NHC, hc = blockIdx.y % NHC;
   const int head0 = kh * G + hc * GC;
   const int ngrid = gridDim.x;
+  if (refused<MODE>(a, z)) return;
   const Seq<T> sq = resolve<T, MODE>(a, z);
-  if (MODE == kLayers && int64_t(sq.past) >= a.kv_cap) {
-    if (tid == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
-    return;
-  }
   const int len = sq.past + 1;
   const int split_len = max(a.min_split, (ceil_div(len, ngrid) + 15) & ~15);
   const int nsplit = ceil_div(len, split_len);

@@ -53,13 +53,15 @@ struct DecodeArgs {
   void* v_cache;
   const int32_t* offsets;
   const int32_t* past;
+  int32_t max_past;      // a sequence with past > max_past is refused (the rope table's bound)
   void* out;
   int64_t ld_o;
   // common
   const void* rope;
   const uint32_t* meta;  // nullable -> pos_host
   int32_t pos_host;
-  int64_t kv_cap;        // kLayers: rows per cache buffer; a position >= kv_cap is refused
+  int64_t kv_cap;        // rows per cache buffer: kLayers refuses a position >= kv_cap, kRagged
+                         // a sequence with a negative entry or offsets[z] + past[z] >= kv_cap
   int32_t* err;          // device error word: bit 0 = position beyond the cache
   int32_t hq, hkv;
   float scale_log2;  // scale * log2(e)

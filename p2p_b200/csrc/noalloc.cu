@@ -36,8 +36,8 @@ std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of g_decode_scratch on `dev`, looked up once per device with that device
-// current.  The first call on a device may load the library's device code (which is when the
-// array is placed in that GPU's memory).
+// current.  The first lookup on a device loads the module that holds the array, which is when
+// the array is placed in that GPU's memory; p2p_ctx_create makes that lookup.
 cudaError_t scratch_address(int dev, void** out) {
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lk(g_mu);
@@ -60,29 +60,33 @@ cudaError_t scratch_address(int dev, void** out) {
 
 }  // namespace
 
+namespace p2p {
+cudaError_t noalloc_prepare(int device) {
+  void* p = nullptr;
+  return scratch_address(device, &p);
+}
+}  // namespace p2p
+
 extern "C" p2p_status p2p_attn_decode_ragged_noalloc(
     p2p_ctx* ctx, const p2p_attn_params* prm, const void* qkv, int64_t ld_qkv,
-    const void* norm_w, const void* rope, void* k_cache, void* v_cache, const int32_t* offsets,
-    const int32_t* past, int32_t nseq, int32_t max_past, int32_t fused_prep, void* out,
-    int64_t ld_o, void* stream) {
-  p2p_status st = p2p::ctx_check_params(ctx, prm);
-  if (st != P2P_OK) return st;
-  const int64_t qw = int64_t(prm->num_heads) * prm->head_dim;
-  const int64_t row = qw + 2 * int64_t(prm->num_kv_heads) * prm->head_dim;
-  if (!qkv || !k_cache || !v_cache || !offsets || !past || !out || (fused_prep && !rope))
-    return p2p::ctx_fail(ctx, P2P_ERR_INVALID_ARG, "decode_ragged_noalloc: NULL buffer");
-  if (nseq < 0 || nseq > 65535 || max_past < 0 || ld_o < qw || ld_qkv < (fused_prep ? row : qw))
-    return p2p::ctx_fail(ctx, P2P_ERR_INVALID_ARG, "decode_ragged_noalloc: bad sizes");
-  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u)
-    return p2p::ctx_fail(ctx, P2P_ERR_INVALID_ARG,
-                         "decode_ragged_noalloc: cache buffers must be 16-byte aligned");
-  if (nseq == 0) return P2P_OK;
+    const void* norm_w, const void* rope, void* k_cache, void* v_cache, int64_t kv_rows,
+    const int32_t* offsets, const int32_t* past, int32_t nseq, int32_t max_past,
+    int32_t fused_prep, void* out, int64_t ld_o, void* stream) {
+  p2p_status st = p2p::check_ragged(ctx, prm, qkv, ld_qkv, rope, k_cache, v_cache, kv_rows,
+                                    offsets, past, nseq, max_past, fused_prep, out, ld_o,
+                                    "decode_ragged_noalloc");
+  if (st != P2P_OK || nseq == 0) return st;
 
   const int hkv = prm->num_kv_heads;
   const int group = prm->num_heads / hkv;
+  // the same split choice as p2p_attn_decode_ragged, P2P_DECODE_SPLITS included
   int min_split = 16;
-  const int splits = p2p::decode_max_splits(int64_t(max_past) + 1, hkv, nseq,
-                                            p2p::ctx_num_sms(ctx), &min_split);
+  int splits = p2p::decode_max_splits(int64_t(max_past) + 1, hkv, nseq, p2p::ctx_num_sms(ctx),
+                                      &min_split);
+  if (p2p::forced_decode_splits() > 0) {
+    splits = p2p::forced_decode_splits();
+    min_split = 16;
+  }
   const size_t pbytes = p2p::decode_partials_bytes(splits, hkv, nseq, group);
   const size_t coff = (pbytes + kCounterAlign - 1) / kCounterAlign * kCounterAlign;
   const size_t cbytes = p2p::decode_counters_bytes(hkv, nseq);
@@ -107,20 +111,14 @@ extern "C" p2p_status p2p_attn_decode_ragged_noalloc(
   e = cudaMemsetAsync(scratch + coff, 0, cbytes, s);
   if (e == cudaSuccess) {
     p2p::DecodeArgs a{};
-    a.qkv = qkv;
-    a.ld_qkv = ld_qkv;
-    a.norm_w = norm_w;
-    a.k_cache = k_cache;
-    a.v_cache = v_cache;
-    a.offsets = offsets;
-    a.past = past;
-    a.out = out;
-    a.ld_o = ld_o;
-    a.rope = rope;
+    p2p::fill_ragged(a, qkv, ld_qkv, norm_w, rope, k_cache, v_cache, kv_rows, offsets, past,
+                     max_past, out, ld_o);
     a.hq = prm->num_heads;
     a.hkv = hkv;
     a.scale_log2 = p2p::eff_scale_log2(prm);
     a.eps = p2p::eff_eps_of(prm);
+    a.err = p2p::ctx_dev_err(ctx);
+    a.wait_deficit = p2p::debug_wait_deficit();
     a.min_split = min_split;
     a.partials = reinterpret_cast<float*>(scratch);
     a.counters = reinterpret_cast<int32_t*>(scratch + coff);

@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     from p2p_b200 import lib
-    assert lib.p2p_abi_version() == 1
+    assert lib.p2p_abi_version() == 2
     for s in range(8):
         assert lib.p2p_status_string(s)
     assert lib.p2p_status_string(3) == b"kv cache full"

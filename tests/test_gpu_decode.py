@@ -420,8 +420,68 @@ def test_ragged_decode(ctx, oracle, fused):
         assert np.array_equal(bits(host(vc_g)), bits(vc_o))
     else:
         ctx.attn_decode_ragged(prm, dev(q_o), None, None, dev(kc_o), dev(vc_o), dev(offsets),
-                               dev(past), out, max_past=1000, fused_prep=False)
+                               dev(past), out, max_past=int(past.max()), fused_prep=False)
     assert_close(host(out), out_o, what="ragged")
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_ragged_entries_outside_the_cache_are_refused(ctx, oracle, fused):
+    """Ragged sequences whose rows would leave the cache (offsets[i] + past[i] >= kv_rows), or
+    with a negative entry, or with past[i] > max_past, are skipped on the device before any
+    load: their output rows keep what they held, sync() reports KV_FULL, and every other
+    sequence still matches the oracle."""
+    import p2p_b200
+    hq, hkv = 32, 8
+    rng = np.random.default_rng(31 + fused)
+    past = np.array([40, 700, 5, 2000, 90, 64, 300, 1500], np.int32)
+    nseq = len(past)
+    offsets = np.zeros(nseq, np.int32)
+    offsets[1:] = np.cumsum(past[:-1] + 1)
+    rows = int(offsets[-1] + past[-1] + 1)
+    max_past = int(past.max())
+    kc = rng.standard_normal((rows, hkv, D)).astype(np.float16)
+    vc = rng.standard_normal((rows, hkv, D)).astype(np.float16)
+    rope = oracle.rope_table(max_past + 1)
+    nw = (1 + 0.1 * rng.standard_normal(2 * D)).astype(np.float16)
+    qkv = rng.standard_normal((nseq, (hq + 2 * hkv) * D)).astype(np.float16)
+    kc_o, vc_o = kc.copy(), vc.copy()
+    q_o = np.zeros((nseq, hq * D), np.float16)
+    for i in range(nseq):
+        sl = slice(offsets[i], offsets[i] + past[i] + 1)
+        kk, vv = kc_o[sl], vc_o[sl]
+        qq = np.zeros((1, hq * D), np.float16)
+        oracle.qk_prep(hq, hkv, D, qkv[i:i + 1], nw, rope, qq, kk, vv, int(past[i]), 1)
+        kc_o[sl], vc_o[sl], q_o[i] = kk, vv, qq[0]
+    out_o = np.zeros((nseq, hq * D), np.float16)
+    oracle.attn_ragged(hq, hkv, D, q_o, kc_o, vc_o, offsets.astype(np.int64), past, out_o)
+    bad_off, bad_past = offsets.copy(), past.copy()
+    bad_past[7] = rows - offsets[7]          # one row past the end of the cache
+    bad_past[2] = -1                         # negative length
+    bad_off[4] = -3                          # negative offset
+    bad_past[5] = max_past + 1               # longer than the host-declared bound
+    refused = [2, 4, 5, 7]
+    prm = p2p_b200.Params(hq, hkv)
+    out = torch.full((nseq, hq * D), 7.0, dtype=torch.float16, device="cuda")
+    kc_g = dev(kc if fused else kc_o)
+    vc_g = dev(vc if fused else vc_o)
+    ctx.attn_decode_ragged(prm, dev(qkv if fused else q_o), dev(nw) if fused else None,
+                           dev(rope) if fused else None, kc_g, vc_g, dev(bad_off),
+                           dev(bad_past), out, max_past=max_past, fused_prep=fused)
+    with pytest.raises(p2p_b200.KvFullError):
+        ctx.sync()
+    got = host(out)
+    ok = [i for i in range(nseq) if i not in refused]
+    assert (got[refused] == 7.0).all()
+    assert_close(got[ok], out_o[ok], what="sequences beside the refused ones")
+    if fused:  # the refused sequences' cache rows were not written either
+        for i in refused:
+            sl = slice(offsets[i], offsets[i] + past[i] + 1)
+            assert np.array_equal(bits(host(kc_g[sl])), bits(kc[sl]))
+    # the context stays usable: a valid call afterwards syncs clean
+    ctx.attn_decode_ragged(prm, dev(q_o), None, None, dev(kc_o), dev(vc_o), dev(offsets),
+                           dev(past), out, max_past=max_past, fused_prep=False)
+    ctx.sync()
+    assert_close(host(out), out_o, what="after the refusal")
 
 
 def test_repeated_calls_reuse_counters(ctx, oracle):
