@@ -172,6 +172,44 @@ def sum_over_ranks(x: float, world: int) -> float:
 
 
 # ---------------------------------------------------------------------------------------------
+# the checker: outputs of each leg compared after its timed region (never inside it).  An
+# element passes when |x - r| <= 2e-3 + 1e-2 |r|; max-abs and max-rel (over |r| > 1e-3) are
+# reported separately as well.
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def parity_stats(got, want, what):
+    import numpy as np
+    x = np.asarray(got, np.float64)
+    r = np.asarray(want, np.float64)
+    err = np.abs(x - r)
+    finite = bool(np.isfinite(x).all())
+    bad = int((~(err <= ATOL + RTOL * np.abs(r))).sum())
+    big = np.abs(r) > 1e-3
+    return {"max_abs": float(err.max()) if err.size else 0.0,
+            "max_rel": float((err[big] / np.abs(r[big])).max()) if big.any() else 0.0,
+            "bad": bad if finite else int(x.size), "n": int(x.size), "checked": what}
+
+
+def reduce_parity(p, world):
+    """Every rank's stats -> the job's (max of the maxima, sum of the counts); same collective
+    steps on every rank."""
+    out = dict(p)
+    out["max_abs"] = max_over_ranks(p["max_abs"], world)
+    out["max_rel"] = max_over_ranks(p["max_rel"], world)
+    out["bad"] = int(sum_over_ranks(float(p["bad"]), world))
+    out["n"] = int(sum_over_ranks(float(p["n"]), world))
+    out["ok"] = out["bad"] == 0
+    out["within_caps"] = out["max_abs"] <= ATOL and out["max_rel"] <= RTOL
+    for k in ("max_abs", "max_rel"):
+        out[k] = float(f"{out[k]:.3e}")
+    if world > 1:
+        out["checked"] = f"every rank: {p['checked']}"
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
 # workloads
 
 def timed_loop(fn, steps, warmup, world, stream):
@@ -190,15 +228,16 @@ def timed_loop(fn, steps, warmup, world, stream):
     return start.elapsed_time(end) / steps  # ms per step on this rank
 
 
-def timed_graph(fn, steps, warmup, world):
+def timed_graph(fn, steps, warmup, world, capture_error_mode="global"):
     """Warm up with direct calls, capture `steps` calls into one CUDA graph, then time one
-    replay (the K steps back to back on the device, no host launch overhead)."""
+    replay (the K steps back to back on the device, no host launch overhead).  Legs with NCCL
+    calls capture in "relaxed" mode (NCCL may enqueue from its own thread)."""
     import torch
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    with torch.cuda.graph(g, capture_error_mode=capture_error_mode):
         for i in range(steps):
             fn(warmup + i)
     g.replay()  # untimed: first replay uploads the graph
@@ -246,11 +285,47 @@ class DecodeWorkload:
                                             for l, (kc, vc) in enumerate(c)],
                                  self.rope, cap, use_meta=True)
             for c in self.copies]
+        # the drop-in per-layer call (engine.js:245-259 runs QK_PREP/ATTN once per attention
+        # layer, between that layer's GEMMs): every (copy, layer) cache as its own one-layer
+        # step, rotating over all of them (605 MB > L2)
+        self.layer_plans = [
+            ctx.plan_decode_step(self.prm, [(self.qkv[l], self.nw[l], kc, vc, self.out[l])],
+                                 self.rope, cap, use_meta=True)
+            for c in self.copies for l, (kc, vc) in enumerate(c)]
         ctx.meta_write(past, 1, 0, stream=torch.cuda.current_stream())
+        self.past = past
         self.bytes_per_step = N_LAYERS * decode_layer_bytes(past)
 
     def step(self, i):
         self.plans[i % len(self.plans)].run()
+
+    def step_one_layer(self, i):
+        self.layer_plans[i % len(self.layer_plans)].run()
+
+    def check(self):
+        """The checker, after the timed regions: copy 0's six layers against the oracle."""
+        import numpy as np
+        from oracle import pyoracle as O
+        torch = self.torch
+        self.plans[0].run()
+        torch.cuda.synchronize()
+        got = self.out.cpu().numpy()
+        rope = self.rope_host()
+        want = np.zeros((N_LAYERS, HQ * D), np.float16)
+        for l, (kc, vc) in enumerate(self.copies[0]):
+            k_h = kc.cpu().numpy()
+            v_h = vc.cpu().numpy()
+            q = np.zeros((1, HQ * D), np.float16)
+            O.qk_prep(HQ, HKV, D, self.qkv[l:l + 1].cpu().numpy(), self.nw[l].cpu().numpy(),
+                      rope, q, k_h, v_h, self.past, 1)
+            o = np.zeros((1, HQ * D), np.float16)
+            O.attn(HQ, HKV, D, q, k_h, v_h, o, self.past, 1)
+            want[l] = o[0]
+        return parity_stats(got, want, f"6 layers x {HQ} heads at past {self.past} vs the oracle")
+
+    def rope_host(self):
+        from oracle import pyoracle as O
+        return O.rope_table(self.cap)
 
 
 def e2e_decode(wl, steps, warmup):
@@ -280,6 +355,25 @@ def e2e_decode(wl, steps, warmup):
     return dt, h_in.numel() * 2, h_out.numel() * 2
 
 
+def e2e_native(device, steps, warmup, world):
+    """The same per-token call from a plain C host (p2p_b200/host/p2p_decode_loop: the C ABI
+    alone, no Python or torch, as a native engine binding calls it), one process per GPU, all
+    ranks at once; returns (seconds per step, h2d bytes, d2h bytes, finite)."""
+    exe = ROOT / "p2p_b200" / "host" / "p2p_decode_loop"
+    if not exe.exists():
+        raise RuntimeError(f"{exe} is missing: build with python p2p_b200/build.py")
+    barrier(world)
+    r = subprocess.run([str(exe), "--device", str(device), "--steps", str(steps),
+                        "--warmup", str(warmup), "--copies", "12", "--past", str(PAST)],
+                       capture_output=True, text=True, timeout=600)
+    barrier(world)
+    if r.returncode != 0:
+        raise RuntimeError(f"p2p_decode_loop failed ({r.returncode}): {r.stderr[-300:]}")
+    j = json.loads(r.stdout.strip().splitlines()[-1])
+    return (j["us_per_step"] * 1e-6, j["h2d_bytes_per_step"], j["d2h_bytes_per_step"],
+            j["outputs_finite"])
+
+
 def ragged_lengths(nseq=256, lo=1024, hi=32768, seed=4):
     import numpy as np
     rng = np.random.default_rng(seed)
@@ -291,7 +385,7 @@ def lpt_shard(lengths, world):
     return lpt_partition([int(x) + 1 for x in lengths], world)
 
 
-def run_ragged(ctx, rank, world, steps, warmup):
+def run_ragged(ctx, rank, world, steps, warmup, check=True):
     import numpy as np
     import torch
     import p2p_b200
@@ -324,21 +418,70 @@ def run_ragged(ctx, rank, world, steps, warmup):
     ms = timed_graph(step, steps, warmup, world)
     my_bytes = float(rows.sum() * HKV * D * 2 * 2 + nseq * ((HQ + 2 * HKV) * D * 2 + 2 * HKV * D * 2
                                                           + HQ * D * 2))
+    if not check:
+        del kc, vc
+        torch.cuda.empty_cache()
+        return ms, my_bytes, None
+    # the checker: this rank's shortest, longest and two more sequences against the oracle
+    from oracle import pyoracle as O
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    rope_h = O.rope_table(int(past_all.max()) + 1)
+    qkv_h, nw_h = qkv.cpu().numpy(), nw.cpu().numpy()
+    sample = sorted({int(np.argmin(past)), int(np.argmax(past)), 0, nseq // 2})
+    want = np.zeros((len(sample), HQ * D), np.float16)
+    for j, i in enumerate(sample):
+        sl = slice(int(offsets[i]), int(offsets[i]) + int(past[i]) + 1)
+        k_i, v_i = kc[sl].cpu().numpy(), vc[sl].cpu().numpy()
+        q_o = np.zeros((1, HQ * D), np.float16)
+        O.qk_prep(HQ, HKV, D, qkv_h[i:i + 1], nw_h, rope_h, q_o, k_i, v_i, int(past[i]), 1)
+        O.attn(HQ, HKV, D, q_o, k_i, v_i, want[j:j + 1], int(past[i]), 1)
+    par = parity_stats(got[sample], want, f"{len(sample)} sequences (shortest, longest, 2 more) "
+                                          f"vs the oracle")
     del kc, vc
     torch.cuda.empty_cache()
-    return ms, my_bytes
+    return ms, my_bytes, par
 
 
-def run_prefill(ctx, steps, warmup):
+def prefill_inputs(s, seed=33, scale=0.5):
+    """The config's prompt: qkv rows [s][3072] ~ scale * N(0,1) (same on every rank)."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (scale * torch.randn((s, (HQ + 2 * HKV) * D), generator=g, device="cuda")).half()
+
+
+def prefill_oracle_rows(qkv, rows, what):
+    """The checker's reference for query rows `rows` of a causal prefill of all heads from
+    position 0: the oracle's QK_PREP on the whole prompt, then its ATTN on those rows."""
+    import numpy as np
+    from oracle import pyoracle as O
+    qkv_h = qkv.cpu().numpy()
+    s = qkv_h.shape[0]
+    rope = O.rope_table(s)
+    q = np.zeros((s, HQ * D), np.float16)
+    kc = np.zeros((s, HKV, D), np.float16)
+    vc = np.zeros_like(kc)
+    O.qk_prep(HQ, HKV, D, qkv_h, None, rope, q, kc, vc, 0, s)
+    want = np.zeros((len(rows), HQ * D), np.float16)
+    for j, r in enumerate(rows):
+        O.attn(HQ, HKV, D, q[r:r + 1], kc, vc, want[j:j + 1], int(r), 1)
+    return want
+
+
+def sample_rows(s):
+    return sorted({0, 1, 2, 127, 128, s // 2, s - 129, s - 2, s - 1})
+
+
+def run_prefill(ctx, steps, warmup, s=2048, copies=4, check=True):
+    """Causal prefill of an s-token prompt on one GPU, all 32 q heads: attention alone (q and
+    the cache rotated beforehand) and QK_PREP + attention (the config's step, cache write
+    included); graph-timed and with direct launches."""
+    import numpy as np
     import torch
     import p2p_b200
-    s = 2048
-    g = torch.Generator(device="cuda").manual_seed(33)
     prm = p2p_b200.Params(HQ, HKV)
     rope = ctx.rope_table(s, D, 1e6)
-    copies = 4
-    qkv = [(0.5 * torch.randn((s, (HQ + 2 * HKV) * D), generator=g, device="cuda")).half()
-           for _ in range(copies)]
+    qkv = [prefill_inputs(s, 33 + i) for i in range(copies)]
     q = torch.zeros((s, HQ * D), device="cuda", dtype=torch.float16)
     kc = torch.zeros((s, HKV, D), device="cuda", dtype=torch.float16)
     vc = torch.zeros_like(kc)
@@ -354,79 +497,86 @@ def run_prefill(ctx, steps, warmup):
         ctx.qk_prep(prm, qkv[i % copies], None, rope, q, kc, vc, pos0=0, m_tokens=s)
         ctx.attn(prm, q, kc, vc, out, pos0=0, m_tokens=s)
 
-    ms_attn = timed_graph(attn_only, steps, warmup, 1)
-    ms_both = timed_graph(prep_and_attn, steps, warmup, 1)
-    return ms_attn, ms_both
+    res = {"ms_attn": timed_graph(attn_only, steps, warmup, 1),
+           "ms_both": timed_graph(prep_and_attn, steps, warmup, 1),
+           "ms_both_direct": timed_loop(prep_and_attn, steps, warmup, 1, stream)}
+    if check:
+        prep_and_attn(0)
+        torch.cuda.synchronize()
+        rows = sample_rows(s)
+        want = prefill_oracle_rows(qkv[0], rows, "")
+        res["parity"] = parity_stats(out.cpu().numpy()[rows], want,
+                                     f"{len(rows)} query rows x {HQ} heads vs the oracle")
+    return res
 
 
-def run_prefill_sharded(ctx, rank, world, s, steps, warmup):
-    """Causal prefill of an s-token prompt split by KV-head group over the ranks, with the NCCL
-    all-gather and the assembly of the [s][Hq*64] output inside the timed region."""
+def sharded_prefill_leg(ctx, comm, rank, world, s, variant, steps, warmup):
+    """Causal prefill of an s-token prompt split by KV-head group over the ranks, one variant
+    of the output assembly, inside the timed region (captured in one CUDA graph with its
+    collectives).  Afterwards the checker compares this rank's full [s][2048] output with all
+    heads computed on this one GPU, and a sample of rows with the oracle."""
+    import numpy as np
     import torch
-    from p2p_b200.sharding import HeadShardedPrefill
-    sp = HeadShardedPrefill(ctx, HQ, HKV, world, rank)
-    g = torch.Generator(device="cuda").manual_seed(33)
-    qkv_full = (0.5 * torch.randn((s, (HQ + 2 * HKV) * D), generator=g, device="cuda")).half()
+    import p2p_b200
+    from p2p_b200.sharding import (HeadShardedPrefill, MulticastHeadShardedPrefill,
+                                   ScatterHeadShardedPrefill)
+    cls = {"allgather": HeadShardedPrefill, "scatter": ScatterHeadShardedPrefill,
+           "multicast": MulticastHeadShardedPrefill}[variant]
+    kw = {} if variant == "allgather" else {"max_tokens": s}
+    sp = cls(ctx, HQ, HKV, world, rank, comm=comm, **kw)
+    qkv_full = prefill_inputs(s)
     qkv_l = qkv_full[:, sp.local_qkv_columns().cuda()].contiguous()
-    del qkv_full
     rope = ctx.rope_table(s, D, 1e6)
     kc = torch.zeros((s, sp.kvn, D), device="cuda", dtype=torch.float16)
     vc = torch.zeros_like(kc)
     q_buf = torch.zeros((s, sp.qn * D), device="cuda", dtype=torch.float16)
-    out_l = torch.zeros_like(q_buf)
-    gather = torch.zeros((world * s, sp.qn * D), device="cuda", dtype=torch.float16)
     out = torch.zeros((s, HQ * D), device="cuda", dtype=torch.float16)
 
     def step(i):
-        sp(qkv_l, None, rope, kc, vc, q_buf, out_l, gather, out, 0, s)
+        if variant == "allgather":
+            sp(qkv_l, None, rope, kc, vc, out, 0, s)
+        else:
+            sp(qkv_l, None, rope, kc, vc, q_buf, 0, s)
 
-    return timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
-
-
-def run_prefill_scatter(ctx, rank, world, s, steps, warmup):
-    """The same head-sharded prefill with the flash kernel writing its rows into every rank's
-    full [s][Hq*64] output over NVLink (CUDA IPC), then one single-element all-reduce ordering
-    the ranks, inside the timed region."""
-    import torch
-    from p2p_b200.sharding import ScatterHeadShardedPrefill
-    sp = ScatterHeadShardedPrefill(ctx, HQ, HKV, world, rank, max_tokens=s)
-    g = torch.Generator(device="cuda").manual_seed(33)
-    qkv_full = (0.5 * torch.randn((s, (HQ + 2 * HKV) * D), generator=g, device="cuda")).half()
-    qkv_l = qkv_full[:, sp.local_qkv_columns().cuda()].contiguous()
-    del qkv_full
-    rope = ctx.rope_table(s, D, 1e6)
-    kc = torch.zeros((s, sp.kvn, D), device="cuda", dtype=torch.float16)
-    vc = torch.zeros_like(kc)
-    q_buf = torch.zeros((s, sp.qn * D), device="cuda", dtype=torch.float16)
-
-    def step(i):
-        sp(qkv_l, None, rope, kc, vc, q_buf, 0, s)
-
-    ms = timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
+    try:
+        ms = timed_graph(step, steps, warmup, world, capture_error_mode="relaxed")
+        timing = "graph"
+    except RuntimeError:  # capture refused: the same steps as direct launches
+        torch.cuda.synchronize()
+        ms = timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
+        timing = "direct"
+    step(0)
+    comm.wait()
+    got = (out if variant == "allgather" else sp.out_full[:s]).clone()
+    # all heads on this GPU (the 1-GPU path the tests pin to the oracle)
+    prm = p2p_b200.Params(HQ, HKV)
+    q1 = torch.zeros((s, HQ * D), device="cuda", dtype=torch.float16)
+    k1 = torch.zeros((s, HKV, D), device="cuda", dtype=torch.float16)
+    v1 = torch.zeros_like(k1)
+    want1 = torch.zeros_like(q1)
+    ctx.qk_prep(prm, qkv_full, None, rope, q1, k1, v1, pos0=0, m_tokens=s)
+    ctx.attn(prm, q1, k1, v1, want1, pos0=0, m_tokens=s)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(got, want1))
+    rows = sample_rows(s)
+    par = parity_stats(got.cpu().numpy()[rows], prefill_oracle_rows(qkv_full, rows, ""),
+                       f"{len(rows)} query rows x {HQ} heads vs the oracle, and the whole "
+                       f"[{s}][{HQ * D}] output vs all heads on one GPU")
     sp.close()
-    return ms
+    del sp
+    return ms, timing, par, same
 
 
-def run_prefill_multicast(ctx, rank, world, s, steps, warmup):
-    """The same head-sharded prefill with the flash epilogue storing each row once to the NVLink
-    multicast address of a symmetric-memory buffer (NVSwitch replicates it into every rank's
-    output), then one single-element all-reduce, inside the timed region."""
-    import torch
-    from p2p_b200.sharding import MulticastHeadShardedPrefill
-    sp = MulticastHeadShardedPrefill(ctx, HQ, HKV, world, rank, max_tokens=s)
-    g = torch.Generator(device="cuda").manual_seed(33)
-    qkv_full = (0.5 * torch.randn((s, (HQ + 2 * HKV) * D), generator=g, device="cuda")).half()
-    qkv_l = qkv_full[:, sp.local_qkv_columns().cuda()].contiguous()
-    del qkv_full
-    rope = ctx.rope_table(s, D, 1e6)
-    kc = torch.zeros((s, sp.kvn, D), device="cuda", dtype=torch.float16)
-    vc = torch.zeros_like(kc)
-    q_buf = torch.zeros((s, sp.qn * D), device="cuda", dtype=torch.float16)
-
-    def step(i):
-        sp(qkv_l, None, rope, kc, vc, q_buf, 0, s)
-
-    return timed_loop(step, steps, warmup, world, torch.cuda.current_stream())
+def vision_oracle_check(q, k, v, out, images, what):
+    import numpy as np
+    from oracle import pyoracle as O
+    want, got = [], []
+    for b in images:
+        w = np.zeros((1024, 12 * D), np.float16)
+        O.vision_attn(12, D, q[b].cpu().numpy(), k[b].cpu().numpy(), v[b].cpu().numpy(), w)
+        want.append(w)
+        got.append(out[b].cpu().numpy())
+    return parity_stats(np.stack(got), np.stack(want), what)
 
 
 def run_vision_split(ctx, rank, world, steps, warmup):
@@ -445,10 +595,14 @@ def run_vision_split(ctx, rank, world, steps, warmup):
         if nb:
             ctx.attn_bidir(prm, q, k, v, out)
 
-    return timed_graph(step, steps, warmup, world)
+    ms = timed_graph(step, steps, warmup, world)
+    torch.cuda.synchronize()
+    par = vision_oracle_check(q, k, v, out, sorted({0, max(nb, 1) - 1}),
+                              "first and last image of each rank (all 12 heads) vs the oracle")
+    return ms, par
 
 
-def run_vision(ctx, steps, warmup):
+def run_vision(ctx, steps, warmup, check=True):
     import torch
     import p2p_b200
     b, s, nh = 16, 1024, 12
@@ -461,7 +615,13 @@ def run_vision(ctx, steps, warmup):
     def step(i):
         ctx.attn_bidir(prm, q, k, v, out)
 
-    return timed_graph(step, steps, warmup, 1)
+    ms = timed_graph(step, steps, warmup, 1)
+    torch.cuda.synchronize()
+    if not check:
+        return ms, None
+    par = vision_oracle_check(q, k, v, out, [0, 7, 15], "images 0, 7, 15 (all 12 heads) vs "
+                                                        "the oracle")
+    return ms, par
 
 
 # ---------------------------------------------------------------------------------------------
@@ -570,14 +730,21 @@ def run_only(ctx, args):
         wl = DecodeWorkload(ctx, 0, copies=4, past=args.past)
         ms = timed_graph(wl.step, args.steps, args.warmup, 1)
         res = {"us_per_step": ms * 1e3, "gbs": wl.bytes_per_step / (ms * 1e-3) / 1e9}
+    elif args.only == "decode1":
+        wl = DecodeWorkload(ctx, 0, copies=12, past=args.past)
+        ms = timed_graph(wl.step_one_layer, args.steps, args.warmup, 1)
+        b = wl.bytes_per_step / N_LAYERS
+        res = {"us_per_step": ms * 1e3, "gbs": b / (ms * 1e-3) / 1e9}
     elif args.only == "ragged":
-        ms, b = run_ragged(ctx, 0, 1, args.steps, args.warmup)
+        ms, b, _ = run_ragged(ctx, 0, 1, args.steps, args.warmup, check=False)
         res = {"ms_per_step": ms, "gbs": b / (ms * 1e-3) / 1e9}
     elif args.only == "prefill":
-        pa, pb = run_prefill(ctx, args.steps, args.warmup)
-        res = {"us_attn": pa * 1e3, "tflops_attn": prefill_flops(2048) / (pa * 1e-3) / 1e12}
+        r = run_prefill(ctx, args.steps, args.warmup, s=args.prefill_s, check=False)
+        fl = prefill_flops(args.prefill_s)
+        res = {"us_attn": r["ms_attn"] * 1e3, "tflops_attn": fl / (r["ms_attn"] * 1e-3) / 1e12,
+               "us_prep_plus_attn": r["ms_both"] * 1e3}
     else:
-        va = run_vision(ctx, args.steps, args.warmup)
+        va, _ = run_vision(ctx, args.steps, args.warmup, check=False)
         res = {"us": va * 1e3, "tflops": vision_flops() / (va * 1e-3) / 1e12}
     print(json.dumps({"only": args.only, **res}), flush=True)
 
@@ -590,9 +757,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip prefill/vision/ragged legs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode", "ragged", "prefill", "vision"],
+    ap.add_argument("--only", choices=["decode", "decode1", "ragged", "prefill", "vision"],
                     help="run one leg on one GPU and print its timing (profiling commands)")
     ap.add_argument("--past", type=int, default=PAST, help="decode context for --only decode")
+    ap.add_argument("--prefill-s", type=int, default=2048, help="prompt length for --only prefill")
     ap.add_argument("--quick", action="store_true",
                     help="headline kernel only (no e2e, side legs, CPU leg or clock tail); "
                          "the profiling command")
@@ -637,17 +805,40 @@ def main():
     value_gbs = total_bytes / (ms_max * 1e-3) / 1e9
     per_gpu_gbs = wl.bytes_per_step / (ms_max * 1e-3) / 1e9
 
+    e2e_note = "plain C host over the C ABI (p2p_b200/host/p2p_decode_loop), wall clock"
     if args.quick:
-        e2e_sec, h2d, d2h = float("nan"), 0, 0
+        e2e_sec, h2d, d2h, py_sec = float("nan"), 0, 0, float("nan")
     else:
-        e2e_sec, h2d, d2h = e2e_decode(wl, max(20, args.steps // 2), args.warmup)
+        try:
+            e2e_sec, h2d, d2h, finite = e2e_native(local, max(50, args.steps), args.warmup,
+                                                   world)
+            if not finite:
+                e2e_note += "; NON-FINITE OUTPUT"
+        except (RuntimeError, subprocess.TimeoutExpired, ValueError) as e:
+            e2e_sec, h2d, d2h = float("nan"), 0, 0
+            e2e_note = f"native host program failed: {str(e)[:160]}"
+        py_sec, _, _ = e2e_decode(wl, max(20, args.steps // 2), args.warmup)
     e2e_sec = max_over_ranks(e2e_sec, world)
+    py_sec = max_over_ranks(py_sec, world)
     e2e_gbs = total_bytes / e2e_sec / 1e9
+
+    # the headline's output against the oracle (after its timed region); every rank checks
+    parity = reduce_parity(wl.check(), world) if not args.quick else None
 
     side = {}
     if not args.no_side:
+        # the drop-in per-layer call: one p2p_decode_step with one layer (8.4 MB)
+        ms1 = max_over_ranks(timed_graph(wl.step_one_layer, args.steps, args.warmup, world),
+                             world)
+        b1 = wl.bytes_per_step / N_LAYERS
+        side["decode_one_layer"] = {
+            "workload": "one attention layer per call (what engine.js:245-259 dispatches "
+                        "between that layer's GEMMs), ctx 4096+1, 32q/8kv, rotating over 72 "
+                        "layer caches (605 MB > L2)",
+            "gbs_per_gpu": round(b1 / (ms1 * 1e-3) / 1e9, 1), "us_per_step": round(ms1 * 1e3, 3),
+            "hbm_frac_of_measured": round(b1 / (ms1 * 1e-3) / 1e9 / hbm_peak, 4)}
         try:
-            r_ms, r_bytes = run_ragged(ctx, rank, world, steps=10, warmup=3)
+            r_ms, r_bytes, r_par = run_ragged(ctx, rank, world, steps=10, warmup=3)
             r_ms = max_over_ranks(r_ms, world)
             r_bytes = sum_over_ranks(r_bytes, world)
             side["ragged_decode"] = {
@@ -655,57 +846,74 @@ def main():
                             "LPT-sharded by tokens across ranks",
                 "gbs": round(r_bytes / (r_ms * 1e-3) / 1e9, 1), "ms_per_step": round(r_ms, 4),
                 "bytes_per_step": int(r_bytes), "hbm_frac_per_gpu_of_measured":
-                    round(r_bytes / world / (r_ms * 1e-3) / 1e9 / hbm_peak, 4)}
+                    round(r_bytes / world / (r_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                "parity": reduce_parity(r_par, world)}
         except p2p_b200.P2PError as e:
             side["ragged_decode"] = {"error": str(e)}
         if world > 1:
+            from p2p_b200.comm import Comm
+            comm = Comm.from_process_group(ctx, world, rank)
+            what = {"allgather": "NCCL all-gather inside the library (p2p_attn_prefill_sharded) "
+                                 "+ [S][2048] assembly",
+                    "scatter": "flash epilogue writes every rank's [S][2048] output over NVLink "
+                               "(CUDA IPC), then one ordering all-reduce",
+                    "multicast": "flash epilogue stores every row once as NVLink multicast "
+                                 "(NVSwitch writes every rank's output), then one ordering "
+                                 "all-reduce"}
             for s_tok in (2048, 16384):
-                ms = max_over_ranks(run_prefill_sharded(ctx, rank, world, s_tok, 10, 3), world)
                 fl = prefill_flops(s_tok)
-                side[f"prefill_head_sharded_s{s_tok}"] = {
-                    "workload": f"causal prefill S={s_tok}, 32q/8kv split by kv-head group over "
-                                f"{world} GPUs + NCCL all-gather + [S][2048] assembly",
-                    "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
-                ms = max_over_ranks(run_prefill_scatter(ctx, rank, world, s_tok, 10, 3), world)
-                side[f"prefill_head_scatter_s{s_tok}"] = {
-                    "workload": f"causal prefill S={s_tok}, 32q/8kv split by kv-head group over "
-                                f"{world} GPUs, flash epilogue writes every rank's [S][2048] "
-                                f"output over NVLink (no all-gather)",
-                    "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
-                key = f"prefill_head_multicast_s{s_tok}"
-                try:
-                    ms = max_over_ranks(run_prefill_multicast(ctx, rank, world, s_tok, 10, 3),
-                                        world)
+                for variant in ("allgather", "scatter", "multicast"):
+                    key = f"prefill_head_{variant}_s{s_tok}"
+                    try:
+                        ms, timing, par, same = sharded_prefill_leg(ctx, comm, rank, world,
+                                                                    s_tok, variant, 10, 3)
+                    except RuntimeError as e:  # same on every rank: no collective was entered
+                        side[key] = {"unavailable": str(e).splitlines()[0][:200]}
+                        continue
+                    ms = max_over_ranks(ms, world)
+                    par = reduce_parity(par, world)
+                    par["equal_to_one_gpu"] = max_over_ranks(0.0 if same else 1.0, world) == 0
+                    par["ok"] = par["ok"] and par["equal_to_one_gpu"]
                     side[key] = {
-                        "workload": f"causal prefill S={s_tok}, 32q/8kv split by kv-head group "
-                                    f"over {world} GPUs, flash epilogue stores every row once as "
-                                    f"NVLink multicast (NVSwitch writes every rank's output)",
-                        "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
-                except RuntimeError as e:  # same on every rank: no collective was entered
-                    side[key] = {"unavailable": str(e).splitlines()[0][:200]}
-            ms = max_over_ranks(run_vision_split(ctx, rank, world, 10, 3), world)
+                        "workload": f"causal prefill S={s_tok} (QK_PREP + attention), 32q/8kv "
+                                    f"split by kv-head group over {world} GPUs, {what[variant]}",
+                        "tflops": round(fl / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2),
+                        "timing": timing, "parity": par}
+            comm.close()
+            v_ms, v_par = run_vision_split(ctx, rank, world, 10, 3)
+            ms = max_over_ranks(v_ms, world)
             side["vision_image_split"] = {
                 "workload": f"vision B=16 S=1024 12 heads split by image over {world} GPUs",
-                "tflops": round(vision_flops() / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
+                "tflops": round(vision_flops() / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2),
+                "parity": reduce_parity(v_par, world)}
         if world == 1:
+            for s_tok, steps in ((2048, 20), (16384, 5)):
+                key = "prefill" if s_tok == 2048 else f"prefill_s{s_tok}"
+                try:
+                    r = run_prefill(ctx, steps=steps, warmup=5 if s_tok == 2048 else 3,
+                                    s=s_tok, copies=4 if s_tok == 2048 else 1)
+                    fl = prefill_flops(s_tok)
+                    pa, pb = r["ms_attn"], r["ms_both"]
+                    side[key] = {
+                        "workload": f"causal prefill S={s_tok}, 32q/8kv, d64, fp16, one GPU",
+                        "tflops_attn": round(fl / (pa * 1e-3) / 1e12, 1),
+                        "us_attn": round(pa * 1e3, 2),
+                        "tflops_prep_plus_attn": round(fl / (pb * 1e-3) / 1e12, 1),
+                        "us_prep_plus_attn": round(pb * 1e3, 2),
+                        "us_prep_plus_attn_direct_launch": round(r["ms_both_direct"] * 1e3, 2),
+                        "tensor_frac_of_measured": round(fl / (pa * 1e-3) / 1e12 / tensor_peak,
+                                                         4),
+                        "parity": reduce_parity(r["parity"], 1)}
+                except p2p_b200.P2PError as e:
+                    side[key] = {"error": str(e)}
             try:
-                pa, pb = run_prefill(ctx, steps=20, warmup=5)
-                fl = prefill_flops(2048)
-                side["prefill"] = {
-                    "workload": "causal prefill S=2048, 32q/8kv, d64, fp16",
-                    "tflops_attn": round(fl / (pa * 1e-3) / 1e12, 1), "us_attn": round(pa * 1e3, 2),
-                    "tflops_prep_plus_attn": round(fl / (pb * 1e-3) / 1e12, 1),
-                    "us_prep_plus_attn": round(pb * 1e3, 2),
-                    "tensor_frac_of_measured": round(fl / (pa * 1e-3) / 1e12 / tensor_peak, 4)}
-            except p2p_b200.P2PError as e:
-                side["prefill"] = {"error": str(e)}
-            try:
-                va = run_vision(ctx, steps=20, warmup=5)
+                va, v_par = run_vision(ctx, steps=20, warmup=5)
                 fl = vision_flops()
                 side["vision"] = {
                     "workload": "bidirectional MHA B=16 S=1024 12 heads d64 fp16",
                     "tflops": round(fl / (va * 1e-3) / 1e12, 1), "us": round(va * 1e3, 2),
-                    "tensor_frac_of_measured": round(fl / (va * 1e-3) / 1e12 / tensor_peak, 4)}
+                    "tensor_frac_of_measured": round(fl / (va * 1e-3) / 1e12 / tensor_peak, 4),
+                    "parity": reduce_parity(v_par, 1)}
             except p2p_b200.P2PError as e:
                 side["vision"] = {"error": str(e)}
 
@@ -741,8 +949,11 @@ def main():
                          "frac_of_nominal_8tbs": round(per_gpu_gbs / 8000.0, 4),
                          "traffic": tr, "kernel": "decode_mma_kernel<G=4,fused,layers,cluster>"},
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_sec * 1e6, 2)},
+                    "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_sec * 1e6, 2),
+                    "host": e2e_note,
+                    "python_ctypes_us_per_step": round(py_sec * 1e6, 2)},
             "gpu_launches": args.steps,
+            "parity": parity,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "side": side,

@@ -178,6 +178,43 @@ p2p_status p2p_shared_open(p2p_ctx* ctx, const unsigned char handle[P2P_IPC_HAND
                            void** ptr);
 p2p_status p2p_shared_close(p2p_ctx* ctx, void* ptr);
 
+/* The library's own communicator over the GPUs of one node (one process per GPU), used by
+ * p2p_attn_prefill_sharded and to order the ranks after p2p_attn_scatter/_multicast.  NCCL is
+ * loaded at run time (libnccl.so.2; P2P_NCCL_LIB names another file).  Rank 0 calls
+ * p2p_comm_unique_id and hands the bytes to the other ranks over any side channel; every rank
+ * then calls p2p_comm_create.  Every wait on the other ranks is bounded by timeout_ms on the
+ * host: when it runs out the communicator is aborted (its collectives in flight end) and the
+ * call returns P2P_ERR_TIMEOUT; an NCCL failure returns P2P_ERR_NCCL.  An aborted communicator
+ * returns P2P_ERR_NCCL from every later call; destroy it and create a new one.  The reference
+ * has no multi-GPU code: these serve the ATTN dispatch (engine.js:222) split over GPUs. */
+#define P2P_COMM_ID_BYTES 128
+typedef struct p2p_comm p2p_comm;
+p2p_status p2p_comm_unique_id(unsigned char id[P2P_COMM_ID_BYTES]);
+p2p_status p2p_comm_create(p2p_ctx* ctx, int32_t nranks, int32_t rank,
+                           const unsigned char id[P2P_COMM_ID_BYTES], int32_t timeout_ms,
+                           p2p_comm** out);
+p2p_status p2p_comm_destroy(p2p_comm* comm);
+/* Waits (bounded) until `stream` has drained, collectives included, then as p2p_sync. */
+p2p_status p2p_comm_wait(p2p_comm* comm, void* stream);
+/* A one-element all-reduce on `stream`: every rank's earlier work on its stream (e.g. the
+ * NVLink stores of p2p_attn_scatter) is complete before any rank's later work starts. */
+p2p_status p2p_comm_barrier(p2p_comm* comm, void* stream);
+
+/* kernels.js:216-319 (QK_PREP + ATTN of a causal prompt chunk) split by kv-head group over the
+ * communicator's ranks: rank g owns kv heads [g*Hkv/G, (g+1)*Hkv/G) and their q heads.  prm
+ * counts the model's heads; qkv holds this rank's columns only, [M][ld_qkv] rows
+ * [its q heads | its k heads | its v heads] (what a column-parallel QKV projection produces);
+ * k_cache/v_cache are this rank's [cap][Hkv/G][D] slices, written at rows pos0..pos0+M-1.
+ * The rank's attention rows are exchanged with one all-gather over NVLink and every rank's
+ * out [M][ld_o] receives all heads (head h at column h*D).  Workspace lives in the
+ * communicator and grows on the first call of a larger M (capture graphs after that call). */
+p2p_status p2p_attn_prefill_sharded(p2p_ctx* ctx, p2p_comm* comm, const p2p_attn_params* prm,
+                                    const void* qkv, int64_t ld_qkv, const void* norm_w,
+                                    const void* rope, void* k_cache, void* v_cache,
+                                    int64_t kv_cap_tokens, const uint32_t* meta_dev,
+                                    int32_t pos0, int32_t m_tokens, void* out, int64_t ld_o,
+                                    void* stream);
+
 /* One decode step (QK_PREP then ATTN with M = 1, engine.js:425-429) for up to
  * P2P_MAX_LAYERS attention layers in ONE launch: for each layer the new token's qkv row is
  * normed/rotated, its k/v are appended at row pos, and its Hq output rows are written.

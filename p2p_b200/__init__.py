@@ -5,11 +5,12 @@ host mirror of the reference engine's attention operators.  Importing it loads t
 and fails if it has not been built; there is no CPU fallback.
 """
 from ._lib import (  # noqa: F401
-    LIB_PATH, MAX_LAYERS, P2P_ERR_INVALID_ARG, P2P_ERR_KV_FULL, P2P_ERR_OOM, P2P_ERR_TIMEOUT,
-    KvFullError, OomError, P2PError, lib,
+    LIB_PATH, MAX_LAYERS, P2P_ERR_INVALID_ARG, P2P_ERR_KV_FULL, P2P_ERR_NCCL, P2P_ERR_OOM,
+    P2P_ERR_TIMEOUT, KvFullError, OomError, P2PError, lib,
 )
 from .attention import Context, KVCache, LfmAttention, Params  # noqa: F401
+from .comm import Comm  # noqa: F401
 
-__all__ = ["Context", "KVCache", "LfmAttention", "Params", "P2PError", "KvFullError",
+__all__ = ["Comm", "Context", "KVCache", "LfmAttention", "Params", "P2PError", "KvFullError",
            "OomError", "lib", "LIB_PATH", "MAX_LAYERS", "P2P_ERR_INVALID_ARG", "P2P_ERR_KV_FULL",
-           "P2P_ERR_OOM", "P2P_ERR_TIMEOUT"]
+           "P2P_ERR_NCCL", "P2P_ERR_OOM", "P2P_ERR_TIMEOUT"]

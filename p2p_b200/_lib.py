@@ -25,6 +25,7 @@ P2P_F16 = 0
 P2P_F32 = 1
 MAX_LAYERS = 16
 P2P_IPC_HANDLE_BYTES = 64
+P2P_COMM_ID_BYTES = 128
 
 
 class P2PError(RuntimeError):
@@ -106,6 +107,13 @@ PROTOTYPES = {
     "p2p_shared_free": (_st, [_v, _v]),
     "p2p_shared_open": (_st, [_v, C.c_char_p, C.POINTER(_v)]),
     "p2p_shared_close": (_st, [_v, _v]),
+    "p2p_comm_unique_id": (_st, [C.c_char_p]),
+    "p2p_comm_create": (_st, [_v, _i32, _i32, C.c_char_p, _i32, C.POINTER(_v)]),
+    "p2p_comm_destroy": (_st, [_v]),
+    "p2p_comm_wait": (_st, [_v, _v]),
+    "p2p_comm_barrier": (_st, [_v, _v]),
+    "p2p_attn_prefill_sharded": (
+        _st, [_v, _v, _pp, _v, _i64, _v, _v, _v, _v, _i64, _v, _i32, _i32, _v, _i64, _v]),
     "p2p_debug_set_alloc_limit": (_st, [_i64]),
     "p2p_debug_set_wait_deficit": (_st, [_i32]),
 }

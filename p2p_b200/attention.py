@@ -224,6 +224,20 @@ class Context:
             rows, _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep),
             _ptr(out), out.stride(0), _stream(stream)))
 
+    def attn_prefill_sharded(self, comm, prm: Params, qkv_local: torch.Tensor, norm_w, rope,
+                             k_cache: torch.Tensor, v_cache: torch.Tensor, out: torch.Tensor, *,
+                             pos0: int = 0, m_tokens: Optional[int] = None,
+                             use_meta: bool = False, stream=None):
+        """QK_PREP + ATTN of a causal chunk split by kv-head group over comm's ranks; prm
+        counts the model's heads, qkv_local / the caches hold this rank's heads only, and every
+        rank's out [M][Hq*64] receives all heads (one all-gather inside the library)."""
+        m = qkv_local.shape[0] if m_tokens is None else m_tokens
+        self._chk(lib.p2p_attn_prefill_sharded(
+            self.h, comm.h, C.byref(prm.c()), _ptr(qkv_local), qkv_local.stride(0),
+            _ptr(norm_w), rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(k_cache),
+            _ptr(v_cache), k_cache.shape[0], self.meta_ptr if use_meta else None, pos0, m,
+            _ptr(out), out.stride(0), _stream(stream)))
+
     def attn_bidir(self, prm: Params, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    out: torch.Tensor, stream=None):
         """q/k/v/out: [B][S][ld] (vision-kernels.js:198 layout)."""

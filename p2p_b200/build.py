@@ -4,7 +4,8 @@
 
 Compiles every p2p_b200/csrc/*.cu with nvcc for `arch=compute_100a,code=sm_100a` into
 p2p_b200/_build/*.o (in parallel) and links p2p_b200/libp2pattn.so in-tree, with the CUDA
-runtime linked statically so the library only needs the driver at run time.
+runtime linked statically so the library only needs the driver at run time; then builds the
+plain C host program p2p_b200/host/p2p_decode_loop against it.
 """
 from __future__ import annotations
 
@@ -63,12 +64,36 @@ def build(verbose_ptxas: bool = False) -> Path:
     newest = max(o.stat().st_mtime for o in objs)
     if not LIB.exists() or LIB.stat().st_mtime < newest:
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs)]
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs),
+               "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         tmp.replace(LIB)
+    build_host_loop()
     return LIB
+
+
+HOST_SRC = PKG / "host" / "decode_loop.c"
+HOST_BIN = PKG / "host" / "p2p_decode_loop"
+
+
+def build_host_loop() -> Path:
+    """The plain C host program that drives the decode step through the C ABI (no Python):
+    the end-to-end leg of bench.py runs it.  CUDA runtime linked statically, the library found
+    beside it through the run path."""
+    deps = [HOST_SRC, LIB, *INCLUDE.glob("*.h")]
+    if HOST_BIN.exists() and HOST_BIN.stat().st_mtime > max(d.stat().st_mtime for d in deps):
+        return HOST_BIN
+    cuda = Path(nvcc()).resolve().parent.parent
+    cmd = ["gcc", "-O2", "-std=c11", "-Wall", "-Wextra", "-I", str(INCLUDE),
+           "-I", str(cuda / "include"), str(HOST_SRC), "-o", str(HOST_BIN),
+           "-L", str(PKG), "-lp2pattn", "-L", str(cuda / "lib64"), "-lcudart_static",
+           "-lpthread", "-ldl", "-lrt", "-lm", "-Wl,-rpath,$ORIGIN/.."]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host program build failed:\n{r.stdout}\n{r.stderr}")
+    return HOST_BIN
 
 
 if __name__ == "__main__":

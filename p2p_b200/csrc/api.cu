@@ -918,6 +918,8 @@ float eff_scale_log2(const p2p_attn_params* prm) {
 }
 float eff_eps_of(const p2p_attn_params* prm) { return eff_eps(prm); }
 int forced_decode_splits() { return forced_splits(); }
+cudaError_t lib_alloc(void** p, size_t bytes) { return dev_alloc(p, bytes); }
+void lib_free(void* p, size_t bytes) { dev_free(p, bytes); }
 int32_t* ctx_dev_err(const p2p_ctx* ctx) { return ctx->dev_err; }
 int32_t debug_wait_deficit() { return g_wait_deficit.load(); }
 

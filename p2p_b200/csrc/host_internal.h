@@ -17,6 +17,9 @@ p2p_status ctx_check_params(p2p_ctx* ctx, const p2p_attn_params* prm);
 float eff_scale_log2(const p2p_attn_params* prm);  // scale (0 -> 1/sqrt(D)) times log2(e)
 float eff_eps_of(const p2p_attn_params* prm);      // RMSNorm epsilon (0 -> 1e-5)
 int forced_decode_splits();                 // P2P_DECODE_SPLITS (0: not set)
+// Device allocations of the library (they honour p2p_debug_set_alloc_limit).
+cudaError_t lib_alloc(void** p, size_t bytes);
+void lib_free(void* p, size_t bytes);
 int32_t* ctx_dev_err(const p2p_ctx* ctx);  // the device error word p2p_sync reports
 int32_t debug_wait_deficit();               // p2p_debug_set_wait_deficit's current value
 

@@ -6,7 +6,8 @@ Where the work shards naturally:
     data path.
   * long-context prefill -- KV-head groups: rank g owns kv heads [g*Hkv/G, (g+1)*Hkv/G) and
     their query heads, computes out[:, heads_g] and its KV-cache slice; either one NCCL
-    all-gather assembles the [S][Hq*D] output (HeadShardedPrefill), or the flash kernel writes
+    all-gather inside the library assembles the [S][Hq*D] output (HeadShardedPrefill, the C
+    ABI's p2p_attn_prefill_sharded over its own communicator), or the flash kernel writes
     its rows straight into every rank's full output over NVLink, either once per peer
     (ScatterHeadShardedPrefill) or once as NVLink multicast stores that NVSwitch replicates
     (MulticastHeadShardedPrefill).
@@ -67,18 +68,25 @@ class HeadShardedPrefill:
 
     Rank g owns kv heads [g*Hkv/G, (g+1)*Hkv/G) and their query heads: its QK_PREP writes only
     its slice of the KV cache (dense [cap][Hkv/G][64] on this GPU, the layout a column-parallel
-    QKV projection produces) and its flash attention produces out[:, heads_g].  One NCCL
-    all-gather over NVLink exchanges the [M][Hq/G*64] slices and the reference's [M][Hq*64]
-    layout is assembled locally.  The only collective of the path.
+    QKV projection produces) and its flash attention produces out[:, heads_g].  One all-gather
+    over NVLink exchanges the [M][Hq/G*64] slices and every rank assembles the reference's
+    [M][Hq*64] layout -- all inside the library (p2p_attn_prefill_sharded, its own NCCL
+    communicator), so a host calling the C ABI needs no collective library of its own.
+    `comm` is a p2p_b200.Comm; without one it is created over the torch.distributed group.
     """
 
     def __init__(self, ctx, num_heads: int, num_kv_heads: int, world: int, rank: int,
-                 group=None):
+                 group=None, comm=None):
         from .attention import Params
+        from .comm import Comm
         self.ctx, self.world, self.rank, self.group = ctx, world, rank, group
         self.kv0, self.kvn, self.q0, self.qn = head_groups(num_heads, num_kv_heads, world, rank)
         self.prm = Params(self.qn, self.kvn)
+        self.prm_full = Params(num_heads, num_kv_heads)
         self.num_heads = num_heads
+        self.own_comm = comm is None
+        self.comm = comm if comm is not None else Comm.from_process_group(ctx, world, rank,
+                                                                          group)
 
     def local_qkv_columns(self, head_dim: int = 64):
         """Column indices of this rank's q, k and v heads inside a full qkv row."""
@@ -90,20 +98,17 @@ class HeadShardedPrefill:
                 torch.arange((hq + hkv) * d + self.kv0 * d, (hq + hkv) * d + (self.kv0 + self.kvn) * d)]
         return torch.cat(cols)
 
-    def __call__(self, qkv_local, norm_w, rope, k_cache, v_cache, q_buf, out_local, gather_buf,
-                 out_full, pos0: int, m_tokens: int, stream=None):
-        import torch.distributed as dist
-        self.ctx.qk_prep(self.prm, qkv_local, norm_w, rope, q_buf, k_cache, v_cache, pos0=pos0,
-                         m_tokens=m_tokens, stream=stream)
-        self.ctx.attn(self.prm, q_buf, k_cache, v_cache, out_local, pos0=pos0, m_tokens=m_tokens,
-                      stream=stream)
-        if self.world > 1:
-            dist.all_gather_into_tensor(gather_buf, out_local, group=self.group)
-            out_full.copy_(assemble_head_shards(
-                gather_buf.view(self.world, m_tokens, self.qn * 64), m_tokens, self.qn))
-        else:
-            out_full.copy_(out_local)
+    def __call__(self, qkv_local, norm_w, rope, k_cache, v_cache, out_full, pos0: int,
+                 m_tokens: int, stream=None):
+        self.ctx.attn_prefill_sharded(self.comm, self.prm_full, qkv_local, norm_w, rope,
+                                      k_cache, v_cache, out_full, pos0=pos0, m_tokens=m_tokens,
+                                      stream=stream)
         return out_full
+
+    def close(self):
+        if self.own_comm and self.comm is not None:
+            self.comm.close()
+        self.comm = None
 
 
 class ScatterHeadShardedPrefill(HeadShardedPrefill):
@@ -117,11 +122,11 @@ class ScatterHeadShardedPrefill(HeadShardedPrefill):
     rank starts the next call (in a model, the next layer's collective orders that)."""
 
     def __init__(self, ctx, num_heads: int, num_kv_heads: int, world: int, rank: int,
-                 max_tokens: int, group=None):
+                 max_tokens: int, group=None, comm=None):
         import torch
         import torch.distributed as dist
         from .attention import _from_device_ptr
-        super().__init__(ctx, num_heads, num_kv_heads, world, rank, group)
+        super().__init__(ctx, num_heads, num_kv_heads, world, rank, group, comm)
         self.max_tokens = max_tokens
         self.ld_o = num_heads * 64
         nbytes = max_tokens * self.ld_o * 2
@@ -135,11 +140,9 @@ class ScatterHeadShardedPrefill(HeadShardedPrefill):
         self.outs = [self.own] + self.peers
         self.out_full = _from_device_ptr(self.own, nbytes, ctx.device).view(torch.float16).view(
             max_tokens, self.ld_o)
-        self.flag = torch.zeros(1, dtype=torch.float32, device=f"cuda:{ctx.device}")
 
     def __call__(self, qkv_local, norm_w, rope, k_cache, v_cache, q_buf, pos0: int,
                  m_tokens: int, stream=None):
-        import torch.distributed as dist
         if m_tokens > self.max_tokens:
             raise ValueError(f"{m_tokens} tokens > max_tokens {self.max_tokens}")
         self.ctx.qk_prep(self.prm, qkv_local, norm_w, rope, q_buf, k_cache, v_cache, pos0=pos0,
@@ -147,7 +150,7 @@ class ScatterHeadShardedPrefill(HeadShardedPrefill):
         self.ctx.attn_scatter(self.prm, q_buf, k_cache, v_cache, self.outs, self.ld_o, self.q0,
                               pos0=pos0, m_tokens=m_tokens, stream=stream)
         if self.world > 1:
-            dist.all_reduce(self.flag, group=self.group)  # every rank's rows have landed
+            self.comm.barrier(stream)  # every rank's rows have landed
         return self.out_full[:m_tokens]
 
     def close(self):
@@ -160,6 +163,7 @@ class ScatterHeadShardedPrefill(HeadShardedPrefill):
         if self.own:
             self.ctx.shared_free(self.own)
             self.own = None
+        super().close()
 
 
 class MulticastHeadShardedPrefill(HeadShardedPrefill):
@@ -171,11 +175,11 @@ class MulticastHeadShardedPrefill(HeadShardedPrefill):
     node has none.  The same buffer reuse rule as ScatterHeadShardedPrefill applies."""
 
     def __init__(self, ctx, num_heads: int, num_kv_heads: int, world: int, rank: int,
-                 max_tokens: int, group=None):
+                 max_tokens: int, group=None, comm=None):
         import torch
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
-        super().__init__(ctx, num_heads, num_kv_heads, world, rank, group)
+        super().__init__(ctx, num_heads, num_kv_heads, world, rank, group, comm)
         self.max_tokens = max_tokens
         self.ld_o = num_heads * 64
         self.out_full = symm_mem.empty((max_tokens, self.ld_o), dtype=torch.float16,
@@ -184,11 +188,9 @@ class MulticastHeadShardedPrefill(HeadShardedPrefill):
         self.mc = int(self.handle.multicast_ptr)
         if not self.mc:
             raise RuntimeError("no NVLink multicast support for this group")
-        self.flag = torch.zeros(1, dtype=torch.float32, device=f"cuda:{ctx.device}")
 
     def __call__(self, qkv_local, norm_w, rope, k_cache, v_cache, q_buf, pos0: int,
                  m_tokens: int, stream=None):
-        import torch.distributed as dist
         if m_tokens > self.max_tokens:
             raise ValueError(f"{m_tokens} tokens > max_tokens {self.max_tokens}")
         self.ctx.qk_prep(self.prm, qkv_local, norm_w, rope, q_buf, k_cache, v_cache, pos0=pos0,
@@ -196,5 +198,5 @@ class MulticastHeadShardedPrefill(HeadShardedPrefill):
         self.ctx.attn_multicast(self.prm, q_buf, k_cache, v_cache, self.mc, self.ld_o, self.q0,
                                 pos0=pos0, m_tokens=m_tokens, stream=stream)
         if self.world > 1:
-            dist.all_reduce(self.flag, group=self.group)  # every rank's rows have landed
+            self.comm.barrier(stream)  # every rank's rows have landed
         return self.out_full[:m_tokens]

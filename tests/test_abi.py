@@ -60,6 +60,24 @@ def test_context_without_gpu_fails_cleanly():
     assert st == 4 and not h.value  # P2P_ERR_CUDA, no context
 
 
+def test_communicator_host_side_without_gpu():
+    """NCCL is loaded at run time; its unique id needs no GPU; bad arguments are statuses."""
+    from p2p_b200 import lib
+    from p2p_b200.comm import unique_id
+    a, b = unique_id(), unique_id()
+    assert len(a) == 128 and a != b
+    h = C.c_void_p()
+    assert lib.p2p_comm_create(None, 2, 0, a, 1000, C.byref(h)) == 1
+    assert lib.p2p_comm_destroy(None) == 1
+    assert lib.p2p_comm_wait(None, None) == 1
+    assert lib.p2p_comm_barrier(None, None) == 1
+    assert lib.p2p_attn_prefill_sharded(None, None, None, None, 0, None, None, None, None, 0,
+                                        None, 0, 0, None, 0, None) == 1
+    deps = subprocess.run(["ldd", str(ROOT / "p2p_b200" / "libp2pattn.so")],
+                          capture_output=True, text=True).stdout
+    assert "libnccl" not in deps  # dlopen'ed when a communicator is first needed
+
+
 def test_product_library_does_not_link_the_oracle():
     import p2p_b200
     out = subprocess.run(["nm", "-D", str(p2p_b200.LIB_PATH)], capture_output=True, text=True,

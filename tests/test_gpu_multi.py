@@ -1,7 +1,8 @@
 """Multi-GPU paths on real GPUs (skipped with fewer than 2 visible GPUs).
 
 Two NCCL ranks, one process per GPU, rendezvous on 127.0.0.1:
-  * causal prefill split by KV-head group + all-gather vs the oracle on the full heads, and
+  * causal prefill split by KV-head group + all-gather (p2p_attn_prefill_sharded: NCCL inside
+    the library, through the C ABI) vs the oracle on the full heads, and
     the same with the flash kernel scattering its rows into every rank's output (CUDA IPC);
   * ragged decode split by sequence (LPT by tokens, no collective) vs the oracle.
 """
@@ -45,6 +46,7 @@ def _worker(rank, world, port, q):
         qkv = (0.5 * rng.standard_normal((m, (hq + 2 * hkv) * D))).astype(np.float16)
         nw = (1 + 0.1 * rng.standard_normal(2 * D)).astype(np.float16)
         rope = O.rope_table(m)
+        # the library's own communicator (NCCL inside libp2pattn.so), id shared over the group
         sp = HeadShardedPrefill(ctx, hq, hkv, world, rank)
         cols = sp.local_qkv_columns().numpy()
         dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
@@ -52,11 +54,9 @@ def _worker(rank, world, port, q):
         kc = torch.zeros((m, sp.kvn, D), dtype=torch.float16, device="cuda")
         vc = torch.zeros_like(kc)
         q_buf = torch.zeros((m, sp.qn * D), dtype=torch.float16, device="cuda")
-        out_l = torch.zeros_like(q_buf)
-        gather = torch.zeros((world * m, sp.qn * D), dtype=torch.float16, device="cuda")
         out = torch.zeros((m, hq * D), dtype=torch.float16, device="cuda")
-        sp(qkv_l, dev(nw), dev(rope), kc, vc, q_buf, out_l, gather, out, 0, m)
-        torch.cuda.synchronize()
+        sp(qkv_l, dev(nw), dev(rope), kc, vc, out, 0, m)
+        sp.comm.wait()
         # oracle on the full heads
         qo = np.zeros((m, hq * D), np.float16)
         ko = np.zeros((m, hkv, D), np.float16)
@@ -69,10 +69,16 @@ def _worker(rank, world, port, q):
         ok["prefill"] = bool((err <= 2e-3 + 1e-2 * np.abs(want.astype(np.float64))).all())
         ok["prefill_kv_slice"] = bool(np.array_equal(
             kc.cpu().numpy().view(np.uint16), ko[:, sp.kv0:sp.kv0 + sp.kvn].view(np.uint16)))
+        # a second chunk through the same communicator, positions 0..m-1 again, same result
+        out.zero_()
+        sp(qkv_l, dev(nw), dev(rope), kc, vc, out, 0, m)
+        sp.comm.wait()
+        ok["prefill_again"] = bool(np.array_equal(out.cpu().numpy(), got.astype(np.float16)))
+        comm = sp.comm
         # the same prefill with the flash kernel writing its rows into every rank's output
         # over NVLink (CUDA IPC mappings) instead of an all-gather; twice in a row
         from p2p_b200.sharding import ScatterHeadShardedPrefill
-        ssp = ScatterHeadShardedPrefill(ctx, hq, hkv, world, rank, max_tokens=m)
+        ssp = ScatterHeadShardedPrefill(ctx, hq, hkv, world, rank, max_tokens=m, comm=comm)
         for it in range(2):
             kc.zero_()
             vc.zero_()
@@ -85,7 +91,8 @@ def _worker(rank, world, port, q):
         # writes it into both ranks' outputs), where the node supports multicast
         from p2p_b200.sharding import MulticastHeadShardedPrefill
         try:
-            msp = MulticastHeadShardedPrefill(ctx, hq, hkv, world, rank, max_tokens=m)
+            msp = MulticastHeadShardedPrefill(ctx, hq, hkv, world, rank, max_tokens=m,
+                                              comm=comm)
         except RuntimeError:
             msp = None
         if msp is not None:
@@ -114,6 +121,7 @@ def _worker(rank, world, port, q):
         ctx.attn_decode_ragged(p2p_b200.Params(hq, hkv), dev(q2), None, None, dev(kc2), dev(vc2),
                                dev(offs), dev(pl), out2, max_past=int(past.max()),
                                fused_prep=False)
+        sp.close()
         g2 = out2.cpu().numpy().astype(np.float64)
         ok["ragged"] = bool((np.abs(g2 - want2) <= 2e-3 + 1e-2 * np.abs(want2.astype(np.float64))).all())
         ctx.close()
