@@ -572,9 +572,10 @@ def vision_oracle_check(q, k, v, out, images, what):
     from oracle import pyoracle as O
     want, got = [], []
     for b in images:
-        w = np.zeros((1024, 12 * D), np.float16)
-        O.vision_attn(12, D, q[b].cpu().numpy(), k[b].cpu().numpy(), v[b].cpu().numpy(), w)
-        want.append(w)
+        w = np.zeros((1, 1024, 12 * D), np.float16)
+        O.vision_attn(12, D, q[b:b + 1].cpu().numpy(), k[b:b + 1].cpu().numpy(),
+                      v[b:b + 1].cpu().numpy(), w)
+        want.append(w[0])
         got.append(out[b].cpu().numpy())
     return parity_stats(np.stack(got), np.stack(want), what)
 
