@@ -253,6 +253,46 @@ p2p_status p2p_attn_decode_ragged(p2p_ctx* ctx, const p2p_attn_params* prm, cons
                                   int32_t max_past, int32_t fused_prep, void* out, int64_t ld_o,
                                   void* stream);
 
+/* KV-cache formats beyond the engine's f16 token-major buffers, for the batched decode:
+ *   - int8 rows (the int8 cache of the reference bundle's GroupQueryAttention kernels,
+ *     public/kernels/megakernel.json: a value is stored as q = clamp(roundeven(x / scale),
+ *     -128, 127) and read as f32(q) * scale, with one f32 scale per tensor or one per
+ *     (kv head, dim) channel, index kh*D + d), which halves the bytes a decode step streams;
+ *   - paged caches (the bundle's PagedAttention layout): k_cache / v_cache are pools of
+ *     [kv_rows pages][block_size][Hkv][D] and key j of sequence i is row j % block_size of page
+ *     block_table[i * max_blocks + j / block_size].
+ * block_size 0 selects the contiguous form of p2p_attn_decode_ragged (offsets). */
+typedef enum p2p_kv_format { P2P_KV_F16 = 0, P2P_KV_I8 = 1 } p2p_kv_format;
+typedef struct p2p_kv_layout {
+  int32_t format;              /* p2p_kv_format */
+  const float* k_scale;        /* int8: scale_count f32 scales in device memory */
+  const float* v_scale;
+  int32_t scale_count;         /* 1 (per tensor) or Hkv*D (per channel) */
+  int32_t block_size;          /* 0: contiguous rows at offsets[i]; else tokens per page, a
+                                  power of two in 16..4096 */
+  const int32_t* block_table;  /* paged: device int32 [nseq][max_blocks] page indices */
+  int32_t max_blocks;
+} p2p_kv_layout;
+
+/* p2p_attn_decode_ragged over any of these formats: kv_rows counts the cache's rows
+ * (contiguous) or pages (paged); offsets is used by the contiguous form only.  With fused_prep
+ * the new token's k/v are appended in the cache's format (int8: quantised as above).  The
+ * kernel checks every sequence before touching it -- a negative entry, past[i] > max_past,
+ * rows beyond kv_rows, more pages than max_blocks or a block-table entry outside the pool --
+ * and skips it; p2p_sync then returns P2P_ERR_KV_FULL. */
+p2p_status p2p_attn_decode_kv(p2p_ctx* ctx, const p2p_attn_params* prm,
+                              const p2p_kv_layout* layout, const void* qkv, int64_t ld_qkv,
+                              const void* norm_w, const void* rope, void* k_cache,
+                              void* v_cache, int64_t kv_rows, const int32_t* offsets,
+                              const int32_t* past, int32_t nseq, int32_t max_past,
+                              int32_t fused_prep, void* out, int64_t ld_o, void* stream);
+
+/* Converts f16 cache rows [rows][Hkv][D] to the int8 format above (src 16-byte and dst 8-byte
+ * aligned; the same restated rule the decode uses when it appends). */
+p2p_status p2p_kv_quantize_q8(p2p_ctx* ctx, const void* src, void* dst, int64_t rows,
+                              int32_t num_kv_heads, const float* scale, int32_t scale_count,
+                              void* stream);
+
 /* vision-kernels.js:176-258 (VISION_ATTN, dispatched (NUM_HEADS, S) at vision.js:271-276),
  * batched: out[b] = softmax(scale * q[b] k[b]^T) v[b] per head, no mask, tcgen05 kernel.
  * q/k/v/out are [batch][s_tokens][ld] with head h at column h*D. */

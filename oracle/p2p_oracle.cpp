@@ -189,6 +189,63 @@ void attn(int hq, int hkv, int d, float scale, const typename P::T* q, int64_t l
 
 }  // namespace
 
+// The int8 KV cache of the reference bundle's GroupQueryAttention kernels
+// (public/kernels/megakernel.json, com.microsoft.GroupQueryAttention): gqa-present.wgsl.jinja
+// (bits == 8) appends q = i32(clamp(round(x / scale), QMIN = -128, QMAX = 127)) with WGSL's
+// round() (to nearest even) and scale = k_scale[perChannel ? hk*HEAD_DIM + d : 0];
+// attn-flash-decode-splitk.wgsl.jinja reads f32(q) * scale (load_key4 / load_value4).
+inline int8_t quantize_q8(float x, float scale) {
+  float q = std::nearbyint(x / scale);  // default rounding mode: to nearest even
+  q = std::fmin(std::fmax(q, -128.0f), 127.0f);
+  return static_cast<int8_t>(q);
+}
+
+// ATTN (kernels.js:268-319, the loop of attn_row) over an int8 cache: every key and value
+// element is dequantised to f32(q) * scale where the f16 shader converts f32(k).
+void attn_row_q8(int hkv, int d, int group, float scale, const uint16_t* qrow,
+                 const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
+                 int per_channel, int h, int64_t pos, uint16_t* orow) {
+  constexpr int CH = 128;
+  const int kh = h / group;
+  float qs[256];
+  float sc[CH];
+  std::vector<float> acc(d, 0.0f);
+  auto kscale = [&](int e) { return per_channel ? ks[kh * d + e] : ks[0]; };
+  auto vscale = [&](int e) { return per_channel ? vs[kh * d + e] : vs[0]; };
+  for (int e = 0; e < d; ++e) qs[e] = f16_to_f32(qrow[int64_t(h) * d + e]) * scale;
+  float rm = -3.0e38f;
+  float rl = 0.0f;
+  for (int64_t j0 = 0; j0 <= pos; j0 += CH) {
+    for (int t = 0; t < CH; ++t) {
+      const int64_t j = j0 + t;
+      float s = -3.0e38f;
+      if (j <= pos) {
+        float dot = 0.0f;
+        const int8_t* kr = kc + (j * hkv + kh) * d;
+        for (int e = 0; e < d; ++e) dot += qs[e] * (float(kr[e]) * kscale(e));
+        s = dot;
+      }
+      sc[t] = s;
+    }
+    float cm = -3.0e38f;
+    for (int t = 0; t < CH; ++t) cm = std::fmax(cm, sc[t]);
+    const float nm = std::fmax(rm, cm);
+    const float f = std::exp(rm - nm);
+    rl = rl * f;
+    for (int e = 0; e < d; ++e) acc[e] = acc[e] * f;
+    for (int t = 0; t < CH; ++t) {
+      const int64_t j2 = j0 + t;
+      if (j2 > pos) break;
+      const float p = std::exp(sc[t] - nm);
+      rl += p;
+      const int8_t* vr = vc + (j2 * hkv + kh) * d;
+      for (int e = 0; e < d; ++e) acc[e] += p * (float(vr[e]) * vscale(e));
+    }
+    rm = nm;
+  }
+  for (int e = 0; e < d; ++e) orow[int64_t(h) * d + e] = f32_to_f16(acc[e] / rl);
+}
+
 extern "C" {
 
 uint16_t p2p_or_f32_to_f16(float v) { return f32_to_f16(v); }
@@ -248,6 +305,29 @@ void p2p_or_attn_f(int hq, int hkv, int d, float scale, const float* q, int64_t 
                    const float* kc, const float* vc, float* out, int64_t ld_o, int pos0,
                    int m_tokens) {
   attn<Flt>(hq, hkv, d, scale, q, ld_q, kc, vc, out, ld_o, pos0, m_tokens);
+}
+
+void p2p_or_quantize_q8(const uint16_t* src, int8_t* dst, int64_t rows, int hkv, int d,
+                        const float* scale, int per_channel) {
+  const int64_t chan = int64_t(hkv) * d;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < chan; ++c)
+      dst[r * chan + c] = quantize_q8(f16_to_f32(src[r * chan + c]), per_channel ? scale[c] : scale[0]);
+}
+
+void p2p_or_attn_ragged_q8(int hq, int hkv, int d, float scale, const uint16_t* q, int64_t ld_q,
+                           const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
+                           int per_channel, const int64_t* offsets, const int32_t* past,
+                           int nseq, uint16_t* out, int64_t ld_o) {
+  const int group = hq / hkv;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+  for (int i = 0; i < nseq; ++i)
+    for (int h = 0; h < hq; ++h) {
+      const int64_t base = offsets[i] * hkv * d;
+      attn_row_q8(hkv, d, group, scale, q + int64_t(i) * ld_q, kc + base, vc + base, ks, vs,
+                  per_channel, h, past[i], out + int64_t(i) * ld_o);
+    }
 }
 
 void p2p_or_attn_ragged_h(int hq, int hkv, int d, float scale, const uint16_t* q, int64_t ld_q,

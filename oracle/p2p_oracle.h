@@ -79,6 +79,16 @@ void p2p_or_attn_ragged_h(int hq, int hkv, int d, float scale, const uint16_t* q
                           const uint16_t* kc, const uint16_t* vc, const int64_t* offsets,
                           const int32_t* past, int nseq, uint16_t* out, int64_t ld_o);
 
+/* The int8 KV cache (the reference bundle's GroupQueryAttention int8 cache: quantise
+ * clamp(roundeven(x / scale), -128, 127), dequantise f32(q) * scale, scale per tensor or per
+ * (kv head, dim) channel): conversion of f16 rows, and ATTN (kernels.js:268-319) per sequence
+ * over int8 cache slices, as p2p_or_attn_ragged_h. */
+void p2p_or_quantize_q8(const uint16_t* src, int8_t* dst, int64_t rows, int hkv, int d,
+                        const float* scale, int per_channel);
+void p2p_or_attn_ragged_q8(int hq, int hkv, int d, float scale, const uint16_t* q, int64_t ld_q,
+                           const int8_t* kc, const int8_t* vc, const float* ks, const float* vs,
+                           int per_channel, const int64_t* offsets, const int32_t* past,
+                           int nseq, uint16_t* out, int64_t ld_o);
 /* vision-kernels.js:176-258.  Bidirectional MHA over S tokens per image, 64-key chunks, first
  * chunk initialises the running max, out = f16(acc/sum).  q/k/v/out are [B][S][ld] with head
  * h at column h*D. */

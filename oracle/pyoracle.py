@@ -58,6 +58,9 @@ def lib():
         L.p2p_or_attn_f.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _i64, _i, _i]
         L.p2p_or_attn_ragged_h.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _p, _i, _p, _i64]
         L.p2p_or_vision_attn_h.argtypes = [_i, _i, _f, _i, _i, _p, _p, _p, _p, _i64]
+        L.p2p_or_quantize_q8.argtypes = [_p, _p, _i64, _i, _i, _p, _i]
+        L.p2p_or_attn_ragged_q8.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _p, _i, _p, _p,
+                                            _i, _p, _i64]
         L.p2p_or_attn_exact.argtypes = [_i, _i, _i, _d, _p, _i64, _p, _p, _p, _i64, _i, _i]
         L.p2p_or_argmax_h.argtypes = [_p, C.c_uint32, _p, _p, _p]
         L.p2p_or_set_threads.restype = _i
@@ -137,6 +140,37 @@ def attn_ragged(hq, hkv, d, q, kc, vc, offsets, past, out, scale=0.125):
     past = np.ascontiguousarray(past, dtype=np.int32)
     lib().p2p_or_attn_ragged_h(hq, hkv, d, scale, _ptr(q), q.shape[-1], _ptr(kc), _ptr(vc),
                                _ptr(offsets), _ptr(past), len(past), _ptr(out), out.shape[-1])
+
+
+def quantize_q8(src, scale):
+    """f16 cache rows [..., Hkv, D] -> int8 (the reference bundle's int8 cache rule)."""
+    src = np.ascontiguousarray(src, dtype=np.float16)
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    hkv, d = src.shape[-2], src.shape[-1]
+    rows = src.size // (hkv * d)
+    out = np.empty(src.shape, np.int8)
+    lib().p2p_or_quantize_q8(_ptr(src), _ptr(out), rows, hkv, d, _ptr(scale),
+                             int(scale.size > 1))
+    return out
+
+
+def attn_ragged_q8(hq, hkv, d, q, kc, vc, k_scale, v_scale, offsets, past, out, scale=0.125):
+    """ATTN per sequence over int8 cache slices (dequantised f32(q) * scale)."""
+    offsets = np.ascontiguousarray(offsets, dtype=np.int64)
+    past = np.ascontiguousarray(past, dtype=np.int32)
+    ks = np.ascontiguousarray(k_scale, dtype=np.float32)
+    vs = np.ascontiguousarray(v_scale, dtype=np.float32)
+    lib().p2p_or_attn_ragged_q8(hq, hkv, d, scale, _ptr(q), q.shape[-1], _ptr(kc), _ptr(vc),
+                                _ptr(ks), _ptr(vs), int(ks.size > 1), _ptr(offsets), _ptr(past),
+                                len(past), _ptr(out), out.shape[-1])
+
+
+def gather_pages(pages, block_table, n_tokens):
+    """The rows of one paged sequence in token order: pages [P][B][Hkv][D], block_table [nb]."""
+    bs = pages.shape[1]
+    nb = (n_tokens + bs - 1) // bs
+    rows = pages[np.asarray(block_table[:nb], np.int64)].reshape(nb * bs, *pages.shape[2:])
+    return np.ascontiguousarray(rows[:n_tokens])
 
 
 def vision_attn(nh, d, q, k, v, out, scale=0.125):

@@ -55,6 +55,22 @@ class AttnParams(C.Structure):
     ]
 
 
+class KvLayout(C.Structure):
+    _fields_ = [
+        ("format", C.c_int32),
+        ("k_scale", C.c_void_p),
+        ("v_scale", C.c_void_p),
+        ("scale_count", C.c_int32),
+        ("block_size", C.c_int32),
+        ("block_table", C.c_void_p),
+        ("max_blocks", C.c_int32),
+    ]
+
+
+P2P_KV_F16 = 0
+P2P_KV_I8 = 1
+
+
 class DecodeLayer(C.Structure):
     _fields_ = [
         ("qkv", C.c_void_p),
@@ -107,6 +123,10 @@ PROTOTYPES = {
     "p2p_shared_free": (_st, [_v, _v]),
     "p2p_shared_open": (_st, [_v, C.c_char_p, C.POINTER(_v)]),
     "p2p_shared_close": (_st, [_v, _v]),
+    "p2p_attn_decode_kv": (
+        _st, [_v, _pp, C.POINTER(KvLayout), _v, _i64, _v, _v, _v, _v, _i64, _v, _v, _i32, _i32,
+              _i32, _v, _i64, _v]),
+    "p2p_kv_quantize_q8": (_st, [_v, _v, _v, _i64, _i32, _v, _i32, _v]),
     "p2p_comm_unique_id": (_st, [C.c_char_p]),
     "p2p_comm_create": (_st, [_v, _i32, _i32, C.c_char_p, _i32, C.POINTER(_v)]),
     "p2p_comm_destroy": (_st, [_v]),

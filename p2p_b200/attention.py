@@ -224,6 +224,53 @@ class Context:
             rows, _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep),
             _ptr(out), out.stride(0), _stream(stream)))
 
+    def attn_decode_kv(self, prm: Params, qkv: torch.Tensor, norm_w, rope,
+                       k_cache: torch.Tensor, v_cache: torch.Tensor, past: torch.Tensor,
+                       out: torch.Tensor, *, max_past: int, offsets: Optional[torch.Tensor] = None,
+                       k_scale: Optional[torch.Tensor] = None,
+                       v_scale: Optional[torch.Tensor] = None,
+                       block_table: Optional[torch.Tensor] = None, fused_prep: bool = True,
+                       kv_rows: Optional[int] = None, stream=None):
+        """Batched decode over an int8 and/or paged KV cache (p2p_attn_decode_kv).
+
+        int8 caches (k_cache.dtype == torch.int8) take k_scale / v_scale (f32, 1 or Hkv*64
+        values).  Paged caches are [pages][block_size][Hkv][64] with block_table [nseq][max
+        blocks] (int32); contiguous ones [rows][Hkv][64] with offsets (int32)."""
+        assert past.dtype == torch.int32
+        q8 = k_cache.dtype == torch.int8
+        lay = _lib.KvLayout()
+        lay.format = _lib.P2P_KV_I8 if q8 else _lib.P2P_KV_F16
+        if q8:
+            assert k_scale is not None and v_scale is not None
+            assert k_scale.dtype == torch.float32 and v_scale.dtype == torch.float32
+            lay.k_scale, lay.v_scale = k_scale.data_ptr(), v_scale.data_ptr()
+            lay.scale_count = k_scale.numel()
+        if block_table is not None:
+            assert block_table.dtype == torch.int32 and k_cache.dim() == 4
+            lay.block_size = k_cache.shape[1]
+            lay.block_table = block_table.data_ptr()
+            lay.max_blocks = block_table.shape[1]
+        else:
+            assert offsets is not None and offsets.dtype == torch.int32
+        rows = k_cache.shape[0] if kv_rows is None else kv_rows
+        self._chk(lib.p2p_attn_decode_kv(
+            self.h, C.byref(prm.c()), C.byref(lay), _ptr(qkv), qkv.stride(0), _ptr(norm_w),
+            rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(k_cache), _ptr(v_cache),
+            rows, _ptr(offsets), _ptr(past), past.shape[0], max_past, int(fused_prep),
+            _ptr(out), out.stride(0), _stream(stream)))
+
+    def kv_quantize_q8(self, src: torch.Tensor, scale: torch.Tensor,
+                       dst: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """f16 cache rows [..., Hkv, 64] -> int8 (the decode's int8 cache format)."""
+        assert src.dtype == torch.float16 and scale.dtype == torch.float32
+        hkv = src.shape[-2]
+        rows = src.numel() // (hkv * HEAD_DIM)
+        if dst is None:
+            dst = torch.empty(src.shape, dtype=torch.int8, device=src.device)
+        self._chk(lib.p2p_kv_quantize_q8(self.h, _ptr(src), _ptr(dst), rows, hkv, _ptr(scale),
+                                         scale.numel(), _stream(stream)))
+        return dst
+
     def attn_prefill_sharded(self, comm, prm: Params, qkv_local: torch.Tensor, norm_w, rope,
                              k_cache: torch.Tensor, v_cache: torch.Tensor, out: torch.Tensor, *,
                              pos0: int = 0, m_tokens: Optional[int] = None,

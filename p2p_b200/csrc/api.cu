@@ -197,6 +197,16 @@ int forced_splits() {
   return v;
 }
 
+// Tuning knob: P2P_PDL=<0|1|2> sets when a decode launch lets the next kernel of its stream
+// start early (DecodeArgs::pdl); 0 turns programmatic dependent launch off.
+int pdl_mode() {
+  static const int v = [] {
+    const char* e = std::getenv("P2P_PDL");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
 // Tuning knob: P2P_DECODE_CLUSTER=0 makes decode steps use the workspace combine instead of
 // the thread-block-cluster combine.
 bool cluster_combine_enabled() {
@@ -217,13 +227,14 @@ p2p_status run_decode(p2p_ctx* ctx, const p2p_attn_params* prm, p2p::DecodeArgs&
   a.eps = eff_eps(prm);
   a.err = ctx->dev_err;
   a.wait_deficit = g_wait_deficit.load();
+  a.pdl = pdl_mode();
   int min_split = 16;
   int cluster = 0;
   int splits = 0;
   if (mode == p2p::kLayers && prm->dtype == P2P_F16 && cluster_combine_enabled()) {
     // Decode step over layers: the splits of one (layer, head chunk) form a cluster.
     cluster = forced_splits() > 0
-                  ? std::min(forced_splits(), 8)
+                  ? std::min(forced_splits(), 16)
                   : p2p::decode_cluster_splits(max_len, hkv, group, nz, fused, ctx->num_sms);
     if (cluster > 1) splits = cluster;
     else cluster = 0;
@@ -233,6 +244,12 @@ p2p_status run_decode(p2p_ctx* ctx, const p2p_attn_params* prm, p2p::DecodeArgs&
     if (forced_splits() > 0) {
       splits = forced_splits();
       min_split = 16;
+    }
+    if (mode == p2p::kPaged) {
+      // a split's block-table entries must fit the kernel's shared copy
+      const int64_t keys = (int64_t(p2p::kPagedTableCap - 3) << a.block_shift) - 16;
+      const int64_t need = (max_len + keys - 1) / keys;
+      if (splits < need) splits = int(need);
     }
     p2p_status st = ensure_workspace(ctx, p2p::decode_partials_bytes(splits, hkv, nz, group),
                                      p2p::decode_counters_bytes(hkv, nz), s);
@@ -861,6 +878,78 @@ p2p_status p2p_attn_decode_ragged(p2p_ctx* ctx, const p2p_attn_params* prm, cons
   DeviceGuard g(ctx->device);
   return run_decode(ctx, prm, a, p2p::kRagged, fused_prep != 0, nseq, int64_t(max_past) + 1,
                     pick_stream(ctx, stream));
+}
+
+p2p_status p2p_attn_decode_kv(p2p_ctx* ctx, const p2p_attn_params* prm,
+                              const p2p_kv_layout* lay, const void* qkv, int64_t ld_qkv,
+                              const void* norm_w, const void* rope, void* k_cache,
+                              void* v_cache, int64_t kv_rows, const int32_t* offsets,
+                              const int32_t* past, int32_t nseq, int32_t max_past,
+                              int32_t fused_prep, void* out, int64_t ld_o, void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  if (!lay) return fail(ctx, P2P_ERR_INVALID_ARG, "decode_kv: layout is NULL");
+  const bool paged = lay->block_size != 0;
+  // the contiguous form needs offsets; the paged one ignores them (checked as non-NULL below)
+  const int32_t* offs = paged ? past : offsets;
+  p2p_status st = p2p::check_ragged(ctx, prm, qkv, ld_qkv, rope, k_cache, v_cache, kv_rows, offs,
+                                    past, nseq, max_past, fused_prep, out, ld_o, "decode_kv");
+  if (st != P2P_OK) return st;
+  if (prm->dtype != P2P_F16)
+    return fail(ctx, P2P_ERR_UNSUPPORTED, "decode_kv: q/out must be f16");
+  if (lay->format != P2P_KV_F16 && lay->format != P2P_KV_I8)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_kv: format %d", lay->format);
+  const int chan = prm->num_kv_heads * prm->head_dim;
+  if (lay->format == P2P_KV_I8 &&
+      (!lay->k_scale || !lay->v_scale || (lay->scale_count != 1 && lay->scale_count != chan)))
+    return fail(ctx, P2P_ERR_INVALID_ARG,
+                "decode_kv: int8 caches need k/v scales, 1 or %d of them (got %d)", chan,
+                lay->scale_count);
+  int shift = 0;
+  if (paged) {
+    const int bs = lay->block_size;
+    if (bs < 16 || bs > 4096 || (bs & (bs - 1)) || !lay->block_table || lay->max_blocks <= 0)
+      return fail(ctx, P2P_ERR_INVALID_ARG,
+                  "decode_kv: block_size %d (a power of two in 16..4096), block table %p, "
+                  "max_blocks %d", bs, (const void*)lay->block_table, lay->max_blocks);
+    while ((1 << shift) < bs) ++shift;
+    if (int64_t(max_past) >= (int64_t(lay->max_blocks) << shift))
+      return fail(ctx, P2P_ERR_INVALID_ARG, "decode_kv: max_past %d beyond %d blocks of %d",
+                  max_past, lay->max_blocks, bs);
+  } else if (!offsets) {
+    return fail(ctx, P2P_ERR_INVALID_ARG, "decode_kv: contiguous caches need offsets");
+  }
+  if (nseq == 0) return P2P_OK;
+  p2p::DecodeArgs a{};
+  p2p::fill_ragged(a, qkv, ld_qkv, norm_w, rope, k_cache, v_cache, kv_rows, offsets, past,
+                   max_past, out, ld_o);
+  a.block_table = lay->block_table;
+  a.max_blocks = lay->max_blocks;
+  a.block_shift = shift;
+  a.kv_format = lay->format == P2P_KV_I8 ? p2p::kKvI8 : p2p::kKvF16;
+  a.k_scale = lay->k_scale;
+  a.v_scale = lay->v_scale;
+  a.scale_per_channel = lay->scale_count > 1 ? 1 : 0;
+  DeviceGuard g(ctx->device);
+  return run_decode(ctx, prm, a, paged ? p2p::kPaged : p2p::kRagged, fused_prep != 0, nseq,
+                    int64_t(max_past) + 1, pick_stream(ctx, stream));
+}
+
+p2p_status p2p_kv_quantize_q8(p2p_ctx* ctx, const void* src, void* dst, int64_t rows,
+                              int32_t num_kv_heads, const float* scale, int32_t scale_count,
+                              void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  if (!src || !dst || !scale || rows < 0 || num_kv_heads <= 0 ||
+      (scale_count != 1 && scale_count != num_kv_heads * 64))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "kv_quantize_q8: rows %lld kv heads %d scales %d",
+                (long long)rows, num_kv_heads, scale_count);
+  if (!aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7u))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "kv_quantize_q8: src must be 16-byte, dst 8-byte aligned");
+  if (rows == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  cudaError_t e = p2p::launch_quantize_q8(src, dst, rows, num_kv_heads, scale, scale_count,
+                                          pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "kv_quantize_q8 launch");
+  return P2P_OK;
 }
 
 p2p_status p2p_attn_bidir(p2p_ctx* ctx, const p2p_attn_params* prm, const void* q,

@@ -12,6 +12,18 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic-stream-serialization
+// attribute may start while the previous kernel of its stream still runs; grid_dependency_wait
+// returns once that kernel has completed and its memory operations are visible (immediately
+// when there is no such kernel), so it goes before the first global load or store.
+// launch_dependents lets the next kernel of the stream start early in the same way.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- storage types ------------------------------------------------------------------------
 // Every kernel reads/writes rows of 64 elements; a "chunk" is 8 consecutive elements
 // (16 bytes of f16 or 32 bytes of f32).

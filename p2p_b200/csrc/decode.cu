@@ -40,6 +40,7 @@
 #include <map>
 #include <mutex>
 #include <set>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -61,67 +62,103 @@ struct Ring {
 };
 
 // ---- per-sequence view ------------------------------------------------------------------------
-template <class T>
+// T: element of q / out / rope / norm weights; TC: element of the KV cache (T, or int8_t).
+template <class T, class TC>
 struct Seq {
   int past;
   const T* qrow;
   const T* nw;
-  T* kc;
-  T* vc;
+  TC* kc;  // kLayers / kRagged: the sequence's row 0; kPaged: the page pool
+  TC* vc;
   T* orow;
+  const int32_t* tbl;  // kPaged: the sequence's block-table row
 };
 
-template <class T, int MODE>
-__device__ __forceinline__ Seq<T> resolve(const DecodeArgs& a, int z) {
-  Seq<T> q;
+template <class T, class TC, int MODE>
+__device__ __forceinline__ Seq<T, TC> resolve(const DecodeArgs& a, int z) {
+  Seq<T, TC> q;
+  q.tbl = nullptr;
   if (MODE == kLayers) {
     const DecodeLayer& L = a.layers[z];
     q.past = a.meta ? int(a.meta[0]) : a.pos_host;
     q.qrow = static_cast<const T*>(L.qkv);
     q.nw = static_cast<const T*>(L.norm_w);
-    q.kc = static_cast<T*>(L.k_cache);
-    q.vc = static_cast<T*>(L.v_cache);
+    q.kc = static_cast<TC*>(L.k_cache);
+    q.vc = static_cast<TC*>(L.v_cache);
     q.orow = static_cast<T*>(L.out);
   } else {
     q.past = a.past[z];
     q.qrow = static_cast<const T*>(a.qkv) + int64_t(z) * a.ld_qkv;
     q.nw = static_cast<const T*>(a.norm_w);
-    const int64_t row0 = int64_t(a.offsets[z]) * a.hkv * kHeadDim;
-    q.kc = static_cast<T*>(a.k_cache) + row0;
-    q.vc = static_cast<T*>(a.v_cache) + row0;
+    const int64_t row0 = MODE == kPaged ? 0 : int64_t(a.offsets[z]) * a.hkv * kHeadDim;
+    q.kc = static_cast<TC*>(a.k_cache) + row0;
+    q.vc = static_cast<TC*>(a.v_cache) + row0;
     q.orow = static_cast<T*>(a.out) + int64_t(z) * a.ld_o;
+    if (MODE == kPaged) q.tbl = a.block_table + int64_t(z) * a.max_blocks;
   }
   return q;
 }
 
 // Whether sequence z must be refused before any of its rows is touched: a decode-step
-// position at or beyond the cache (kLayers), or a ragged entry that is negative, longer than
-// max_past (the rope table's bound) or reaching past the cache's kv_cap rows (kRagged).  One
-// CTA per sequence records the refusal in the device error word, which p2p_sync reports.
+// position at or beyond the cache (kLayers); a ragged entry that is negative, longer than
+// max_past (the rope table's bound) or reaching past the cache's kv_cap rows (kRagged); a
+// paged sequence with more pages than its block-table row holds or a block-table entry
+// outside the kv_cap pages (kPaged; every thread takes part, every CTA of the sequence reads
+// the same entries and decides alike).  One CTA per sequence records the refusal in the device
+// error word, which p2p_sync reports.
 template <int MODE>
 __device__ __forceinline__ bool refused(const DecodeArgs& a, int z) {
   bool bad;
   if (MODE == kLayers) {
     const int pos = a.meta ? int(a.meta[0]) : a.pos_host;
     bad = pos < 0 || int64_t(pos) >= a.kv_cap;
-  } else {
+  } else if (MODE == kRagged) {
     const int off = a.offsets[z], past = a.past[z];
     bad = off < 0 || past < 0 || past > a.max_past || int64_t(off) + past >= a.kv_cap;
+  } else {
+    const int past = a.past[z];
+    bad = past < 0 || past > a.max_past || (past >> a.block_shift) >= a.max_blocks;
+    if (!bad) {
+      const int32_t* tbl = a.block_table + int64_t(z) * a.max_blocks;
+      const int n = (past >> a.block_shift) + 1;
+      bool mine = false;
+      for (int b = threadIdx.x; b < n; b += blockDim.x) {
+        const int32_t pg = tbl[b];
+        mine |= pg < 0 || int64_t(pg) >= a.kv_cap;
+      }
+      bad = __syncthreads_or(mine) != 0;
+    }
   }
   if (bad && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
     atomicOr(a.err, kErrPosBeyondCache);
   return bad;
 }
 
+// int8 cache: the scale of (kv head kh, dim d) and the quantisation of one value,
+// q = clamp(roundeven(x / scale), -128, 127) (the GroupQueryAttention int8 cache append).
+__device__ __forceinline__ float kv_scale(const float* sc, int per_channel, int kh, int d) {
+  return per_channel ? sc[kh * kHeadDim + d] : sc[0];
+}
+__device__ __forceinline__ int8_t quantize_q8(float x, float scale) {
+  const float q = rintf(__fdiv_rn(x, scale));
+  return static_cast<int8_t>(fminf(fmaxf(q, -128.f), 127.f));
+}
+template <class TC>
+__device__ __forceinline__ float cache_f32(TC x) { return to_f32(x); }
+template <>
+__device__ __forceinline__ float cache_f32<int8_t>(int8_t x) { return float(x); }
+
 // Rotated query heads head0..head0+GC-1 into q_s (times `qscale`), and for the split that
 // holds the new token its normed/rotated k and raw v (QK_PREP's k and v units) into
-// knew_s/vnew_s and, by head chunk 0, into cache row `past`.  Unfused: q is read as given.
-template <class T, int GC, bool FUSED>
-__device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T>& sq, int kh, int hc,
-                                         int head0, bool has_new, float qscale,
-                                         float (*q_s)[kHeadDim], float* knew_s, float* vnew_s,
-                                         bool do_q = true) {
+// knew_s/vnew_s and, by head chunk 0, into cache row `new_row` (an int8 cache stores them
+// quantised, and knew_s/vnew_s then hold the quantised integers).  Unfused: q is read as given.
+template <class T, class TC, int GC, bool FUSED>
+__device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T, TC>& sq, int kh,
+                                         int hc, int head0, bool has_new, int64_t new_row,
+                                         float qscale, float (*q_s)[kHeadDim], float* knew_s,
+                                         float* vnew_s, bool do_q = true) {
   constexpr int D = kHeadDim;
+  constexpr bool kQ8 = sizeof(TC) == 1;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (FUSED) {
     const int64_t kv_stride = int64_t(a.hkv) * D;
@@ -137,30 +174,36 @@ __device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T>& sq, 
                           sq.nw != nullptr, a.eps, cs, sn, r0, r1);
         q_s[u][lane] = round_st<T>(r0) * qscale;
         q_s[u][lane + 32] = round_st<T>(r1) * qscale;
-      } else if (u == GC) {  // QK_PREP k unit -> cache row `past`
-        const int64_t off = int64_t(a.hq + kh) * D;
-        float r0, r1;
-        norm_rope_head<T>(to_f32(sq.qrow[off + lane]), to_f32(sq.qrow[off + lane + 32]),
-                          sq.nw ? sq.nw + D : nullptr, sq.nw != nullptr, a.eps, cs, sn, r0, r1);
-        const T k0 = from_f32<T>(r0), k1 = from_f32<T>(r1);
-        if (hc == 0) {
-          T* dst = sq.kc + int64_t(sq.past) * kv_stride + kh * D;
-          dst[lane] = k0;
-          dst[lane + 32] = k1;
-        }
-        knew_s[lane] = to_f32(k0);
-        knew_s[lane + 32] = to_f32(k1);
-      } else {  // QK_PREP v unit: raw copy -> cache row `past`
-        const int64_t off = int64_t(a.hq + a.hkv + kh) * D;
-        const T x0 = sq.qrow[off + lane], x1 = sq.qrow[off + lane + 32];
-        if (hc == 0) {
-          T* dst = sq.vc + int64_t(sq.past) * kv_stride + kh * D;
-          dst[lane] = x0;
-          dst[lane + 32] = x1;
-        }
-        vnew_s[lane] = to_f32(x0);
-        vnew_s[lane + 32] = to_f32(x1);
+        continue;
       }
+      // QK_PREP k unit (normed, rotated) or v unit (raw copy) -> cache row `new_row`
+      const bool is_k = u == GC;
+      const int64_t off = int64_t(a.hq + (is_k ? 0 : a.hkv) + kh) * D;
+      float x0 = to_f32(sq.qrow[off + lane]), x1 = to_f32(sq.qrow[off + lane + 32]);
+      if (is_k) {
+        float r0, r1;
+        norm_rope_head<T>(x0, x1, sq.nw ? sq.nw + D : nullptr, sq.nw != nullptr, a.eps, cs, sn,
+                          r0, r1);
+        x0 = round_st<T>(r0);
+        x1 = round_st<T>(r1);
+      }
+      TC c0, c1;
+      if constexpr (kQ8) {
+        const float* sc = is_k ? a.k_scale : a.v_scale;
+        c0 = quantize_q8(x0, kv_scale(sc, a.scale_per_channel, kh, lane));
+        c1 = quantize_q8(x1, kv_scale(sc, a.scale_per_channel, kh, lane + 32));
+      } else {
+        c0 = from_f32<TC>(x0);
+        c1 = from_f32<TC>(x1);
+      }
+      if (hc == 0) {
+        TC* dst = (is_k ? sq.kc : sq.vc) + new_row * kv_stride + kh * D;
+        dst[lane] = c0;
+        dst[lane + 32] = c1;
+      }
+      float* dst_s = is_k ? knew_s : vnew_s;
+      dst_s[lane] = cache_f32<TC>(c0);
+      dst_s[lane + 32] = cache_f32<TC>(c1);
     }
   } else if (do_q) {
     for (int i = tid; i < GC * D; i += kThreads)
@@ -229,10 +272,12 @@ __device__ __forceinline__ void finish(const DecodeArgs& a, T* out_h, int pair, 
 }
 
 // ---- cluster push-combine ---------------------------------------------------------------------
-constexpr int kMaxCluster = 8;
+constexpr int kMaxCluster = 16;         // non-portable sizes above 8: few (layer, head) rows
+constexpr int kPortableCluster = 8;
 constexpr int kPushStride = kHeadDim + 4;  // acc[64], max, sum, 2 pad: 17 16-byte chunks
 constexpr int kPushChunks = kPushStride / 4;
-constexpr int kRecvSlots = 8;  // ceil(GC / n) * n <= 8 for GC <= 4, n <= 8
+// receive slots of a cluster of up to `cl` CTAs: ceil(GC / n) * n <= cl for GC <= 4, n <= cl
+constexpr int recv_slots(int cl) { return cl > kPortableCluster ? kMaxCluster : kPortableCluster; }
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -351,27 +396,13 @@ __device__ __forceinline__ void finish_push(const DecodeArgs& a, T* out_h, int s
   for (int idx = tid; idx < owned * D; idx += kThreads) {
     const int h = idx / D, d = idx % D;
     const float(*src)[kPushStride] = recv_s + h * nsplit;
-    float m[kMaxCluster], l[kMaxCluster], ac[kMaxCluster];
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r) {
-      if (r < nsplit) {
-        m[r] = src[r][D];
-        l[r] = src[r][D + 1];
-        ac[r] = src[r][d];
-      }
-    }
-    float mx = kNegBig;
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r)
-      if (r < nsplit) mx = fmaxf(mx, m[r]);
+    float mx = kNegBig;  // the partials are read straight from shared memory (few registers)
+    for (int r = 0; r < nsplit; ++r) mx = fmaxf(mx, src[r][D]);
     float lt = 0.f, at = 0.f;
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r) {
-      if (r < nsplit) {
-        const float c = fast_exp2(m[r] - mx);
-        lt = fmaf(l[r], c, lt);
-        at = fmaf(ac[r], c, at);
-      }
+    for (int r = 0; r < nsplit; ++r) {
+      const float c = fast_exp2(src[r][D] - mx);
+      lt = fmaf(src[r][D + 1], c, lt);
+      at = fmaf(src[r][d], c, at);
     }
     out_h[(split + h * nsplit) * D + d] = from_f32<T>(at / lt);  // kernels.js:317
   }
@@ -412,16 +443,45 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return uint32_t(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-template <int G, bool FUSED, int MODE, bool CL>
+// int8 caches: per stage a K and a V tile of 64 rows x 64 bytes (row-contiguous), 6 stages,
+// then one f16 K and V tile pair (swizzled like the f16 ring) that each stage is converted
+// into before the MMAs read it.
+struct RingQ8 {
+  static constexpr int kStages = 6;
+  static constexpr int kTileBytes = kStageKeys * kHeadDim;
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kConvOff = kStages * kStageBytes;
+  static constexpr int kBytes = kConvOff + 2 * kStageKeys * kHeadDim * 2;
+};
+
+// Four int8 values (one 32-bit word, dims 4k..4k+3) -> two f16x2 words, exactly: the byte
+// x ^ 0x80 under the f16 pattern 0x64xx is 1024 + 128 + x; subtracting 1152 leaves x.
+__device__ __forceinline__ void s8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x = w ^ 0x80808080u;
+  uint32_t l = __byte_perm(x, 0x64646464u, 0x5140);
+  uint32_t h = __byte_perm(x, 0x64646464u, 0x7362);
+  const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
+  const __half2 lh = __hsub2(*reinterpret_cast<const __half2*>(&l), bias);
+  const __half2 hh = __hsub2(*reinterpret_cast<const __half2*>(&h), bias);
+  lo = *reinterpret_cast<const uint32_t*>(&lh);
+  hi = *reinterpret_cast<const uint32_t*>(&hh);
+}
+
+// CL: 0 (no cluster: workspace combine) or the largest cluster the instance serves (8 or 16;
+// the larger receive buffer of 16 would cost the 8-CTA form its third CTA per SM).
+template <int G, bool FUSED, int MODE, int CL, int KVF>
 __global__ void __launch_bounds__(kThreads, 3)
     decode_mma_kernel(const __grid_constant__ DecodeArgs a) {
   using T = __half;
+  constexpr bool kQ8 = KVF == kKvI8;
+  using TC = typename std::conditional<kQ8, int8_t, __half>::type;
+  constexpr bool kPg = MODE == kPaged;
   constexpr int D = kHeadDim;
   constexpr int GC = G > 4 ? 4 : G;
   constexpr int NHC = G / GC;
-  constexpr int kStages = Ring<T>::kStages;
-  constexpr int kTile = Ring<T>::kTileElems;
-  constexpr uint32_t kVOff = kStages * kTile * 2;  // byte offset of the V ring
+  constexpr int kStages = kQ8 ? RingQ8::kStages : Ring<T>::kStages;
+  constexpr int kTile = Ring<T>::kTileElems;       // f16 elements of one 64-key K (or V) tile
+  constexpr uint32_t kVOff = kStages * kTile * 2;  // f16 ring: byte offset of the V ring
   extern __shared__ __align__(128) unsigned char smem_raw[];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -429,11 +489,21 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int kh = blockIdx.y / NHC, hc = blockIdx.y % NHC;
   const int head0 = kh * G + hc * GC;
   const int ngrid = gridDim.x;
+  // Launched early behind the previous kernel of the stream (programmatic dependent launch):
+  // nothing of global memory is read or written before that kernel has completed.
+  grid_dependency_wait();
+  if (a.pdl == 1) launch_dependents();
   if (refused<MODE>(a, z)) return;  // rows beyond the cache: touch nothing
-  const Seq<T> sq = resolve<T, MODE>(a, z);
+  const Seq<T, TC> sq = resolve<T, TC, MODE>(a, z);
   const int len = sq.past + 1;  // keys 0..past, key `past` is the new token
   const int split_len = max(a.min_split, (ceil_div(len, ngrid) + 15) & ~15);
   const int nsplit = ceil_div(len, split_len);
+  if (kPg && (split_len >> a.block_shift) + 2 > kPagedTableCap) {
+    // a split longer than the block-table copy holds (the host sizes the grid so that this
+    // does not happen); the same for every CTA of the sequence, so none of them starts
+    if (tid == 0 && split == 0 && blockIdx.y == 0) atomicOr(a.err, kErrPosBeyondCache);
+    return;
+  }
   // A cluster CTA past the last split still takes part in the cluster barriers (empty range).
   if (!CL && split >= nsplit) return;
   const int j0 = min(split * split_len, len);
@@ -442,8 +512,25 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int jcopy = has_new ? sq.past : j1;  // rows streamed from the cache
   const int64_t kv_stride = int64_t(a.hkv) * D;
 
+  // paged: this split's block-table entries, pages j0 >> shift .. (j1 - 1) >> shift
+  __shared__ int32_t tbl_s[kPg ? kPagedTableCap : 1];
+  const int bshift = kPg ? a.block_shift : 0;
+  const int blk0 = kPg ? (j0 >> bshift) : 0;
+  if constexpr (kPg) {
+    const int nblk = j1 > j0 ? ((j1 - 1) >> bshift) - blk0 + 1 : 0;
+    for (int b = tid; b < nblk; b += kThreads) tbl_s[b] = sq.tbl[blk0 + b];
+    __syncthreads();
+  }
+  // cache row of key j of this split
+  auto row_of = [&](int j) -> int64_t {
+    if constexpr (kPg)
+      return (int64_t(tbl_s[(j >> bshift) - blk0]) << bshift) | int64_t(j & ((1 << bshift) - 1));
+    else
+      return int64_t(j);
+  };
+
   __shared__ __align__(16) float stage_s[CL ? GC : 1][kPushStride];
-  __shared__ __align__(16) float recv_s[CL ? kRecvSlots : 1][kPushStride];
+  __shared__ __align__(16) float recv_s[CL ? recv_slots(CL) : 1][kPushStride];
   __shared__ __align__(8) uint64_t recv_bar;
   __shared__ __align__(8) uint64_t q_bar;
   if constexpr (CL) {
@@ -461,22 +548,35 @@ __global__ void __launch_bounds__(kThreads, 3)
   __shared__ float red_acc[kWarps][GC][D];
   __shared__ int s_last;
 
-  const T* kbase = sq.kc + kh * D;
-  const T* vbase = sq.vc + kh * D;
+  const TC* kbase = sq.kc + kh * D;
+  const TC* vbase = sq.vc + kh * D;
   const int n_tiles = ceil_div(j1 - j0, kStageKeys);
   const uint32_t ring = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
   auto issue_tile = [&](int tile) {
     if (tile < n_tiles) {
-      const uint32_t off = (tile % kStages) * (kTile * 2);
       const int jt = j0 + tile * kStageKeys;
-      const int c = tid & 7;
+      if constexpr (kQ8) {  // 64-byte rows, four 16-byte pieces each, row-contiguous staging
+        const uint32_t st = (tile % kStages) * RingQ8::kStageBytes;
+        const int c = tid & 3;
 #pragma unroll
-      for (int i = 0; i < kStageKeys / 16; ++i) {
-        const int r = (tid >> 3) + 16 * i;
-        const bool ok = jt + r < jcopy;
-        const int64_t src = int64_t(ok ? jt + r : j0) * kv_stride + c * 8;
-        cp_async16(smem_raw + off + swz(r, c), kbase + src, ok);
-        cp_async16(smem_raw + kVOff + off + swz(r, c), vbase + src, ok);
+        for (int i = 0; i < kStageKeys / 32; ++i) {
+          const int r = (tid >> 2) + 32 * i;
+          const bool ok = jt + r < jcopy;
+          const int64_t src = row_of(ok ? jt + r : j0) * kv_stride + c * 16;
+          cp_async16(smem_raw + st + r * 64 + c * 16, kbase + src, ok);
+          cp_async16(smem_raw + st + RingQ8::kTileBytes + r * 64 + c * 16, vbase + src, ok);
+        }
+      } else {
+        const uint32_t off = (tile % kStages) * (kTile * 2);
+        const int c = tid & 7;
+#pragma unroll
+        for (int i = 0; i < kStageKeys / 16; ++i) {
+          const int r = (tid >> 3) + 16 * i;
+          const bool ok = jt + r < jcopy;
+          const int64_t src = row_of(ok ? jt + r : j0) * kv_stride + c * 8;
+          cp_async16(smem_raw + off + swz(r, c), kbase + src, ok);
+          cp_async16(smem_raw + kVOff + off + swz(r, c), vbase + src, ok);
+        }
       }
     }
     cp_async_commit();
@@ -488,9 +588,9 @@ __global__ void __launch_bounds__(kThreads, 3)
   // of a (layer, head chunk), so rank 0 alone reads them across the host link and rotates
   // them, and pushes the result into every peer's q_s (st.async, completing on the peer's
   // q_bar); the first K/V tiles are already in flight meanwhile.
-  const bool q_bcast = CL && a.q_bcast;
-  prologue<T, GC, FUSED>(a, sq, kh, hc, head0, has_new, 1.0f, q_s, knew_s, vnew_s,
-                         !q_bcast || split == 0);
+  const bool q_bcast = CL != 0 && a.q_bcast;
+  prologue<T, TC, GC, FUSED>(a, sq, kh, hc, head0, has_new, has_new ? row_of(sq.past) : 0,
+                             1.0f, q_s, knew_s, vnew_s, !q_bcast || split == 0);
   if (q_bcast) {
     cluster_wait();  // every rank's q_bar and recv_bar are initialised
     constexpr int kQChunks = GC * D * 4 / 16;  // 16-byte pieces of q_s
@@ -516,6 +616,16 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
   }
   __syncthreads();
+  // int8 cache: the key scales fold into q (one per channel) or into the score scale
+  float sl2 = a.scale_log2;
+  if constexpr (kQ8) {
+    if (a.scale_per_channel) {
+      for (int i = tid; i < GC * D; i += kThreads) q_s[i / D][i % D] *= a.k_scale[kh * D + i % D];
+      __syncthreads();
+    } else {
+      sl2 *= a.k_scale[0];
+    }
+  }
 
   // Q^T as the B operand (k = dims, n = heads): lane holds head n = lane/4 (zero when
   // n >= GC), dims 2(lane%4)+{0,1} and +8 of every 16-dim k-step.
@@ -536,24 +646,50 @@ __global__ void __launch_bounds__(kThreads, 3)
   float o[4][4];  // O^T tiles: dims 16i + gid (+8), heads 2*tig + {0,1}
 #pragma unroll
   for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  const float sl2 = a.scale_log2;
   const int mi = lane >> 3;
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     cp_async_wait<kStages - 2>();
     __syncthreads();  // tile landed for every thread; slot (tile-1) % kStages is free again
     issue_tile(tile + kStages - 1);
-    const uint32_t off = (tile % kStages) * (kTile * 2);
     const int jt = j0 + tile * kStageKeys;
+    // byte offsets (from smem_raw) of the f16 K and V tiles the MMAs read
+    uint32_t koff, voff;
+    if constexpr (kQ8) {
+      // int8 -> f16 (exact) into the conversion tiles, swizzled like the f16 ring
+      const uint32_t st = (tile % kStages) * RingQ8::kStageBytes;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int idx = tid + kThreads * q;  // 512 16-byte pieces: K tile, then V tile
+        const int which = idx >> 8, r = (idx >> 2) & 63, c = idx & 3;
+        const uint4 w = *reinterpret_cast<const uint4*>(smem_raw + st +
+                                                        which * RingQ8::kTileBytes + r * 64 +
+                                                        c * 16);
+        uint4 o0, o1;
+        s8x4_to_f16x4(w.x, o0.x, o0.y);
+        s8x4_to_f16x4(w.y, o0.z, o0.w);
+        s8x4_to_f16x4(w.z, o1.x, o1.y);
+        s8x4_to_f16x4(w.w, o1.z, o1.w);
+        unsigned char* dst = smem_raw + RingQ8::kConvOff + which * (kTile * 2);
+        *reinterpret_cast<uint4*>(dst + swz(r, 2 * c)) = o0;
+        *reinterpret_cast<uint4*>(dst + swz(r, 2 * c + 1)) = o1;
+      }
+      koff = RingQ8::kConvOff;
+      voff = RingQ8::kConvOff + kTile * 2;
+      __syncthreads();
+    } else {
+      koff = (tile % kStages) * (kTile * 2);
+      voff = kVOff + koff;
+    }
     if (FUSED && has_new && sq.past >= jt && sq.past < jt + kStageKeys) {
-      // the new token's k/v (computed in the prologue) replace the zero-filled ring row
+      // the new token's k/v (computed in the prologue) replace the zero-filled tile row
       const int r = sq.past - jt;
       if (tid < 16) {
         const int c = tid & 7;
         const float* src = (tid < 8 ? knew_s : vnew_s) + c * 8;
         const uint4 val = make_uint4(pack_h2(src[0], src[1]), pack_h2(src[2], src[3]),
                                      pack_h2(src[4], src[5]), pack_h2(src[6], src[7]));
-        *reinterpret_cast<uint4*>(smem_raw + (tid < 8 ? 0u : kVOff) + off + swz(r, c)) = val;
+        *reinterpret_cast<uint4*>(smem_raw + (tid < 8 ? koff : voff) + swz(r, c)) = val;
       }
       __syncthreads();
     }
@@ -565,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 3)
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t af[4];
-        ldsm_x4(ring + off + swz(r, kk * 2 + (mi >> 1)), af);
+        ldsm_x4(ring + koff + swz(r, kk * 2 + (mi >> 1)), af);
         mma16816(sacc, af, qb[kk][0], qb[kk][1]);
       }
     }
@@ -605,12 +741,24 @@ __global__ void __launch_bounds__(kThreads, 3)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t af[4];
-        ldsm_x4_trans(ring + kVOff + off + swz(r, 2 * i + (mi & 1)), af);
+        ldsm_x4_trans(ring + voff + swz(r, 2 * i + (mi & 1)), af);
         mma16816(o[i], af, pb0, pb1);
       }
     }
   }
   cp_async_wait<0>();
+  if (a.pdl == 2) launch_dependents();
+  if constexpr (kQ8) {  // the value scales, per output dim (16i + gid, 16i + gid + 8)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float s0 = kv_scale(a.v_scale, a.scale_per_channel, kh, 16 * i + gid);
+      const float s1 = kv_scale(a.v_scale, a.scale_per_channel, kh, 16 * i + gid + 8);
+      o[i][0] *= s0;
+      o[i][1] *= s0;
+      o[i][2] *= s1;
+      o[i][3] *= s1;
+    }
+  }
 
   // ---- warp totals: sum l over the 8 lanes that share a head column, then publish
 #pragma unroll
@@ -721,7 +869,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int head0 = kh * G + hc * GC;
   const int ngrid = gridDim.x;
   if (refused<MODE>(a, z)) return;
-  const Seq<T> sq = resolve<T, MODE>(a, z);
+  const Seq<T, T> sq = resolve<T, T, MODE>(a, z);
   const int len = sq.past + 1;
   const int split_len = max(a.min_split, (ceil_div(len, ngrid) + 15) & ~15);
   const int nsplit = ceil_div(len, split_len);
@@ -766,7 +914,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
   for (int t = 0; t < kStages - 1; ++t) issue_tile(t);
 
-  prologue<T, GC, FUSED>(a, sq, kh, hc, head0, has_new, a.scale_log2, q_s, knew_s, vnew_s);
+  prologue<T, T, GC, FUSED>(a, sq, kh, hc, head0, has_new, sq.past, a.scale_log2, q_s, knew_s,
+                            vnew_s);
   __syncthreads();
 
   float qr[GC][8];
@@ -862,10 +1011,10 @@ struct KernelInfo {
   int smem;
 };
 
-template <int G, bool FUSED, int MODE, bool CL>
+template <int G, bool FUSED, int MODE, int CL, int KVF>
 KernelInfo info_h() {
-  return {reinterpret_cast<const void*>(&decode_mma_kernel<G, FUSED, MODE, CL>),
-          Ring<__half>::kBytes};
+  return {reinterpret_cast<const void*>(&decode_mma_kernel<G, FUSED, MODE, CL, KVF>),
+          KVF == kKvI8 ? RingQ8::kBytes : Ring<__half>::kBytes};
 }
 template <int G, bool FUSED, int MODE>
 KernelInfo info_f() {
@@ -873,28 +1022,36 @@ KernelInfo info_f() {
           Ring<float>::kBytes};
 }
 
-template <int G>
-KernelInfo pick_fm(bool half, bool fused, int mode, bool cl) {
-  if (half) {
-    if (cl) {  // cluster combine: decode steps over layers only
-      if (mode != kLayers) return {nullptr, 0};
-      return fused ? info_h<G, true, kLayers, true>() : info_h<G, false, kLayers, true>();
-    }
-    if (mode == kLayers)
-      return fused ? info_h<G, true, kLayers, false>() : info_h<G, false, kLayers, false>();
-    return fused ? info_h<G, true, kRagged, false>() : info_h<G, false, kRagged, false>();
+template <int G, bool FUSED>
+KernelInfo pick_h(int mode, int cl, int kvf) {
+  if (cl) {  // cluster combine: decode steps over layers only (f16 caches)
+    if (mode != kLayers || kvf != kKvF16) return {nullptr, 0};
+    return cl > kPortableCluster ? info_h<G, FUSED, kLayers, kMaxCluster, kKvF16>()
+                                 : info_h<G, FUSED, kLayers, kPortableCluster, kKvF16>();
   }
-  if (cl) return {nullptr, 0};
+  if (mode == kLayers) return kvf == kKvF16 ? info_h<G, FUSED, kLayers, 0, kKvF16>()
+                                            : KernelInfo{nullptr, 0};
+  if (mode == kRagged) return kvf == kKvF16 ? info_h<G, FUSED, kRagged, 0, kKvF16>()
+                                            : info_h<G, FUSED, kRagged, 0, kKvI8>();
+  return kvf == kKvF16 ? info_h<G, FUSED, kPaged, 0, kKvF16>()
+                       : info_h<G, FUSED, kPaged, 0, kKvI8>();
+}
+
+template <int G>
+KernelInfo pick_fm(bool half, bool fused, int mode, int cl, int kvf) {
+  if (half) return fused ? pick_h<G, true>(mode, cl, kvf) : pick_h<G, false>(mode, cl, kvf);
+  if (cl || kvf != kKvF16 || mode == kPaged) return {nullptr, 0};
   if (mode == kLayers) return fused ? info_f<G, true, kLayers>() : info_f<G, false, kLayers>();
   return fused ? info_f<G, true, kRagged>() : info_f<G, false, kRagged>();
 }
 
-KernelInfo pick(int group, bool half, bool fused, int mode, bool cl) {
+// cl: 0 (workspace combine) or the cluster size
+KernelInfo pick(int group, bool half, bool fused, int mode, int cl, int kvf = kKvF16) {
   switch (group) {
-    case 1: return pick_fm<1>(half, fused, mode, cl);
-    case 2: return pick_fm<2>(half, fused, mode, cl);
-    case 4: return pick_fm<4>(half, fused, mode, cl);
-    case 8: return pick_fm<8>(half, fused, mode, cl);
+    case 1: return pick_fm<1>(half, fused, mode, cl, kvf);
+    case 2: return pick_fm<2>(half, fused, mode, cl, kvf);
+    case 4: return pick_fm<4>(half, fused, mode, cl, kvf);
+    case 8: return pick_fm<8>(half, fused, mode, cl, kvf);
     default: return {nullptr, 0};
   }
 }
@@ -987,12 +1144,16 @@ int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fuse
   int64_t c = slots / rows;
   const int64_t by_len = (max_len + 15) / 16;
   if (c > by_len) c = by_len;
-  if (c > kMaxCluster) c = kMaxCluster;
+  // Non-portable clusters (up to 16) only when portable ones would leave most SMs idle (one
+  // layer: 8 kv heads x 8 splits = 64 CTAs on 148 SMs); with more rows they schedule worse.
+  const int cap = int64_t(rows) * kPortableCluster * 2 <= num_sms ? kMaxCluster : kPortableCluster;
+  if (c > cap) c = cap;
   if (c < 2) return 1;
-  const KernelInfo k = pick(group, true, fused, kLayers, true);
-  if (!k.fn || configure(k, true) != cudaSuccess) return 1;
-  for (; c >= 2; --c)
+  for (; c >= 2; --c) {
+    const KernelInfo k = pick(group, true, fused, kLayers, int(c));
+    if (!k.fn || configure(k, true) != cudaSuccess) return 1;
     if (max_active_clusters(k, int(c)) >= rows) return int(c);
+  }
   return 1;
 }
 
@@ -1001,25 +1162,34 @@ cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, 
   const int group = a.hq / a.hkv;
   const bool cl = cluster > 1;
   if (cl && (cluster > kMaxCluster || cluster != max_splits)) return cudaErrorInvalidValue;
-  const KernelInfo k = pick(group, dtype == 0, fused, mode, cl);
+  const KernelInfo k = pick(group, dtype == 0, fused, mode, cl ? cluster : 0, a.kv_format);
   if (!k.fn) return cudaErrorInvalidValue;
   cudaError_t e = configure(k, cl);
   if (e != cudaSuccess) return e;
   dim3 grid(max_splits, a.hkv * head_chunks(group), nz);
   void* args[] = {const_cast<DecodeArgs*>(&a)};
-  if (!cl) return cudaLaunchKernel(k.fn, grid, dim3(kThreads), args, size_t(k.smem), s);
+  if (!cl && !a.pdl) return cudaLaunchKernel(k.fn, grid, dim3(kThreads), args, size_t(k.smem), s);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = size_t(k.smem);
   cfg.stream = s;
-  cudaLaunchAttribute at{};
-  at.id = cudaLaunchAttributeClusterDimension;
-  at.val.clusterDim.x = unsigned(cluster);
-  at.val.clusterDim.y = 1;
-  at.val.clusterDim.z = 1;
-  cfg.attrs = &at;
-  cfg.numAttrs = 1;
+  cudaLaunchAttribute at[2] = {};
+  int n_at = 0;
+  if (cl) {
+    at[n_at].id = cudaLaunchAttributeClusterDimension;
+    at[n_at].val.clusterDim.x = unsigned(cluster);
+    at[n_at].val.clusterDim.y = 1;
+    at[n_at].val.clusterDim.z = 1;
+    ++n_at;
+  }
+  if (a.pdl) {
+    at[n_at].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n_at].val.programmaticStreamSerializationAllowed = 1;
+    ++n_at;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = unsigned(n_at);
   return cudaLaunchKernelExC(&cfg, k.fn, args);
 }
 

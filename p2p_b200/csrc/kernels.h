@@ -43,9 +43,13 @@ struct DecodeLayer {
 // One work "sequence" per blockIdx.z.  Mode kLayers: z indexes layers[], every sequence has
 // the same past (meta[0] or pos_host).  Mode kRagged: z indexes sequences of one cache pair;
 // rows start at offsets[z], past = past_dev[z], q/out rows z*ld.
+// KV-cache storage of the ragged / paged decode: f16 rows, or int8 rows dequantised as
+// f32(q) * scale with one f32 scale per tensor or per (kv head, dim) channel.
+enum KvFormat { kKvF16 = 0, kKvI8 = 1 };
+
 struct DecodeArgs {
   DecodeLayer layers[kMaxLayers];
-  // ragged mode
+  // ragged / paged modes
   const void* qkv;
   int64_t ld_qkv;
   const void* norm_w;
@@ -54,6 +58,16 @@ struct DecodeArgs {
   const int32_t* offsets;
   const int32_t* past;
   int32_t max_past;      // a sequence with past > max_past is refused (the rope table's bound)
+  // paged mode: k_cache / v_cache hold kv_cap pages of (1 << block_shift) token rows; key j of
+  // sequence z lives in page block_table[z * max_blocks + (j >> block_shift)]
+  const int32_t* block_table;
+  int32_t max_blocks;
+  int32_t block_shift;
+  // int8 caches
+  int32_t kv_format;       // KvFormat
+  const float* k_scale;    // int8: 1 or hkv*64 scales (scale_per_channel)
+  const float* v_scale;
+  int32_t scale_per_channel;
   void* out;
   int64_t ld_o;
   // common
@@ -72,9 +86,17 @@ struct DecodeArgs {
   int32_t wait_deficit;  // test hook: extra bytes the cluster combine waits for (0 normally)
   int32_t q_bcast;       // cluster form: rank 0 alone reads the qkv rows (host memory) and
                          // hands the rotated q to its peers
+  int32_t pdl;           // programmatic dependent launch: 0 off; 1 let the next kernel of the
+                         // stream launch once every CTA has started, 2 once it has streamed
+                         // its keys (the next kernel still waits for this one to complete
+                         // before touching memory)
 };
 
-enum DecodeMode { kLayers = 0, kRagged = 1 };
+enum DecodeMode { kLayers = 0, kRagged = 1, kPaged = 2 };
+
+// Block-table entries a paged split keeps in shared memory (a split covers at most
+// (kPagedTableCap - 2) pages; the host sizes the grid so that it does).
+constexpr int kPagedTableCap = 1024;
 
 // grid = (max_splits, hkv, nz).  Workspace sizes in bytes for that grid.
 size_t decode_partials_bytes(int max_splits, int hkv, int nz, int group);
@@ -88,6 +110,12 @@ cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, 
 int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fused, int num_sms);
 // Choose the split count for a sequence of up to max_len keys.
 int decode_max_splits(int64_t max_len, int hkv, int nz, int num_sms, int* min_split);
+
+// ---- kv_quant.cu ----------------------------------------------------------------------------
+// f16 cache rows [rows][hkv][64] -> int8, q = clamp(roundeven(x / scale), -128, 127) with one
+// scale (scale_count 1) or one per (kv head, dim) channel (scale_count hkv*64).
+cudaError_t launch_quantize_q8(const void* src, void* dst, int64_t rows, int hkv,
+                               const float* scale, int scale_count, cudaStream_t s);
 
 // ---- prefill_sm100.cu ----------------------------------------------------------------------
 constexpr int kMaxFlashOuts = 8;  // output buffers one flash launch writes (one per rank)
