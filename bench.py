@@ -385,7 +385,14 @@ def lpt_shard(lengths, world):
     return lpt_partition([int(x) + 1 for x in lengths], world)
 
 
-def run_ragged(ctx, rank, world, steps, warmup, check=True):
+RAGGED_BLOCK = 64  # tokens per page of the paged leg
+
+
+def run_ragged(ctx, rank, world, steps, warmup, check=True, fmt="f16"):
+    """The 256-sequence batched decode (this rank's LPT share) with the KV cache in format
+    `fmt`: "f16" rows at per-sequence offsets (the engine's layout), "int8" rows with
+    per-channel scales (half the bytes), or "paged" f16 pages of RAGGED_BLOCK tokens in a
+    shuffled pool with a block table.  Returns (ms per step, algorithmic bytes, parity)."""
     import numpy as np
     import torch
     import p2p_b200
@@ -398,44 +405,84 @@ def run_ragged(ctx, rank, world, steps, warmup, check=True):
     total_rows = int(rows.sum())
     if total_rows >= 2**31:
         raise RuntimeError("ragged cache too large for int32 offsets")
-    g = torch.Generator(device="cuda").manual_seed(77 + rank)
-    kc = torch.randn((total_rows, HKV, D), generator=g, device="cuda", dtype=torch.float16)
-    vc = torch.randn((total_rows, HKV, D), generator=g, device="cuda", dtype=torch.float16)
     nseq = len(past)
+    max_past = int(past_all.max())
+    g = torch.Generator(device="cuda").manual_seed(77 + rank)
+    table = None
+    ks = vs = None
+    if fmt == "paged":
+        nblk = (rows + RAGGED_BLOCK - 1) // RAGGED_BLOCK
+        n_pages = int(nblk.sum())
+        perm = np.random.default_rng(5 + rank).permutation(n_pages).astype(np.int32)
+        table = np.full((nseq, int(nblk.max())), -1, np.int32)
+        start = np.concatenate([[0], np.cumsum(nblk)[:-1]])
+        for i in range(nseq):
+            table[i, :nblk[i]] = perm[start[i]:start[i] + nblk[i]]
+        shape = (n_pages, RAGGED_BLOCK, HKV, D)
+    else:
+        shape = (total_rows, HKV, D)
+    kc = torch.randn(shape, generator=g, device="cuda", dtype=torch.float16)
+    vc = torch.randn(shape, generator=g, device="cuda", dtype=torch.float16)
+    if fmt == "int8":
+        ks = (0.02 + 0.02 * torch.rand((HKV * D,), generator=g, device="cuda")).float()
+        vs = (0.02 + 0.02 * torch.rand((HKV * D,), generator=g, device="cuda")).float()
+        kc, vc = ctx.kv_quantize_q8(kc, ks), ctx.kv_quantize_q8(vc, vs)
+        torch.cuda.synchronize()
     qkv = torch.randn((nseq, (HQ + 2 * HKV) * D), generator=g, device="cuda",
                       dtype=torch.float16)
     nw = (1 + 0.1 * torch.randn((2 * D,), generator=g, device="cuda")).half()
     out = torch.zeros((nseq, HQ * D), device="cuda", dtype=torch.float16)
-    rope = ctx.rope_table(int(past_all.max()) + 1, D, 1e6)
+    rope = ctx.rope_table(max_past + 1, D, 1e6)
     off_d = torch.from_numpy(offsets.astype(np.int32)).cuda()
     past_d = torch.from_numpy(past).cuda()
+    tbl_d = torch.from_numpy(table).cuda() if table is not None else None
     prm = p2p_b200.Params(HQ, HKV)
 
     def step(i):
-        ctx.attn_decode_ragged(prm, qkv, nw, rope, kc, vc, off_d, past_d, out,
-                               max_past=int(past_all.max()), fused_prep=True)
+        if fmt == "f16":
+            ctx.attn_decode_ragged(prm, qkv, nw, rope, kc, vc, off_d, past_d, out,
+                                   max_past=max_past, fused_prep=True)
+        else:
+            ctx.attn_decode_kv(prm, qkv, nw, rope, kc, vc, past_d, out, max_past=max_past,
+                               offsets=off_d if fmt == "int8" else None, k_scale=ks,
+                               v_scale=vs, block_table=tbl_d, fused_prep=True)
 
     ms = timed_graph(step, steps, warmup, world)
-    my_bytes = float(rows.sum() * HKV * D * 2 * 2 + nseq * ((HQ + 2 * HKV) * D * 2 + 2 * HKV * D * 2
-                                                          + HQ * D * 2))
+    row_bytes = HKV * D * (1 if fmt == "int8" else 2)
+    my_bytes = float(rows.sum() * row_bytes * 2 + nseq * ((HQ + 2 * HKV) * D * 2
+                                                          + 2 * row_bytes + HQ * D * 2))
     if not check:
         del kc, vc
         torch.cuda.empty_cache()
         return ms, my_bytes, None
     # the checker: this rank's shortest, longest and two more sequences against the oracle
     from oracle import pyoracle as O
-    torch.cuda.synchronize()
+    ctx.sync()
     got = out.cpu().numpy()
-    rope_h = O.rope_table(int(past_all.max()) + 1)
+    rope_h = O.rope_table(max_past + 1)
     qkv_h, nw_h = qkv.cpu().numpy(), nw.cpu().numpy()
     sample = sorted({int(np.argmin(past)), int(np.argmax(past)), 0, nseq // 2})
     want = np.zeros((len(sample), HQ * D), np.float16)
     for j, i in enumerate(sample):
-        sl = slice(int(offsets[i]), int(offsets[i]) + int(past[i]) + 1)
-        k_i, v_i = kc[sl].cpu().numpy(), vc[sl].cpu().numpy()
+        n = int(past[i]) + 1
+        if fmt == "paged":  # the sequence's pages, gathered (the new k/v included)
+            k_i = O.gather_pages(kc[tbl_d[i].clamp(min=0).long()].cpu().numpy(),
+                                 np.arange(table.shape[1], dtype=np.int32), n)
+            v_i = O.gather_pages(vc[tbl_d[i].clamp(min=0).long()].cpu().numpy(),
+                                 np.arange(table.shape[1], dtype=np.int32), n)
+        else:
+            sl = slice(int(offsets[i]), int(offsets[i]) + n)
+            k_i, v_i = kc[sl].cpu().numpy(), vc[sl].cpu().numpy()
         q_o = np.zeros((1, HQ * D), np.float16)
-        O.qk_prep(HQ, HKV, D, qkv_h[i:i + 1], nw_h, rope_h, q_o, k_i, v_i, int(past[i]), 1)
-        O.attn(HQ, HKV, D, q_o, k_i, v_i, want[j:j + 1], int(past[i]), 1)
+        if fmt == "int8":  # q as QK_PREP rotates it; the int8 rows already hold the new k/v
+            k_scr = np.zeros((n, HKV, D), np.float16)
+            O.qk_prep(HQ, HKV, D, qkv_h[i:i + 1], nw_h, rope_h, q_o, k_scr, k_scr.copy(),
+                      n - 1, 1)
+            O.attn_ragged_q8(HQ, HKV, D, q_o, k_i, v_i, ks.cpu().numpy(), vs.cpu().numpy(),
+                             np.zeros(1, np.int64), past[i:i + 1], want[j:j + 1])
+        else:
+            O.qk_prep(HQ, HKV, D, qkv_h[i:i + 1], nw_h, rope_h, q_o, k_i, v_i, n - 1, 1)
+            O.attn(HQ, HKV, D, q_o, k_i, v_i, want[j:j + 1], n - 1, 1)
     par = parity_stats(got[sample], want, f"{len(sample)} sequences (shortest, longest, 2 more) "
                                           f"vs the oracle")
     del kc, vc
@@ -851,6 +898,24 @@ def main():
                 "parity": reduce_parity(r_par, world)}
         except p2p_b200.P2PError as e:
             side["ragged_decode"] = {"error": str(e)}
+        f16_ms = side.get("ragged_decode", {}).get("ms_per_step")
+        for fmt, what in (("int8", "int8 KV cache, per-channel f32 scales (half the bytes)"),
+                          ("paged", f"paged f16 KV cache, {RAGGED_BLOCK}-token pages in a "
+                                    f"shuffled pool + block table")):
+            try:
+                r_ms, r_bytes, r_par = run_ragged(ctx, rank, world, steps=10, warmup=3, fmt=fmt)
+                r_ms = max_over_ranks(r_ms, world)
+                r_bytes = sum_over_ranks(r_bytes, world)
+                side[f"ragged_decode_{fmt}"] = {
+                    "workload": f"the 256-sequence batched decode with an {what}",
+                    "gbs": round(r_bytes / (r_ms * 1e-3) / 1e9, 1),
+                    "ms_per_step": round(r_ms, 4), "bytes_per_step": int(r_bytes),
+                    "hbm_frac_per_gpu_of_measured":
+                        round(r_bytes / world / (r_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                    "speedup_vs_f16_rows": round(f16_ms / r_ms, 3) if f16_ms else None,
+                    "parity": reduce_parity(r_par, world)}
+            except p2p_b200.P2PError as e:
+                side[f"ragged_decode_{fmt}"] = {"error": str(e)}
         if world > 1:
             from p2p_b200.comm import Comm
             comm = Comm.from_process_group(ctx, world, rank)

@@ -293,6 +293,38 @@ p2p_status p2p_kv_quantize_q8(p2p_ctx* ctx, const void* src, void* dst, int64_t 
                               int32_t num_kv_heads, const float* scale, int32_t scale_count,
                               void* stream);
 
+/* The 4-bit projections on either side of the attention path, for one token (decode).  A
+ * matrix is ONNX MatMulNBits with bits 4, block 32 and zero points (kernels.js:4-9): qweight
+ * u32 [n][k/8] (value 8w+i of a row is nibble i of word w), scales f16 [n][k/32], zero_points
+ * bytes [n][ceil(k/32/2)] (low nibble = even block; 4-byte aligned, read as u32 words), value
+ * (q - zp) * scale.  k must be a multiple of 32 and at most 4608.  Every output is computed
+ * as the GEMV shader computes it (kernels.js:22-68), so the results are bit-identical to it. */
+typedef struct p2p_q4_matrix {
+  const void* qweight;
+  const void* scales;
+  const void* zero_points;
+  int32_t n;
+  int32_t k;
+} p2p_q4_matrix;
+
+/* kernels.js:22-68 (GEMV): y[y_off + n] = f16(x . W[n]) for one f16 row x [k] -- the o_proj
+ * that consumes the attention row (engine.js:224), or any other projection of the engine. */
+p2p_status p2p_gemv_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, void* y,
+                       int64_t y_off, void* stream);
+
+/* The q/k/v projections of one token (three GEMV dispatches, engine.js:202-204) with QK_PREP
+ * (kernels.js:216-266) in their epilogue: from the normed hidden row x [k], wq/wk/wv with
+ * Hq*64 / Hkv*64 / Hkv*64 rows produce the qkv row in f16 (never written to memory), whose
+ * heads are normed and rotated as QK_PREP does -- rotated q to q_out [Hq*64], rotated k and raw
+ * v to cache row pos (meta_dev[0] when meta_dev is not NULL).  Bit-identical to the GEMVs
+ * followed by QK_PREP.  A host position at or beyond kv_cap_tokens returns P2P_ERR_KV_FULL; a
+ * device one is refused by the kernel (nothing written) and reported by p2p_sync. */
+p2p_status p2p_qkv_gemv_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const void* x,
+                             const p2p_q4_matrix* wq, const p2p_q4_matrix* wk,
+                             const p2p_q4_matrix* wv, const void* norm_w, const void* rope,
+                             void* q_out, void* k_cache, void* v_cache, int64_t kv_cap_tokens,
+                             const uint32_t* meta_dev, int32_t pos, void* stream);
+
 /* vision-kernels.js:176-258 (VISION_ATTN, dispatched (NUM_HEADS, S) at vision.js:271-276),
  * batched: out[b] = softmax(scale * q[b] k[b]^T) v[b] per head, no mask, tcgen05 kernel.
  * q/k/v/out are [batch][s_tokens][ld] with head h at column h*D. */

@@ -307,6 +307,41 @@ void p2p_or_attn_f(int hq, int hkv, int d, float scale, const float* q, int64_t 
   attn<Flt>(hq, hkv, d, scale, q, ld_q, kc, vc, out, ld_o, pos0, m_tokens);
 }
 
+// kernels.js:22-68 (GEMV, ONNX MatMulNBits bits=4 block_size=32 with zero points,
+// kernels.js:4-9): y[y_off + n] = f16(sum_k x[k] * W[n][k]).  Row n is one workgroup
+// subgroup of 32 lanes: lane l walks words w = l, l+32, ... of the row (8 nibbles each,
+// element 8w+i is nibble i), a = sum_i f32(x[8w+i]) * (q_i - zp) in order, acc += a * scale,
+// then the shader's shared-memory tree over the 32 lanes (red[l] += red[l+s], s = 16..1).
+void p2p_or_gemv_q4(int k, int n_rows, const uint16_t* x, const uint32_t* wq, const uint16_t* sc,
+                    const uint32_t* zp, uint16_t* y, int64_t y_off) {
+  const int nb = k / 32, zr = (nb + 1) / 2, wpr = k / 8;
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < n_rows; ++n) {
+    float red[32];
+    for (int lane = 0; lane < 32; ++lane) {
+      float acc = 0.0f;
+      for (int w = lane; w < wpr; w += 32) {  // kernels.js:46-59
+        const uint32_t word = wq[int64_t(n) * wpr + w];
+        const int blk = w >> 2;
+        const float s = f16_to_f32(sc[int64_t(n) * nb + blk]);
+        const int64_t zi = int64_t(n) * zr + (blk >> 1);
+        const uint32_t zb = (zp[zi >> 2] >> ((zi & 3) * 8)) & 255u;     // kernels.js:16-19
+        const float z = float((zb >> ((blk & 1) * 4)) & 15u);
+        float a = 0.0f;
+        for (int i = 0; i < 8; ++i) {
+          const float q = float((word >> (i * 4)) & 15u);
+          a += f16_to_f32(x[w * 8 + i]) * (q - z);
+        }
+        acc += a * s;
+      }
+      red[lane] = acc;
+    }
+    for (int s = 16; s > 0; s >>= 1)  // kernels.js:61-65
+      for (int l = 0; l < s; ++l) red[l] += red[l + s];
+    y[y_off + n] = f32_to_f16(red[0]);  // kernels.js:66
+  }
+}
+
 void p2p_or_quantize_q8(const uint16_t* src, int8_t* dst, int64_t rows, int hkv, int d,
                         const float* scale, int per_channel) {
   const int64_t chan = int64_t(hkv) * d;

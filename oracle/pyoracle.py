@@ -59,6 +59,7 @@ def lib():
         L.p2p_or_attn_ragged_h.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _p, _i, _p, _i64]
         L.p2p_or_vision_attn_h.argtypes = [_i, _i, _f, _i, _i, _p, _p, _p, _p, _i64]
         L.p2p_or_quantize_q8.argtypes = [_p, _p, _i64, _i, _i, _p, _i]
+        L.p2p_or_gemv_q4.argtypes = [_i, _i, _p, _p, _p, _p, _p, _i64]
         L.p2p_or_attn_ragged_q8.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _p, _i, _p, _p,
                                             _i, _p, _i64]
         L.p2p_or_attn_exact.argtypes = [_i, _i, _i, _d, _p, _i64, _p, _p, _p, _i64, _i, _i]
@@ -81,7 +82,7 @@ def ref():
         if not path.exists():
             raise FileNotFoundError(f"{path} not built (needs the reference sources)")
         L = C.CDLL(str(path))
-        for name in ("QK_PREP", "ATTN", "VISION_ATTN", "ARGMAX"):
+        for name in ("QK_PREP", "ATTN", "VISION_ATTN", "ARGMAX", "GEMV"):
             fn = getattr(L, f"ref_{name}")
             fn.restype = _i
             fn.argtypes = [_p, _p, C.c_uint32, C.c_uint32, C.c_uint32]
@@ -140,6 +141,38 @@ def attn_ragged(hq, hkv, d, q, kc, vc, offsets, past, out, scale=0.125):
     past = np.ascontiguousarray(past, dtype=np.int32)
     lib().p2p_or_attn_ragged_h(hq, hkv, d, scale, _ptr(q), q.shape[-1], _ptr(kc), _ptr(vc),
                                _ptr(offsets), _ptr(past), len(past), _ptr(out), out.shape[-1])
+
+
+def gemv_q4(x, wq, sc, zp, y=None, y_off=0):
+    """kernels.js:22-68: y[y_off + n] = f16(x . W[n]) for the 4-bit matrix (wq u32 [N][K/8],
+    sc f16 [N][K/32], zp u8 bytes packed in u32 words).  Returns y (float16)."""
+    x = np.ascontiguousarray(x, dtype=np.float16).reshape(-1)
+    n, wpr = wq.shape
+    if y is None:
+        y = np.zeros(y_off + n, np.float16)
+    lib().p2p_or_gemv_q4(x.size, n, _ptr(x), _ptr(np.ascontiguousarray(wq, np.uint32)),
+                         _ptr(np.ascontiguousarray(sc, np.float16)),
+                         _ptr(np.ascontiguousarray(zp, np.uint32)), _ptr(y), y_off)
+    return y
+
+
+def ref_gemv(x, wq, sc, zp, y, y_off=0):
+    """The reference's own GEMV shader (oracle/_ref), dispatched as engine.js does: N/8
+    workgroups of 256."""
+    n = wq.shape[0]
+    ovr = (C.c_double * 3)(x.size, n, y_off)
+    rc = ref().ref_GEMV(_bind(x, wq, sc, zp, y), ovr, (n + 7) // 8, 1, 1)
+    if rc:
+        raise RuntimeError(f"ref_GEMV failed ({rc})")
+
+
+def random_q4(rng, n, k):
+    """A random 4-bit matrix in the reference layout: (wq, scales, zero-point words)."""
+    wq = rng.integers(0, 2**32, (n, k // 8), dtype=np.uint64).astype(np.uint32)
+    sc = (0.01 + 0.02 * rng.random((n, k // 32))).astype(np.float16)
+    zr = (k // 32 + 1) // 2
+    zbytes = rng.integers(0, 256, n * zr + (-(n * zr)) % 4, dtype=np.uint64).astype(np.uint8)
+    return wq, sc, zbytes.view(np.uint32)
 
 
 def quantize_q8(src, scale):

@@ -27,6 +27,7 @@ SHADERS = [
     ("src/scripts/lfm-engine/kernels.js", "ATTN"),
     ("src/scripts/lfm-engine/vision-kernels.js", "VISION_ATTN"),
     ("src/scripts/lfm-engine/kernels.js", "ARGMAX"),
+    ("src/scripts/lfm-engine/kernels.js", "GEMV"),
 ]
 
 TYPES = {"f32": "float", "f16": "wgsl::h16", "u32": "uint32_t", "i32": "int32_t"}
@@ -39,8 +40,15 @@ def extract(src: str, name: str) -> str:
     if not m:
         raise SystemExit(f"shader {name} not found")
     body = m.group(1)
-    if "${" in body:
-        raise SystemExit(f"shader {name} interpolates other snippets; not supported")
+
+    # snippets the shader interpolates (e.g. the GEMV's ${ZP_FN}) are module constants
+    def snippet(sm):
+        c = re.search(r"const " + sm.group(1) + r" = `(.*?)`;", src, re.S)
+        if not c or "${" in c.group(1):
+            raise SystemExit(f"shader {name}: snippet {sm.group(1)} not found or nested")
+        return c.group(1)
+
+    body = re.sub(r"\$\{(\w+)\}", snippet, body)
     return body
 
 
@@ -65,7 +73,9 @@ def translate(name: str, wgsl: str) -> str:
     wg_size = None
     params = {}
     body: list[str] = []
+    helpers: list[str] = []
     in_main = False
+    in_fn = False
     for raw in wgsl.splitlines():
         line = raw.strip()
         if not line or line.startswith("enable "):
@@ -73,8 +83,27 @@ def translate(name: str, wgsl: str) -> str:
         if in_main:
             body.append(translate_expr(raw))
             continue
+        if in_fn:  # a helper function's body, up to its closing brace at column 0
+            helpers.append(translate_expr(raw))
+            if raw.startswith("}"):
+                in_fn = False
+            continue
+        if m := re.match(r"fn (\w+)\((.*)\)\s*->\s*(\w+)\s*\{", line):
+            if m.group(1) != "main":
+                args = []
+                for a in m.group(2).split(","):
+                    am = re.match(r"\s*(\w+)\s*:\s*(\w+)\s*$", a)
+                    if not am:
+                        raise SystemExit(f"{name}: unsupported helper parameter {a!r}")
+                    args.append(f"{TYPES[am.group(2)]} {am.group(1)}")
+                helpers.append(f"static {TYPES[m.group(3)]} {m.group(1)}({', '.join(args)}) {{")
+                in_fn = True
+                continue
         if m := re.match(r"override (\w+): (\w+) = ([^;]+);", line):
             overrides.append((m.group(1), TYPES[m.group(2)], translate_expr(m.group(3))))
+            continue
+        if m := re.match(r"override (\w+): (\w+);", line):  # no default: set by the runner
+            overrides.append((m.group(1), TYPES[m.group(2)], "0"))
             continue
         if m := re.match(r"@group\(0\) @binding\((\d+)\) var<storage, (\w+)> (\w+): array<(\w+)>;", line):
             bindings[int(m.group(1))] = (m.group(3), TYPES[m.group(4)], m.group(2))
@@ -113,6 +142,7 @@ def translate(name: str, wgsl: str) -> str:
         out.append(f"static {btype}* {bname} = nullptr;  // binding {idx} ({access})")
     for vname, vtype, vlen in wgvars:
         out.append(f"static thread_local {vtype} {vname}[{vlen}];")
+    out.extend(helpers)
     wid = params.get("workgroup_id", "wid_unused")
     lid = params.get("local_invocation_index", "lid_unused")
     out.append(f"static wgsl::Task main_(wgsl::uvec3 {wid}, uint32_t {lid}) {{")

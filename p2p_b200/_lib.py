@@ -67,6 +67,16 @@ class KvLayout(C.Structure):
     ]
 
 
+class Q4Matrix(C.Structure):
+    _fields_ = [
+        ("qweight", C.c_void_p),
+        ("scales", C.c_void_p),
+        ("zero_points", C.c_void_p),
+        ("n", C.c_int32),
+        ("k", C.c_int32),
+    ]
+
+
 P2P_KV_F16 = 0
 P2P_KV_I8 = 1
 
@@ -127,6 +137,10 @@ PROTOTYPES = {
         _st, [_v, _pp, C.POINTER(KvLayout), _v, _i64, _v, _v, _v, _v, _i64, _v, _v, _i32, _i32,
               _i32, _v, _i64, _v]),
     "p2p_kv_quantize_q8": (_st, [_v, _v, _v, _i64, _i32, _v, _i32, _v]),
+    "p2p_gemv_q4": (_st, [_v, C.POINTER(Q4Matrix), _v, _v, _i64, _v]),
+    "p2p_qkv_gemv_prep": (
+        _st, [_v, _pp, _v, C.POINTER(Q4Matrix), C.POINTER(Q4Matrix), C.POINTER(Q4Matrix), _v,
+              _v, _v, _v, _v, _i64, _v, _i32, _v]),
     "p2p_comm_unique_id": (_st, [C.c_char_p]),
     "p2p_comm_create": (_st, [_v, _i32, _i32, C.c_char_p, _i32, C.POINTER(_v)]),
     "p2p_comm_destroy": (_st, [_v]),

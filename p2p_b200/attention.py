@@ -271,6 +271,30 @@ class Context:
                                          scale.numel(), _stream(stream)))
         return dst
 
+    @staticmethod
+    def q4(w) -> "_lib.Q4Matrix":
+        """(qweight u32 [n][k/8], scales f16 [n][k/32], zero_points u32 words) -> the C view."""
+        qw, sc, zp = w
+        return _lib.Q4Matrix(qw.data_ptr(), sc.data_ptr(), zp.data_ptr(), qw.shape[0],
+                             qw.shape[1] * 8)
+
+    def gemv_q4(self, w, x: torch.Tensor, y: torch.Tensor, y_off: int = 0, stream=None):
+        """kernels.js:22-68: y[y_off + n] = f16(x . W[n]) for one token (e.g. o_proj)."""
+        m = self.q4(w)
+        self._chk(lib.p2p_gemv_q4(self.h, C.byref(m), _ptr(x), _ptr(y), y_off, _stream(stream)))
+
+    def qkv_gemv_prep(self, prm: Params, x: torch.Tensor, wq, wk, wv, norm_w, rope,
+                      q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+                      pos: int = 0, use_meta: bool = False, stream=None):
+        """q/k/v projections of one token with QK_PREP in the epilogue (rotated q to q_out,
+        k/v to cache row pos)."""
+        mq, mk, mv = self.q4(wq), self.q4(wk), self.q4(wv)
+        self._chk(lib.p2p_qkv_gemv_prep(
+            self.h, C.byref(prm.c()), _ptr(x), C.byref(mq), C.byref(mk), C.byref(mv),
+            _ptr(norm_w), rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(q_out),
+            _ptr(k_cache), _ptr(v_cache), k_cache.shape[0], self.meta_ptr if use_meta else None,
+            pos, _stream(stream)))
+
     def attn_prefill_sharded(self, comm, prm: Params, qkv_local: torch.Tensor, norm_w, rope,
                              k_cache: torch.Tensor, v_cache: torch.Tensor, out: torch.Tensor, *,
                              pos0: int = 0, m_tokens: Optional[int] = None,

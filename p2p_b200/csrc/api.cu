@@ -934,6 +934,70 @@ p2p_status p2p_attn_decode_kv(p2p_ctx* ctx, const p2p_attn_params* prm,
                     int64_t(max_past) + 1, pick_stream(ctx, stream));
 }
 
+namespace {
+// Validation of one MatMulNBits matrix argument: rows, k, alignment of its three buffers.
+p2p_status check_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, int32_t n, int32_t k,
+                    const char* what) {
+  if (!w || !w->qweight || !w->scales || !w->zero_points)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "%s: NULL matrix or buffer", what);
+  if ((n >= 0 && w->n != n) || w->n <= 0 || w->k != k || k <= 0 || k % 32 ||
+      k > p2p::kGemvMaxK)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "%s: n %d (want %d), k %d (want %d; a multiple of "
+                "32, at most %d)", what, w->n, n, w->k, k, p2p::kGemvMaxK);
+  if ((reinterpret_cast<uintptr_t>(w->qweight) | reinterpret_cast<uintptr_t>(w->zero_points)) &
+          3u ||
+      reinterpret_cast<uintptr_t>(w->scales) & 1u)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "%s: qweight / zero_points must be 4-byte aligned, "
+                "scales 2-byte", what);
+  return P2P_OK;
+}
+p2p::Q4Matrix to_q4(const p2p_q4_matrix* w) {
+  return {static_cast<const uint32_t*>(w->qweight), static_cast<const __half*>(w->scales),
+          static_cast<const uint32_t*>(w->zero_points), w->n};
+}
+}  // namespace
+
+p2p_status p2p_gemv_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, void* y,
+                       int64_t y_off, void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  p2p_status st = check_q4(ctx, w, -1, w ? w->k : 0, "gemv_q4");
+  if (st != P2P_OK) return st;
+  if (!x || !y || !aligned16(x) || y_off < 0 || (reinterpret_cast<uintptr_t>(y) & 1u))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "gemv_q4: x must be 16-byte aligned, y non-NULL");
+  DeviceGuard g(ctx->device);
+  p2p::GemvArgs a{to_q4(w), w->k, x, y, y_off};
+  cudaError_t e = p2p::launch_gemv_q4(a, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "gemv_q4 launch");
+  return P2P_OK;
+}
+
+p2p_status p2p_qkv_gemv_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const void* x,
+                             const p2p_q4_matrix* wq, const p2p_q4_matrix* wk,
+                             const p2p_q4_matrix* wv, const void* norm_w, const void* rope,
+                             void* q_out, void* k_cache, void* v_cache, int64_t kv_cap_tokens,
+                             const uint32_t* meta_dev, int32_t pos, void* stream) {
+  p2p_status st = check_params(ctx, prm, false);
+  if (st != P2P_OK) return st;
+  const int k = wq ? wq->k : 0;
+  const int qn = prm->num_heads * prm->head_dim, kn = prm->num_kv_heads * prm->head_dim;
+  if ((st = check_q4(ctx, wq, qn, k, "qkv_gemv_prep (wq)")) != P2P_OK) return st;
+  if ((st = check_q4(ctx, wk, kn, k, "qkv_gemv_prep (wk)")) != P2P_OK) return st;
+  if ((st = check_q4(ctx, wv, kn, k, "qkv_gemv_prep (wv)")) != P2P_OK) return st;
+  if (!x || !aligned16(x) || !rope || !q_out || !k_cache || !v_cache || kv_cap_tokens <= 0 ||
+      (!meta_dev && pos < 0))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "qkv_gemv_prep: NULL or misaligned buffer, cap or pos");
+  if (!meta_dev && int64_t(pos) >= kv_cap_tokens)
+    return fail(ctx, P2P_ERR_KV_FULL, "qkv_gemv_prep: pos %d >= cache rows %lld", pos,
+                (long long)kv_cap_tokens);
+  DeviceGuard g(ctx->device);
+  p2p::QkvPrepArgs a{to_q4(wq), to_q4(wk), to_q4(wv), k, x, norm_w, rope, q_out, k_cache,
+                     v_cache, kv_cap_tokens, meta_dev, pos, prm->num_heads, prm->num_kv_heads,
+                     eff_eps(prm), ctx->dev_err};
+  cudaError_t e = p2p::launch_qkv_prep(a, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemv_prep launch");
+  return P2P_OK;
+}
+
 p2p_status p2p_kv_quantize_q8(p2p_ctx* ctx, const void* src, void* dst, int64_t rows,
                               int32_t num_kv_heads, const float* scale, int32_t scale_count,
                               void* stream) {

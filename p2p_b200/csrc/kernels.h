@@ -1,6 +1,7 @@
 // kernels.h -- host-side launchers of the sm_100a kernels (internal to libp2pattn.so).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -110,6 +111,41 @@ cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, 
 int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fused, int num_sms);
 // Choose the split count for a sequence of up to max_len keys.
 int decode_max_splits(int64_t max_len, int hkv, int nz, int num_sms, int* min_split);
+
+// ---- gemv_q4.cu -----------------------------------------------------------------------------
+// A MatMulNBits matrix (bits 4, block 32, zero points): n rows of k values.
+struct Q4Matrix {
+  const uint32_t* qweight;      // [n][k/8], value 8w+i of a row is nibble i of word w
+  const __half* scales;         // [n][k/32]
+  const uint32_t* zero_points;  // bytes [n][ceil(k/32/2)] (low nibble: even block), as words
+  int32_t n;
+};
+constexpr int kGemvMaxK = 4608;  // the GEMV shader's workgroup copy of x (kernels.js:31)
+struct GemvArgs {
+  Q4Matrix w;
+  int32_t k;
+  const void* x;  // f16 [k]
+  void* y;        // f16, rows at y_off..y_off+n-1
+  int64_t y_off;
+};
+struct QkvPrepArgs {
+  Q4Matrix wq, wk, wv;  // Hq*64, Hkv*64, Hkv*64 rows of k values
+  int32_t k;
+  const void* x;        // f16 [k]: the normed hidden row of the token
+  const void* norm_w;   // [q(64) | k(64)] or NULL
+  const void* rope;     // [max_ctx][64]
+  void* q_out;          // f16 [Hq*64]: rotated q
+  void* k_cache;        // [cap][Hkv][64]: rotated k at row pos
+  void* v_cache;        // [cap][Hkv][64]: v at row pos
+  int64_t kv_cap;
+  const uint32_t* meta;  // nullable -> pos_host
+  int32_t pos_host;
+  int32_t hq, hkv;
+  float eps;
+  int32_t* err;
+};
+cudaError_t launch_gemv_q4(const GemvArgs& a, cudaStream_t s);
+cudaError_t launch_qkv_prep(const QkvPrepArgs& a, cudaStream_t s);
 
 // ---- kv_quant.cu ----------------------------------------------------------------------------
 // f16 cache rows [rows][hkv][64] -> int8, q = clamp(roundeven(x / scale), -128, 127) with one

@@ -1,6 +1,6 @@
 """Generate the golden fixtures of tests/golden/ from the reference's own shaders.
 
-Runs oracle/_ref (the reference's QK_PREP / ATTN / VISION_ATTN WGSL, translated to C++ by
+Runs oracle/_ref (the reference's QK_PREP / ATTN / VISION_ATTN / GEMV WGSL, translated to C++ by
 oracle/wgsl2cpp.py, which needs the reference sources) on seeded inputs at the reference's
 hard-coded shapes (16 q heads, 8 kv heads, head_dim 64, qkv row 2048, q row 1024, vision row
 768), dispatched exactly as engine.js:221-222 and vision.js:271-276 do, and stores inputs and
@@ -55,12 +55,24 @@ def vision_case(name: str, seed: int, s_tokens: int):
                         s_tokens=np.int32(s_tokens))
 
 
+def gemv_case(name: str, seed: int, k: int, n: int):
+    """The GEMV shader (kernels.js:22-68) at the reference's q_proj shape class: one token's
+    4-bit projection (x [k] -> y [n]), dispatched N/8 workgroups as engine.js does."""
+    rng = np.random.default_rng(seed)
+    wq, sc, zp = O.random_q4(rng, n, k)
+    x = rng.standard_normal(k).astype(np.float16)
+    y = np.zeros(n, np.float16)
+    O.ref_gemv(x, wq, sc, zp, y)
+    np.savez_compressed(OUT / f"{name}.npz", x=x, wq=wq, sc=sc, zp=zp, y=y)
+
+
 def main():
     if not O.ref_available():
         raise SystemExit("oracle/_ref not built: run `make -C oracle` where the reference exists")
     decoder_case("decoder_prefill_16x8", seed=101, pos0=60, m=4, with_norm_scale=0.1)
     decoder_case("decoder_decode_16x8", seed=202, pos0=130, m=1, with_norm_scale=0.1)
     vision_case("vision_s70_h12", seed=303, s_tokens=70)
+    gemv_case("gemv_q4_k1024_n96", seed=404, k=1024, n=96)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -172,3 +172,24 @@ def test_restatement_reproduces_golden_vision(oracle, golden_dir):
     out = np.zeros_like(z["q"])[None]
     oracle.vision_attn(12, 64, z["q"][None], z["k"][None], z["v"][None], out)
     assert np.array_equal(_bits(out[0]), _bits(z["out"]))
+
+
+@ref_only
+@pytest.mark.parametrize("k,n,seed", [(1024, 2048, 1), (2048, 3072, 2), (96, 40, 3), (4608, 16, 4)])
+def test_gemv_restatement_matches_reference_shader(oracle, k, n, seed):
+    """kernels.js:22-68 (GEMV): the restatement equals the translated shader bit for bit,
+    including an odd block count (K = 96: the zero-point row ends mid-byte) and the largest K
+    its workgroup array holds (4608)."""
+    rng = np.random.default_rng(seed)
+    wq, sc, zp = oracle.random_q4(rng, n, k)
+    x = (2 * rng.standard_normal(k)).astype(np.float16)
+    want = np.zeros(n + 5, np.float16)
+    oracle.ref_gemv(x, wq, sc, zp, want, y_off=5)
+    got = oracle.gemv_q4(x, wq, sc, zp, y=np.zeros(n + 5, np.float16), y_off=5)
+    assert np.array_equal(_bits(got), _bits(want))
+
+
+def test_gemv_restatement_reproduces_golden(oracle, golden_dir):
+    z = np.load(golden_dir / "gemv_q4_k1024_n96.npz")
+    got = oracle.gemv_q4(z["x"], z["wq"], z["sc"], z["zp"])
+    assert np.array_equal(_bits(got), _bits(z["y"]))
