@@ -328,6 +328,73 @@ class DecodeWorkload:
         return O.rope_table(self.cap)
 
 
+def q4_weights(g, n, k):
+    """A random 4-bit MatMulNBits matrix (qweight words, f16 scales, zero-point words) on the
+    device; int32 tensors carry the u32 words."""
+    import torch
+    qw = torch.randint(-2**31, 2**31 - 1, (n, k // 8), generator=g, device="cuda",
+                       dtype=torch.int32)
+    sc = (0.01 + 0.02 * torch.rand((n, k // 32), generator=g, device="cuda")).half()
+    zr = (k // 32 + 1) // 2
+    zp = torch.randint(-2**31, 2**31 - 1, ((n * zr + 3) // 4,), generator=g, device="cuda",
+                       dtype=torch.int32)
+    return qw, sc, zp
+
+
+def q4_bytes(n, k):
+    return n * (k // 2 + (k // 32) * 2 + (k // 32 + 1) // 2)
+
+
+def run_decode_block(ctx, wl, steps, warmup, fused=True, sets=4):
+    """The six attention layers of one LFM2.5-1.2B decode step with their projections: per
+    layer the q/k/v projection of the token's hidden row (4-bit weights), QK_PREP, attention
+    over the ctx-4096 cache and the o_proj consumer.  fused: p2p_qkv_gemv_prep (QK_PREP in the
+    projection's epilogue) + p2p_attn + p2p_gemv_q4, 3 launches per layer; unfused: the
+    reference's order, three GEMVs into the qkv row, then QK_PREP + attention
+    (p2p_decode_step, one layer) and o_proj, 5 launches.  Weights rotate over `sets` copies
+    and the caches over the workload's 12 (L2 defeated).  Returns (ms per step, bytes)."""
+    import torch
+    import p2p_b200
+    k = HQ * D  # the hidden size of LFM2.5-1.2B (2048)
+    g = torch.Generator(device="cuda").manual_seed(91)
+    weights = [[tuple(q4_weights(g, n, k) for n in (HQ * D, HKV * D, HKV * D, k))
+                for _ in range(N_LAYERS)] for _ in range(sets)]
+    x = (torch.randn((N_LAYERS, k), generator=g, device="cuda")).half()
+    q = torch.zeros((N_LAYERS, HQ * D), device="cuda", dtype=torch.float16)
+    att = torch.zeros_like(q)
+    y = torch.zeros((N_LAYERS, k), device="cuda", dtype=torch.float16)
+    qkv = torch.zeros((N_LAYERS, (HQ + 2 * HKV) * D), device="cuda", dtype=torch.float16)
+    prm = p2p_b200.Params(HQ, HKV)
+    plans = None
+    if not fused:
+        plans = [[ctx.plan_decode_step(prm, [(qkv[l], wl.nw[l], kc, vc, att[l])], wl.rope,
+                                       wl.cap, use_meta=True)
+                  for l, (kc, vc) in enumerate(c)] for c in wl.copies]
+
+    def step(i):
+        ws = weights[i % sets]
+        caches = wl.copies[i % len(wl.copies)]
+        for l in range(N_LAYERS):
+            wq, wk, wv, wo = ws[l]
+            kc, vc = caches[l]
+            if fused:
+                ctx.qkv_gemv_prep(prm, x[l], wq, wk, wv, wl.nw[l], wl.rope, q[l], kc, vc,
+                                  use_meta=True)
+                ctx.attn(prm, q[l:l + 1], kc, vc, att[l:l + 1], m_tokens=1, use_meta=True)
+            else:
+                ctx.gemv_q4(wq, x[l], qkv[l], 0)
+                ctx.gemv_q4(wk, x[l], qkv[l], HQ * D)
+                ctx.gemv_q4(wv, x[l], qkv[l], (HQ + HKV) * D)
+                plans[i % len(plans)][l].run()
+            ctx.gemv_q4(wo, att[l], y[l])
+
+    ms = timed_graph(step, steps, warmup, 1)
+    per_layer = (q4_bytes(HQ * D, k) + 2 * q4_bytes(HKV * D, k) + q4_bytes(k, HQ * D)
+                 + decode_layer_bytes(wl.past) + k * 2 * 2)
+    del weights
+    return ms, N_LAYERS * per_layer
+
+
 def e2e_decode(wl, steps, warmup):
     """The user-facing per-token call with host buffers: p2p_decode_step whose 6 qkv rows and 6
     output rows live in page-locked host memory, so the kernel itself reads the step's inputs
@@ -784,8 +851,15 @@ def run_only(ctx, args):
         b = wl.bytes_per_step / N_LAYERS
         res = {"us_per_step": ms * 1e3, "gbs": b / (ms * 1e-3) / 1e9}
     elif args.only == "ragged":
-        ms, b, _ = run_ragged(ctx, 0, 1, args.steps, args.warmup, check=False)
+        ms, b, _ = run_ragged(ctx, 0, 1, args.steps, args.warmup, check=False, fmt=args.kv)
         res = {"ms_per_step": ms, "gbs": b / (ms * 1e-3) / 1e9}
+    elif args.only == "block":
+        wl = DecodeWorkload(ctx, 0, copies=12, past=args.past)
+        res = {}
+        for fused in (True, False):
+            ms, b = run_decode_block(ctx, wl, args.steps, args.warmup, fused=fused)
+            res["fused" if fused else "unfused"] = {"us_per_layer": ms * 1e3 / N_LAYERS,
+                                                    "gbs": b / (ms * 1e-3) / 1e9}
     elif args.only == "prefill":
         r = run_prefill(ctx, args.steps, args.warmup, s=args.prefill_s, check=False)
         fl = prefill_flops(args.prefill_s)
@@ -805,10 +879,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip prefill/vision/ragged legs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode", "decode1", "ragged", "prefill", "vision"],
+    ap.add_argument("--only", choices=["decode", "decode1", "ragged", "prefill", "vision", "block"],
                     help="run one leg on one GPU and print its timing (profiling commands)")
     ap.add_argument("--past", type=int, default=PAST, help="decode context for --only decode")
     ap.add_argument("--prefill-s", type=int, default=2048, help="prompt length for --only prefill")
+    ap.add_argument("--kv", default="f16", choices=["f16", "int8", "paged"],
+                    help="KV-cache format for --only ragged")
     ap.add_argument("--quick", action="store_true",
                     help="headline kernel only (no e2e, side legs, CPU leg or clock tail); "
                          "the profiling command")
@@ -885,6 +961,24 @@ def main():
                         "layer caches (605 MB > L2)",
             "gbs_per_gpu": round(b1 / (ms1 * 1e-3) / 1e9, 1), "us_per_step": round(ms1 * 1e3, 3),
             "hbm_frac_of_measured": round(b1 / (ms1 * 1e-3) / 1e9 / hbm_peak, 4)}
+        for fused in (True, False):
+            key = "decode_layers_with_projections" + ("" if fused else "_unfused")
+            try:
+                b_ms, b_bytes = run_decode_block(ctx, wl, steps=20, warmup=3, fused=fused)
+                b_ms = max_over_ranks(b_ms, world)
+                side[key] = {
+                    "workload": "6 LFM2.5-1.2B attention layers of a decode step at ctx 4096 "
+                                "with their 4-bit q/k/v and o_proj GEMVs (hidden 2048): " +
+                                ("QK_PREP fused into the q/k/v projection's epilogue, then "
+                                 "attention and o_proj (3 launches per layer)" if fused else
+                                 "three GEMVs into the qkv row, QK_PREP + attention, o_proj "
+                                 "(5 launches per layer, the reference's order)"),
+                    "us_per_step": round(b_ms * 1e3, 2),
+                    "us_per_layer": round(b_ms * 1e3 / N_LAYERS, 2),
+                    "gbs_per_gpu": round(b_bytes / (b_ms * 1e-3) / 1e9, 1),
+                    "bytes_per_step": int(b_bytes)}
+            except p2p_b200.P2PError as e:
+                side[key] = {"error": str(e)}
         try:
             r_ms, r_bytes, r_par = run_ragged(ctx, rank, world, steps=10, warmup=3)
             r_ms = max_over_ranks(r_ms, world)

@@ -7,9 +7,10 @@
 // 4-bit zero point per 32-element block, w = (q - zp) * scale.
 //
 //   gemv_q4_kernel   y[y_off + n] = f16(x . W[n]): the o_proj consumer (any projection).
-//   qkv_prep_kernel  the q/k/v projections of one token with QK_PREP in the epilogue: one CTA
-//                    per head unit computes its 64 outputs, rounds them to f16 (the qkv row the
-//                    shader would store), then norms and rotates q / k (kernels.js:244-264) and
+//   qkv_prep_kernel  the q/k/v projections of one token with QK_PREP in the epilogue: a cluster
+//                    of 4 CTAs per head unit computes its 64 outputs (16 each, gathered in the
+//                    first CTA's shared memory), rounds them to f16 (the qkv row the shader
+//                    would store), then norms and rotates q / k (kernels.js:244-264) and
 //                    writes rotated q to q_out and k / v to the cache row at the position -- the
 //                    qkv row never goes through HBM and no separate QK_PREP launch runs.
 //
@@ -31,31 +32,60 @@ namespace {
 constexpr int kThreads = 512;  // 16 warps
 constexpr int kWarps = kThreads / 32;
 
+// Barrier over the CTAs of the thread-block cluster (release / acquire of shared memory).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// Generic address of `p` (a shared-memory variable) in the cluster CTA of rank `rank`.
+template <class T>
+__device__ __forceinline__ T* map_cluster_rank(T* p, unsigned rank) {
+  T* r;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(p), "r"(rank));
+  return r;
+}
+
 // One output row as the shader's 32-lane subgroup computes it (kernels.js:44-66); the row's
-// value ends in lane 0.
+// value ends in lane 0.  The words of a lane are fetched 8 at a time (all loads of a batch in
+// flight together) and then accumulated in the shader's order.
 __device__ __forceinline__ float row_dot(const Q4Matrix& w, int n, int k, const __half* xs,
                                          int lane) {
   const int nb = k >> 5, zr = (nb + 1) >> 1, wpr = k >> 3;
   const uint32_t* wrow = w.qweight + int64_t(n) * wpr;
   const __half* srow = w.scales + int64_t(n) * nb;
-  const unsigned char* zbytes = reinterpret_cast<const unsigned char*>(w.zero_points);
+  const unsigned char* zrow =
+      reinterpret_cast<const unsigned char*>(w.zero_points) + int64_t(n) * zr;
   float acc = 0.f;
-#pragma unroll 4
-  for (int wi = lane; wi < wpr; wi += 32) {
-    const uint32_t word = __ldg(wrow + wi);
-    const int blk = wi >> 2;
-    const float s = __half2float(__ldg(srow + blk));
-    const uint32_t zb = __ldg(zbytes + int64_t(n) * zr + (blk >> 1));  // kernels.js:16-19
-    const float z = float((zb >> ((blk & 1) * 4)) & 15u);
-    const uint4 xv = *reinterpret_cast<const uint4*>(xs + wi * 8);
-    const __half* xh = reinterpret_cast<const __half*>(&xv);
-    float a = 0.f;
+  for (int base = lane; base < wpr; base += 32 * 8) {
+    uint32_t word[8];
+    __half sc[8];
+    uint32_t zb[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float q = float((word >> (4 * i)) & 15u);
-      a = __fadd_rn(a, __fmul_rn(__half2float(xh[i]), __fsub_rn(q, z)));
+    for (int j = 0; j < 8; ++j) {
+      const int wi = base + 32 * j;
+      if (wi < wpr) {
+        word[j] = __ldg(wrow + wi);
+        sc[j] = __ldg(srow + (wi >> 2));
+        zb[j] = __ldg(zrow + (wi >> 3));  // kernels.js:16-19 (byte (blk >> 1) of the row)
+      }
     }
-    acc = __fadd_rn(acc, __fmul_rn(a, s));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int wi = base + 32 * j;
+      if (wi < wpr) {
+        const int blk = wi >> 2;
+        const float z = float((zb[j] >> ((blk & 1) * 4)) & 15u);
+        const uint4 xv = *reinterpret_cast<const uint4*>(xs + wi * 8);
+        const __half* xh = reinterpret_cast<const __half*>(&xv);
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float q = float((word[j] >> (4 * i)) & 15u);
+          a = __fadd_rn(a, __fmul_rn(__half2float(xh[i]), __fsub_rn(q, z)));
+        }
+        acc = __fadd_rn(acc, __fmul_rn(a, __half2float(sc[j])));
+      }
+    }
   }
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, s));
@@ -80,15 +110,22 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const __grid_constant
   if (lane == 0) static_cast<__half*>(a.y)[a.y_off + n] = __float2half_rn(v);  // kernels.js:66
 }
 
-__global__ void __launch_bounds__(kThreads) qkv_prep_kernel(const __grid_constant__ QkvPrepArgs a) {
+// One head unit per cluster of kUnitCtas CTAs: CTA r computes rows 16r..16r+15 of the head
+// (one per warp) and stores them in the first CTA's shared memory, which runs the epilogue.
+constexpr int kUnitCtas = 4;
+
+__global__ void __cluster_dims__(kUnitCtas, 1, 1) __launch_bounds__(kThreads)
+    qkv_prep_kernel(const __grid_constant__ QkvPrepArgs a) {
   constexpr int D = kHeadDim;
+  static_assert(D == kUnitCtas * kWarps, "one row per warp");
   __shared__ __align__(16) __half xs[kGemvMaxK];
   __shared__ float y_s[D];
   grid_dependency_wait();
-  const int unit = blockIdx.x;
+  const int unit = blockIdx.x / kUnitCtas;
+  const int part = blockIdx.x % kUnitCtas;  // rank in the cluster
   const int pos = a.meta ? int(a.meta[0]) : a.pos_host;
   if (pos < 0 || int64_t(pos) >= a.kv_cap) {  // the same for every CTA: nothing is written
-    if (threadIdx.x == 0 && unit == 0) atomicOr(a.err, kErrPosBeyondCache);
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
     return;
   }
   stage_x(static_cast<const __half*>(a.x), a.k, xs);
@@ -98,15 +135,17 @@ __global__ void __launch_bounds__(kThreads) qkv_prep_kernel(const __grid_constan
   const int head = kind == 0 ? unit : kind == 1 ? unit - a.hq : unit - a.hq - a.hkv;
   const Q4Matrix& w = kind == 0 ? a.wq : kind == 1 ? a.wk : a.wv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // 64 rows of this head, 4 per warp; the value the GEMV shader would store is the f16 one
-#pragma unroll
-  for (int r = 0; r < D / kWarps; ++r) {
-    const int row = warp * (D / kWarps) + r;
-    const float v = row_dot(w, head * D + row, a.k, xs, lane);
-    if (lane == 0) y_s[row] = __half2float(__float2half_rn(v));
+  // this CTA's 16 rows of the head; the value the GEMV shader would store is the f16 one,
+  // written into the cluster leader's y_s
+  const int row = part * kWarps + warp;
+  const float v = row_dot(w, head * D + row, a.k, xs, lane);
+  cluster_sync_all();  // every CTA of the cluster is running: its shared memory is mapped
+  if (lane == 0) {
+    float* dst = map_cluster_rank(&y_s[row], 0);
+    *dst = __half2float(__float2half_rn(v));
   }
-  __syncthreads();
-  if (warp != 0) return;
+  cluster_sync_all();  // the leader's y_s is complete
+  if (part != 0 || warp != 0) return;
   const int64_t crow = (int64_t(pos) * a.hkv + head) * D;  // cache row `pos`, kv head `head`
   if (kind == 2) {  // QK_PREP v unit (kernels.js:237-241): raw copy
     __half* vc = static_cast<__half*>(a.v_cache) + crow;
@@ -150,7 +189,7 @@ cudaError_t launch_gemv_q4(const GemvArgs& a, cudaStream_t s) {
 cudaError_t launch_qkv_prep(const QkvPrepArgs& a, cudaStream_t s) {
   void* args[] = {const_cast<QkvPrepArgs*>(&a)};
   return launch_pdl(reinterpret_cast<const void*>(&qkv_prep_kernel),
-                    dim3(unsigned(a.hq + 2 * a.hkv)), args, s);
+                    dim3(unsigned((a.hq + 2 * a.hkv) * kUnitCtas)), args, s);
 }
 
 }  // namespace p2p
