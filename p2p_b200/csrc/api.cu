@@ -298,6 +298,7 @@ p2p_status run_causal_flash(p2p_ctx* ctx, const p2p_attn_params* prm, const void
   f.scale_log2 = eff_scale(prm) * 1.4426950408889634f;
   f.err = ctx->dev_err;
   f.wait_deficit = g_wait_deficit.load();
+  f.num_sms = ctx->num_sms;
   cudaError_t e = p2p::launch_flash(f, s);
   if (e == cudaErrorNotSupported) return fail(ctx, P2P_ERR_UNSUPPORTED, "prefill kernel");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill launch");

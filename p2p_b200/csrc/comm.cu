@@ -383,6 +383,7 @@ p2p_status p2p_attn_prefill_sharded(p2p_ctx* ctx, p2p_comm* c, const p2p_attn_pa
     f.scale_log2 = p2p::eff_scale_log2(prm);
     f.err = p2p::ctx_dev_err(ctx);
     f.wait_deficit = p2p::debug_wait_deficit();
+    f.num_sms = p2p::ctx_num_sms(ctx);
     e = p2p::launch_flash(f, s);
   }
   if (st == P2P_OK && e == cudaSuccess && G > 1) {  // one all-gather of the slices, in place
