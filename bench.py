@@ -173,8 +173,9 @@ def sum_over_ranks(x: float, world: int) -> float:
 
 # ---------------------------------------------------------------------------------------------
 # the checker: outputs of each leg compared after its timed region (never inside it).  An
-# element passes when |x - r| <= 2e-3 + 1e-2 |r|; max-abs and max-rel (over |r| > 1e-3) are
-# reported separately as well.
+# element passes when |x - r| <= 2e-3 + 1e-2 |r|; max-abs and max-rel (over |r| > 1e-3, and
+# over |r| > 1e-2) are reported separately as well; within_caps = max-abs <= 2e-3 and
+# max-rel <= 1e-2 as two separate caps.
 
 ATOL, RTOL = 2e-3, 1e-2
 
@@ -187,8 +188,10 @@ def parity_stats(got, want, what):
     finite = bool(np.isfinite(x).all())
     bad = int((~(err <= ATOL + RTOL * np.abs(r))).sum())
     big = np.abs(r) > 1e-3
+    big2 = np.abs(r) > 1e-2
     return {"max_abs": float(err.max()) if err.size else 0.0,
             "max_rel": float((err[big] / np.abs(r[big])).max()) if big.any() else 0.0,
+            "max_rel_r_gt_1e-2": float((err[big2] / np.abs(r[big2])).max()) if big2.any() else 0.0,
             "bad": bad if finite else int(x.size), "n": int(x.size), "checked": what}
 
 
@@ -198,11 +201,12 @@ def reduce_parity(p, world):
     out = dict(p)
     out["max_abs"] = max_over_ranks(p["max_abs"], world)
     out["max_rel"] = max_over_ranks(p["max_rel"], world)
+    out["max_rel_r_gt_1e-2"] = max_over_ranks(p["max_rel_r_gt_1e-2"], world)
     out["bad"] = int(sum_over_ranks(float(p["bad"]), world))
     out["n"] = int(sum_over_ranks(float(p["n"]), world))
     out["ok"] = out["bad"] == 0
     out["within_caps"] = out["max_abs"] <= ATOL and out["max_rel"] <= RTOL
-    for k in ("max_abs", "max_rel"):
+    for k in ("max_abs", "max_rel", "max_rel_r_gt_1e-2"):
         out[k] = float(f"{out[k]:.3e}")
     if world > 1:
         out["checked"] = f"every rank: {p['checked']}"

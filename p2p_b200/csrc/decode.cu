@@ -732,9 +732,17 @@ __global__ void __launch_bounds__(kThreads, 3)
       o[i][2] *= c0;
       o[i][3] *= c1;
     }
-    // P^T as the B operand: the f16 accumulator fragment transposed in registers
-    const uint32_t pb0 = movmatrix_trans(pack_h2(p0, p1));
-    const uint32_t pb1 = movmatrix_trans(pack_h2(p2, p3));
+    // P^T as the B operand: the accumulator fragment transposed in registers, as f16 pairs
+    // p = hi + lo (hi = f16(p), lo = f16(p - hi)): two MMAs per V fragment carry p to ~22
+    // bits, so the weights that multiply V keep the f32 precision of the reference's p
+    // (kernels.js:306-310) instead of f16's 11 bits; the tensor pipe has room (HBM bound).
+    const uint32_t h01 = pack_h2(p0, p1), h23 = pack_h2(p2, p3);
+    const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+    const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+    const uint32_t pb0 = movmatrix_trans(h01);
+    const uint32_t pb1 = movmatrix_trans(h23);
+    const uint32_t pl0 = movmatrix_trans(pack_h2(p0 - f01.x, p1 - f01.y));
+    const uint32_t pl1 = movmatrix_trans(pack_h2(p2 - f23.x, p3 - f23.y));
     // ---- O^T += V^T P^T (4 m-tiles of 16 dims)
     {
       const int r = rw + (mi >> 1) * 8 + (lane & 7);
@@ -743,6 +751,7 @@ __global__ void __launch_bounds__(kThreads, 3)
         uint32_t af[4];
         ldsm_x4_trans(ring + voff + swz(r, 2 * i + (mi & 1)), af);
         mma16816(o[i], af, pb0, pb1);
+        mma16816(o[i], af, pl0, pl1);
       }
     }
   }
