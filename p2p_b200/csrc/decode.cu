@@ -443,16 +443,18 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return uint32_t(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-// int8 caches: per stage a K and a V tile of 64 rows x 64 bytes (row-contiguous), 6 stages,
-// then one f16 K and V tile pair (swizzled like the f16 ring) that each stage is converted
-// into before the MMAs read it.
+// int8 caches: per stage a K and a V tile of 64 rows x 64 bytes, 8 stages (the f16 ring's 64
+// KB).  Row r's four 16-byte pieces are XOR-swizzled with (r >> 1) & 3, so the eight rows one
+// ldmatrix phase reads hit all 32 banks.
 struct RingQ8 {
-  static constexpr int kStages = 6;
+  static constexpr int kStages = 8;
   static constexpr int kTileBytes = kStageKeys * kHeadDim;
   static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kConvOff = kStages * kStageBytes;
-  static constexpr int kBytes = kConvOff + 2 * kStageKeys * kHeadDim * 2;
+  static constexpr int kBytes = kStages * kStageBytes;
 };
+__device__ __forceinline__ uint32_t swz8(int r, int c) {
+  return uint32_t(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
 
 // Four int8 values (one 32-bit word, dims 4k..4k+3) -> two f16x2 words, exactly: the byte
 // x ^ 0x80 under the f16 pattern 0x64xx is 1024 + 128 + x; subtracting 1152 leaves x.
@@ -563,8 +565,8 @@ __global__ void __launch_bounds__(kThreads, 3)
           const int r = (tid >> 2) + 32 * i;
           const bool ok = jt + r < jcopy;
           const int64_t src = row_of(ok ? jt + r : j0) * kv_stride + c * 16;
-          cp_async16(smem_raw + st + r * 64 + c * 16, kbase + src, ok);
-          cp_async16(smem_raw + st + RingQ8::kTileBytes + r * 64 + c * 16, vbase + src, ok);
+          cp_async16(smem_raw + st + swz8(r, c), kbase + src, ok);
+          cp_async16(smem_raw + st + RingQ8::kTileBytes + swz8(r, c), vbase + src, ok);
         }
       } else {
         const uint32_t off = (tile % kStages) * (kTile * 2);
@@ -629,14 +631,18 @@ __global__ void __launch_bounds__(kThreads, 3)
 
   // Q^T as the B operand (k = dims, n = heads): lane holds head n = lane/4 (zero when
   // n >= GC), dims 2(lane%4)+{0,1} and +8 of every 16-dim k-step.
+  // int8 keys are read four dims per register (dims 4t..4t+3 of a 16-dim step), so there the
+  // k index of the MMA runs over the dims in the order 4t, 4t+1 (k = 2t, 2t+1) and 4t+2, 4t+3
+  // (k = 2t+8, 2t+9); q takes the same order (a permutation of the summed index).
   const int gid = lane >> 2, tig = lane & 3;
   uint32_t qb[4][2];
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
-    const int d0 = kk * 16 + 2 * tig;
+    const int d0 = kQ8 ? kk * 16 + 4 * tig : kk * 16 + 2 * tig;
+    const int d1 = kQ8 ? d0 + 2 : d0 + 8;
     if (gid < GC) {
       qb[kk][0] = pack_h2(q_s[gid][d0], q_s[gid][d0 + 1]);
-      qb[kk][1] = pack_h2(q_s[gid][d0 + 8], q_s[gid][d0 + 9]);
+      qb[kk][1] = pack_h2(q_s[gid][d1], q_s[gid][d1 + 1]);
     } else {
       qb[kk][0] = qb[kk][1] = 0u;
     }
@@ -653,30 +659,11 @@ __global__ void __launch_bounds__(kThreads, 3)
     __syncthreads();  // tile landed for every thread; slot (tile-1) % kStages is free again
     issue_tile(tile + kStages - 1);
     const int jt = j0 + tile * kStageKeys;
-    // byte offsets (from smem_raw) of the f16 K and V tiles the MMAs read
+    // byte offsets (from smem_raw) of the K and V tiles the MMAs read
     uint32_t koff, voff;
     if constexpr (kQ8) {
-      // int8 -> f16 (exact) into the conversion tiles, swizzled like the f16 ring
-      const uint32_t st = (tile % kStages) * RingQ8::kStageBytes;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int idx = tid + kThreads * q;  // 512 16-byte pieces: K tile, then V tile
-        const int which = idx >> 8, r = (idx >> 2) & 63, c = idx & 3;
-        const uint4 w = *reinterpret_cast<const uint4*>(smem_raw + st +
-                                                        which * RingQ8::kTileBytes + r * 64 +
-                                                        c * 16);
-        uint4 o0, o1;
-        s8x4_to_f16x4(w.x, o0.x, o0.y);
-        s8x4_to_f16x4(w.y, o0.z, o0.w);
-        s8x4_to_f16x4(w.z, o1.x, o1.y);
-        s8x4_to_f16x4(w.w, o1.z, o1.w);
-        unsigned char* dst = smem_raw + RingQ8::kConvOff + which * (kTile * 2);
-        *reinterpret_cast<uint4*>(dst + swz(r, 2 * c)) = o0;
-        *reinterpret_cast<uint4*>(dst + swz(r, 2 * c + 1)) = o1;
-      }
-      koff = RingQ8::kConvOff;
-      voff = RingQ8::kConvOff + kTile * 2;
-      __syncthreads();
+      koff = (tile % kStages) * RingQ8::kStageBytes;
+      voff = koff + RingQ8::kTileBytes;
     } else {
       koff = (tile % kStages) * (kTile * 2);
       voff = kVOff + koff;
@@ -684,7 +671,21 @@ __global__ void __launch_bounds__(kThreads, 3)
     if (FUSED && has_new && sq.past >= jt && sq.past < jt + kStageKeys) {
       // the new token's k/v (computed in the prologue) replace the zero-filled tile row
       const int r = sq.past - jt;
-      if (tid < 16) {
+      if constexpr (kQ8) {
+        if (tid < 8) {  // the quantised integers, 16 bytes per thread
+          const int c = tid & 3;
+          const float* src = (tid < 4 ? knew_s : vnew_s) + c * 16;
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            w[k] = (uint32_t(int32_t(src[4 * k]) & 255)) |
+                   (uint32_t(int32_t(src[4 * k + 1]) & 255) << 8) |
+                   (uint32_t(int32_t(src[4 * k + 2]) & 255) << 16) |
+                   (uint32_t(int32_t(src[4 * k + 3]) & 255) << 24);
+          *reinterpret_cast<uint4*>(smem_raw + (tid < 4 ? koff : voff) + swz8(r, c)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else if (tid < 16) {
         const int c = tid & 7;
         const float* src = (tid < 8 ? knew_s : vnew_s) + c * 8;
         const uint4 val = make_uint4(pack_h2(src[0], src[1]), pack_h2(src[2], src[3]),
@@ -696,7 +697,23 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int rw = warp * 16;  // this warp's 16 keys of the tile
     // ---- S^T = K Q^T (4 k-steps over the 64 dims)
     float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-    {
+    if constexpr (kQ8) {
+      // one ldmatrix.x4 of int8 rows covers 16 keys x 32 dims: register 0 = key gid, dims
+      // 4t..4t+3 of the first 16; 1 = key gid + 8; 2, 3 = the same for the next 16 dims
+      const int r = rw + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int kk2 = 0; kk2 < 2; ++kk2) {
+        uint32_t kr[4];
+        ldsm_x4(ring + koff + swz8(r, kk2 * 2 + (lane >> 4)), kr);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t af[4];
+          s8x4_to_f16x4(kr[2 * h], af[0], af[2]);
+          s8x4_to_f16x4(kr[2 * h + 1], af[1], af[3]);
+          mma16816(sacc, af, qb[kk2 * 2 + h][0], qb[kk2 * 2 + h][1]);
+        }
+      }
+    } else {
       const int r = rw + (mi & 1) * 8 + (lane & 7);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
@@ -744,7 +761,27 @@ __global__ void __launch_bounds__(kThreads, 3)
     const uint32_t pl0 = movmatrix_trans(pack_h2(p0 - f01.x, p1 - f01.y));
     const uint32_t pl1 = movmatrix_trans(pack_h2(p2 - f23.x, p3 - f23.y));
     // ---- O^T += V^T P^T (4 m-tiles of 16 dims)
-    {
+    if constexpr (kQ8) {
+      // int8 V rows (keys) read four dims per register, converted to f16 pairs (dims 4t, 4t+1
+      // and 4t+2, 4t+3 of key gid) and transposed with movmatrix into V^T fragments whose rows
+      // are the dims 4(g>>1) + (g&1) (first 8 rows) and that + 2 (last 8) of each 16-dim tile
+      const int r = rw + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int i2 = 0; i2 < 2; ++i2) {
+        uint32_t vr[4];
+        ldsm_x4(ring + voff + swz8(r, i2 * 2 + (lane >> 4)), vr);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t lo0, hi0, lo1, hi1;  // keys 0-7 and keys 8-15 of the warp's 16
+          s8x4_to_f16x4(vr[2 * h], lo0, hi0);
+          s8x4_to_f16x4(vr[2 * h + 1], lo1, hi1);
+          const uint32_t af[4] = {movmatrix_trans(lo0), movmatrix_trans(hi0),
+                                  movmatrix_trans(lo1), movmatrix_trans(hi1)};
+          mma16816(o[i2 * 2 + h], af, pb0, pb1);
+          mma16816(o[i2 * 2 + h], af, pl0, pl1);
+        }
+      }
+    } else {
       const int r = rw + (mi >> 1) * 8 + (lane & 7);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -757,11 +794,15 @@ __global__ void __launch_bounds__(kThreads, 3)
   }
   cp_async_wait<0>();
   if (a.pdl == 2) launch_dependents();
-  if constexpr (kQ8) {  // the value scales, per output dim (16i + gid, 16i + gid + 8)
+  // output dims of the accumulator rows gid and gid + 8 of tile i: 16i + gid and 16i + gid + 8
+  // for f16 caches; 16i + 4(gid>>1) + (gid&1) and that + 2 for int8 (the V^T row order above)
+  const int dlo = kQ8 ? 4 * (gid >> 1) + (gid & 1) : gid;
+  const int dhi = kQ8 ? dlo + 2 : gid + 8;
+  if constexpr (kQ8) {  // the value scales, per output dim
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float s0 = kv_scale(a.v_scale, a.scale_per_channel, kh, 16 * i + gid);
-      const float s1 = kv_scale(a.v_scale, a.scale_per_channel, kh, 16 * i + gid + 8);
+      const float s0 = kv_scale(a.v_scale, a.scale_per_channel, kh, 16 * i + dlo);
+      const float s1 = kv_scale(a.v_scale, a.scale_per_channel, kh, 16 * i + dhi);
       o[i][0] *= s0;
       o[i][1] *= s0;
       o[i][2] *= s1;
@@ -785,8 +826,8 @@ __global__ void __launch_bounds__(kThreads, 3)
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        red_acc[warp][g][16 * i + gid] = o[i][e];
-        red_acc[warp][g][16 * i + gid + 8] = o[i][2 + e];
+        red_acc[warp][g][16 * i + dlo] = o[i][e];
+        red_acc[warp][g][16 * i + dhi] = o[i][2 + e];
       }
     }
   }
