@@ -138,6 +138,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Launched behind QK_PREP (programmatic dependent launch): the CTA may be resident before
+  // that kernel completes, and reads nothing it writes (q, the cache rows, meta) before this.
+  grid_dependency_wait();
   // Grid (heads, q pairs, images), launched in linear order: every head's q pair before the
   // next q pair, and causal q pairs longest first (the last pair sees the most keys), so the
   // block scheduler hands out the work longest-processing-time first.
@@ -556,8 +559,17 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
   if (attr_err != cudaSuccess) return attr_err;
   void* args[] = {&tq, &tk, &tv, &p};
   auto launch = [&](dim3 grid) {
-    return cudaLaunchKernel(reinterpret_cast<const void*>(&flash_fwd_kernel), grid,
-                            dim3(kThreads), args, smem, stream);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at{};
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(&flash_fwd_kernel), args);
   };
   // Non-causal (all items equal): when the items do not fill the last wave of one CTA per SM,
   // the last R pairs run as 2R one-tile CTAs at the end of the same grid (the block scheduler

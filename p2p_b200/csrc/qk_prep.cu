@@ -126,6 +126,9 @@ constexpr int kRowsPerBlock = 128;  // 4 warps; one q/k row per thread
 template <class T>
 __global__ void __launch_bounds__(kRowsPerBlock)
     qk_prep_rows_kernel(const QkPrepArgs a) {
+  // the attention that follows may launch now; it waits for this kernel to complete before
+  // it reads anything
+  launch_dependents();
   constexpr int kVec = 16 / sizeof(T);             // elements per 16-byte access
   constexpr int kPieces = kHeadDim / kVec;         // 16-byte pieces per row
   constexpr int kStride = kHeadDim * sizeof(T) + 16;  // staged row stride in bytes
@@ -230,15 +233,29 @@ __global__ void __launch_bounds__(kRowsPerBlock)
         }
       }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < 8; k += 2) {
         const int i = c + k;
-        float n0 = x.get(i), n1 = x.get(i + 32);
+        float n0[2] = {x.get(i), x.get(i + 1)}, n1[2] = {x.get(i + 32), x.get(i + 33)};
         if (has_norm) {
-          n0 = round_st<T>(__fmul_rn(__fmul_rn(n0, inv), w[i]));
-          n1 = round_st<T>(__fmul_rn(__fmul_rn(n1, inv), w[i + 32]));
+          float u0[2], u1[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            u0[e] = __fmul_rn(__fmul_rn(n0[e], inv), w[i + e]);
+            u1[e] = __fmul_rn(__fmul_rn(n1[e], inv), w[i + 32 + e]);
+          }
+          if constexpr (sizeof(T) == 2) {  // the shader's f16() rounding, two values at once
+            const float2 r0 = __half22float2(__floats2half2_rn(u0[0], u0[1]));
+            const float2 r1 = __half22float2(__floats2half2_rn(u1[0], u1[1]));
+            n0[0] = r0.x; n0[1] = r0.y; n1[0] = r1.x; n1[1] = r1.y;
+          } else {
+            n0[0] = u0[0]; n0[1] = u0[1]; n1[0] = u1[0]; n1[1] = u1[1];
+          }
         }
-        lo[k] = __fsub_rn(__fmul_rn(n0, cs[k]), __fmul_rn(n1, sn[k]));
-        hi[k] = __fadd_rn(__fmul_rn(n1, cs[k]), __fmul_rn(n0, sn[k]));
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          lo[k + e] = __fsub_rn(__fmul_rn(n0[e], cs[k + e]), __fmul_rn(n1[e], sn[k + e]));
+          hi[k + e] = __fadd_rn(__fmul_rn(n1[e], cs[k + e]), __fmul_rn(n0[e], sn[k + e]));
+        }
       }
       store8(out + c, lo);
       store8(out + 32 + c, hi);

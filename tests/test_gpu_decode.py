@@ -56,7 +56,12 @@ def oracle_decode(oracle, hq, hkv, qkv, nw, rope, kc, vc, past):
 
 @pytest.mark.parametrize("hq,hkv,pos0,m,norm", [(32, 8, 0, 5, True), (32, 8, 4000, 3, True),
                                                 (16, 8, 77, 64, True), (32, 8, 9, 2, False),
-                                                (12, 12, 3, 7, True)])
+                                                (12, 12, 3, 7, True),
+                                                # whole prompt chunks (the token-tile kernel),
+                                                # including the config's S = 2048 and a last
+                                                # tile of 5 tokens
+                                                (32, 8, 0, 2048, True), (32, 8, 0, 2048, False),
+                                                (32, 8, 150, 333, True), (16, 8, 0, 8, True)])
 def test_qk_prep_bit_exact(ctx, oracle, hq, hkv, pos0, m, norm):
     import p2p_b200
     rng = np.random.default_rng(hq * 1000 + pos0 + m)
