@@ -459,7 +459,7 @@ def lpt_shard(lengths, world):
 RAGGED_BLOCK = 64  # tokens per page of the paged leg
 
 
-def run_ragged(ctx, rank, world, steps, warmup, check=True, fmt="f16"):
+def run_ragged(ctx, rank, world, steps, warmup, check=True, fmt="f16", nseq_total=256):
     """The 256-sequence batched decode (this rank's LPT share) with the KV cache in format
     `fmt`: "f16" rows at per-sequence offsets (the engine's layout), "int8" rows with
     per-channel scales (half the bytes), or "paged" f16 pages of RAGGED_BLOCK tokens in a
@@ -467,7 +467,7 @@ def run_ragged(ctx, rank, world, steps, warmup, check=True, fmt="f16"):
     import numpy as np
     import torch
     import p2p_b200
-    past_all = ragged_lengths()
+    past_all = ragged_lengths()[:nseq_total]
     mine = lpt_shard(past_all, world)[rank]
     past = past_all[mine].astype(np.int32)
     rows = past + 1
@@ -855,7 +855,8 @@ def run_only(ctx, args):
         b = wl.bytes_per_step / N_LAYERS
         res = {"us_per_step": ms * 1e3, "gbs": b / (ms * 1e-3) / 1e9}
     elif args.only == "ragged":
-        ms, b, _ = run_ragged(ctx, 0, 1, args.steps, args.warmup, check=False, fmt=args.kv)
+        ms, b, _ = run_ragged(ctx, 0, 1, args.steps, args.warmup, check=False, fmt=args.kv,
+                              nseq_total=args.ragged_seqs)
         res = {"ms_per_step": ms, "gbs": b / (ms * 1e-3) / 1e9}
     elif args.only == "block":
         wl = DecodeWorkload(ctx, 0, copies=12, past=args.past)
@@ -889,6 +890,8 @@ def main():
     ap.add_argument("--prefill-s", type=int, default=2048, help="prompt length for --only prefill")
     ap.add_argument("--kv", default="f16", choices=["f16", "int8", "paged"],
                     help="KV-cache format for --only ragged")
+    ap.add_argument("--ragged-seqs", type=int, default=256,
+                    help="sequences of the batch for --only ragged (a smaller case to profile)")
     ap.add_argument("--quick", action="store_true",
                     help="headline kernel only (no e2e, side legs, CPU leg or clock tail); "
                          "the profiling command")
