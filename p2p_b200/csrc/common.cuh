@@ -137,23 +137,32 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // sum of squares is folded with xor-butterflies 16, 8, 4, 2, 1 after pairing (l, l+32): every
 // partial sum equals the shader's shared-memory tree (kernels.js:246-251) bit for bit, since
 // each IEEE addition is commutative.  Separate __fmul_rn/__fadd_rn keep the shader's
-// rounding (no FMA contraction).
+// rounding (no FMA contraction).  norm_rope_vals takes the lane's norm weights already loaded
+// (w0 = nw[lane], w1 = nw[lane + 32]); norm_rope_head loads them from nw.
 template <class T>
-__device__ __forceinline__ void norm_rope_head(float v0, float v1, const T* nw, bool has_norm,
-                                               float eps, float cs, float sn, float& r0,
-                                               float& r1) {
+__device__ __forceinline__ void norm_rope_vals(float v0, float v1, float w0, float w1,
+                                               bool has_norm, float eps, float cs, float sn,
+                                               float& r0, float& r1) {
   float n0 = v0, n1 = v1;
   if (has_norm) {
-    const int l = threadIdx.x & 31;
     float ss = __fadd_rn(__fmul_rn(v0, v0), __fmul_rn(v1, v1));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
     const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, 64.0f), eps));
-    n0 = round_st<T>(__fmul_rn(__fmul_rn(v0, inv), to_f32(nw[l])));
-    n1 = round_st<T>(__fmul_rn(__fmul_rn(v1, inv), to_f32(nw[l + 32])));
+    n0 = round_st<T>(__fmul_rn(__fmul_rn(v0, inv), w0));
+    n1 = round_st<T>(__fmul_rn(__fmul_rn(v1, inv), w1));
   }
   r0 = __fsub_rn(__fmul_rn(n0, cs), __fmul_rn(n1, sn));
   r1 = __fadd_rn(__fmul_rn(n1, cs), __fmul_rn(n0, sn));
+}
+template <class T>
+__device__ __forceinline__ void norm_rope_head(float v0, float v1, const T* nw, bool has_norm,
+                                               float eps, float cs, float sn, float& r0,
+                                               float& r1) {
+  const int l = threadIdx.x & 31;
+  const float w0 = has_norm ? to_f32(nw[l]) : 0.f;
+  const float w1 = has_norm ? to_f32(nw[l + 32]) : 0.f;
+  norm_rope_vals<T>(v0, v1, w0, w1, has_norm, eps, cs, sn, r0, r1);
 }
 
 }  // namespace p2p

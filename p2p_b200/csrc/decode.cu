@@ -152,38 +152,163 @@ __device__ __forceinline__ float cache_f32<int8_t>(int8_t x) { return float(x); 
 // holds the new token its normed/rotated k and raw v (QK_PREP's k and v units) into
 // knew_s/vnew_s and, by head chunk 0, into cache row `new_row` (an int8 cache stores them
 // quantised, and knew_s/vnew_s then hold the quantised integers).  Unfused: q is read as given.
+// The prologue's inputs in registers, per lane.
+struct PrologueIn {
+  float cs, sn;   // fused: this lane's rope row entries (lane, lane + 32)
+  float x[2][2];  // fused: unit (warp + 4i)'s values at lane and lane + 32; else q_s values
+  float w[2][2];  // fused: that unit's norm weights (q and k units)
+  float ks[2];    // int8 cache: the key scales that fold into q (per channel) or the one scale
+};
+
+// Where the prologue reads its inputs: the global rows, or the CTA's shared-memory copy of
+// them (PrologueStage).
+template <class T>
+struct PrologueSrc {
+  const T* q;       // the split's GC q heads, 64 values each, consecutive
+  const T* k;       // fused: the new token's k head and v head (64 values each)
+  const T* v;
+  const T* nw;      // [q norm | k norm] or nullptr
+  const T* rope;    // fused: the position's rope row
+  const float* ks;  // int8 caches: the kv head's 64 key scales, or the one scale
+};
+
+template <class T, class TC>
+__device__ __forceinline__ PrologueSrc<T> prologue_global(const DecodeArgs& a,
+                                                          const Seq<T, TC>& sq, int kh,
+                                                          int head0) {
+  constexpr int D = kHeadDim;
+  PrologueSrc<T> src;
+  src.q = sq.qrow + int64_t(head0) * D;
+  src.k = sq.qrow + int64_t(a.hq + kh) * D;
+  src.v = sq.qrow + int64_t(a.hq + a.hkv + kh) * D;
+  src.nw = sq.nw;
+  src.rope = static_cast<const T*>(a.rope) + int64_t(sq.past) * D;
+  src.ks = a.k_scale ? a.k_scale + (a.scale_per_channel ? kh * D : 0) : nullptr;
+  return src;
+}
+
+// The prologue's inputs copied into shared memory as the CTA's first cp.async group, ahead
+// of the K/V tiles: loads issued behind a CTA's tile burst return only after it (about 2 us
+// with three CTAs per SM), and the prologue would then hold up the ring's refills.  16-byte
+// pieces: the q heads, k and v (fused, new token), the norm weights, the rope row, the key
+// scales (int8 per channel); the host enables it when every source is 16-byte aligned.
+// Layout (bytes): q GC*128 | k 128 | v 128 | nw 256 | rope 128 | ks 256 = GC*128 + 896.
+template <int GC>
+constexpr int prologue_stage_bytes() {
+  return GC * 128 + 896;
+}
+
+template <class T, class TC, int GC, bool FUSED>
+__device__ __forceinline__ PrologueSrc<T> prologue_stage(const DecodeArgs& a,
+                                                         const PrologueSrc<T>& g,
+                                                         bool has_new, bool do_q,
+                                                         unsigned char* stage) {
+  constexpr bool kQ8 = sizeof(TC) == 1;
+  const int tid = threadIdx.x;
+  const int c = tid;  // one 16-byte piece per thread (at most GC*8 + 56 <= 88 pieces)
+  const void* from = nullptr;
+  int at = 0;
+  if (c < GC * 8) {
+    if (do_q) from = g.q + c * 8, at = c * 16;
+  } else if (c < GC * 8 + 16) {
+    const int e = c - GC * 8;
+    if (FUSED && has_new) from = (e < 8 ? g.k : g.v) + (e & 7) * 8, at = GC * 128 + e * 16;
+  } else if (c < GC * 8 + 32) {
+    const int e = c - GC * 8 - 16;
+    if (g.nw != nullptr) from = g.nw + e * 8, at = GC * 128 + 256 + e * 16;
+  } else if (c < GC * 8 + 40) {
+    const int e = c - GC * 8 - 32;
+    if (FUSED) from = g.rope + e * 8, at = GC * 128 + 512 + e * 16;
+  } else if (c < GC * 8 + 56) {
+    const int e = c - GC * 8 - 40;
+    if (kQ8 && a.scale_per_channel) from = g.ks + e * 4, at = GC * 128 + 640 + e * 16;
+  }
+  if (from != nullptr) cp_async16(stage + at, from, true);
+  cp_async_commit();
+  PrologueSrc<T> s;
+  s.q = reinterpret_cast<const T*>(stage);
+  s.k = reinterpret_cast<const T*>(stage + GC * 128);
+  s.v = reinterpret_cast<const T*>(stage + GC * 128 + 128);
+  s.nw = g.nw != nullptr ? reinterpret_cast<const T*>(stage + GC * 128 + 256) : nullptr;
+  s.rope = reinterpret_cast<const T*>(stage + GC * 128 + 512);
+  s.ks = (kQ8 && a.scale_per_channel) ? reinterpret_cast<const float*>(stage + GC * 128 + 640)
+                                      : g.ks;
+  return s;
+}
+
+template <class T, class TC, int GC, bool FUSED>
+__device__ __forceinline__ PrologueIn prologue_load(const DecodeArgs& a, const PrologueSrc<T>& src,
+                                                    bool has_new, bool do_q) {
+  constexpr int D = kHeadDim;
+  constexpr bool kQ8 = sizeof(TC) == 1;
+  static_assert(kWarps == 4 && GC <= 4, "the warp's units are warp and warp + 4");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  PrologueIn in{};
+  if (FUSED) {
+    in.cs = to_f32(src.rope[lane]);
+    in.sn = to_f32(src.rope[32 + lane]);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int u = warp + i * kWarps;
+      if (u >= GC + 2 || (u < GC ? !do_q : !has_new)) continue;
+      const T* x = u < GC ? src.q + u * D : (u == GC ? src.k : src.v);
+      in.x[i][0] = to_f32(x[lane]);
+      in.x[i][1] = to_f32(x[lane + 32]);
+      if (src.nw != nullptr && u <= GC) {  // q units take the q norm, the k unit the k norm
+        const T* w = src.nw + (u < GC ? 0 : D);
+        in.w[i][0] = to_f32(w[lane]);
+        in.w[i][1] = to_f32(w[lane + 32]);
+      }
+    }
+  } else if (do_q) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      if (tid + i * kThreads < GC * D) in.x[i][0] = to_f32(src.q[tid + i * kThreads]);
+  }
+  if constexpr (kQ8) {
+    if (a.scale_per_channel) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        if (tid + i * kThreads < GC * D) in.ks[i] = src.ks[(tid + i * kThreads) % D];
+    } else {
+      in.ks[0] = src.ks[0];
+    }
+  }
+  return in;
+}
+
+// QK_PREP of the split's q heads (and, in the CTA holding the new token, its k and v) from
+// the loaded inputs: the normed, rotated q (times qscale) into q_s; k/v into knew_s / vnew_s
+// and, for head chunk 0, into cache row new_row (int8 caches: quantised).
 template <class T, class TC, int GC, bool FUSED>
 __device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T, TC>& sq, int kh,
                                          int hc, int head0, bool has_new, int64_t new_row,
                                          float qscale, float (*q_s)[kHeadDim], float* knew_s,
-                                         float* vnew_s, bool do_q = true) {
+                                         float* vnew_s, const PrologueIn& in, bool do_q = true) {
   constexpr int D = kHeadDim;
   constexpr bool kQ8 = sizeof(TC) == 1;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (FUSED) {
     const int64_t kv_stride = int64_t(a.hkv) * D;
-    const T* rope = static_cast<const T*>(a.rope) + int64_t(sq.past) * D;
-    const float cs = to_f32(rope[lane]);
-    const float sn = to_f32(rope[32 + lane]);
-    for (int u = warp; u < GC + 2; u += kWarps) {
-      if (u < GC ? !do_q : !has_new) continue;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int u = warp + i * kWarps;
+      if (u >= GC + 2 || (u < GC ? !do_q : !has_new)) continue;
       if (u < GC) {  // QK_PREP q unit (kernels.js:255-263), f16 rounding of the stored q
-        const int64_t off = int64_t(head0 + u) * D;
         float r0, r1;
-        norm_rope_head<T>(to_f32(sq.qrow[off + lane]), to_f32(sq.qrow[off + lane + 32]), sq.nw,
-                          sq.nw != nullptr, a.eps, cs, sn, r0, r1);
+        norm_rope_vals<T>(in.x[i][0], in.x[i][1], in.w[i][0], in.w[i][1], sq.nw != nullptr,
+                          a.eps, in.cs, in.sn, r0, r1);
         q_s[u][lane] = round_st<T>(r0) * qscale;
         q_s[u][lane + 32] = round_st<T>(r1) * qscale;
         continue;
       }
       // QK_PREP k unit (normed, rotated) or v unit (raw copy) -> cache row `new_row`
       const bool is_k = u == GC;
-      const int64_t off = int64_t(a.hq + (is_k ? 0 : a.hkv) + kh) * D;
-      float x0 = to_f32(sq.qrow[off + lane]), x1 = to_f32(sq.qrow[off + lane + 32]);
+      float x0 = in.x[i][0], x1 = in.x[i][1];
       if (is_k) {
         float r0, r1;
-        norm_rope_head<T>(x0, x1, sq.nw ? sq.nw + D : nullptr, sq.nw != nullptr, a.eps, cs, sn,
-                          r0, r1);
+        norm_rope_vals<T>(x0, x1, in.w[i][0], in.w[i][1], sq.nw != nullptr, a.eps, in.cs,
+                          in.sn, r0, r1);
         x0 = round_st<T>(r0);
         x1 = round_st<T>(r1);
       }
@@ -206,8 +331,11 @@ __device__ __forceinline__ void prologue(const DecodeArgs& a, const Seq<T, TC>& 
       dst_s[lane + 32] = cache_f32<TC>(c1);
     }
   } else if (do_q) {
-    for (int i = tid; i < GC * D; i += kThreads)
-      q_s[i / D][i % D] = to_f32(sq.qrow[int64_t(head0) * D + i]) * qscale;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int e = tid + i * kThreads;
+      if (e < GC * D) q_s[e / D][e % D] = in.x[i][0] * qscale;
+    }
   }
 }
 
@@ -583,16 +711,27 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
     cp_async_commit();
   };
+  const bool q_bcast = CL != 0 && a.q_bcast;
+  const bool do_q = !q_bcast || split == 0;
+  PrologueSrc<T> psrc = prologue_global<T, TC>(a, sq, kh, head0);
+  static_assert(prologue_stage_bytes<GC>() <= int(sizeof(red_acc)), "stage fits red_acc");
+  if (a.pro_async)  // red_acc is free until the warp merge after the key loop
+    psrc = prologue_stage<T, TC, GC, FUSED>(a, psrc, has_new, do_q,
+                                            reinterpret_cast<unsigned char*>(&red_acc[0][0][0]));
 #pragma unroll
   for (int t = 0; t < kStages - 1; ++t) issue_tile(t);
+  if (a.pro_async) {
+    cp_async_wait<kStages - 1>();  // the prologue's group, the oldest, has landed
+    __syncthreads();               // ... for every thread's pieces
+  }
+  const PrologueIn pin = prologue_load<T, TC, GC, FUSED>(a, psrc, has_new, do_q);
 
   // Cluster form with the qkv rows in host memory: the query rows are the same for every split
   // of a (layer, head chunk), so rank 0 alone reads them across the host link and rotates
   // them, and pushes the result into every peer's q_s (st.async, completing on the peer's
   // q_bar); the first K/V tiles are already in flight meanwhile.
-  const bool q_bcast = CL != 0 && a.q_bcast;
   prologue<T, TC, GC, FUSED>(a, sq, kh, hc, head0, has_new, has_new ? row_of(sq.past) : 0,
-                             1.0f, q_s, knew_s, vnew_s, !q_bcast || split == 0);
+                             1.0f, q_s, knew_s, vnew_s, pin, do_q);
   if (q_bcast) {
     cluster_wait();  // every rank's q_bar and recv_bar are initialised
     constexpr int kQChunks = GC * D * 4 / 16;  // 16-byte pieces of q_s
@@ -622,10 +761,14 @@ __global__ void __launch_bounds__(kThreads, 3)
   float sl2 = a.scale_log2;
   if constexpr (kQ8) {
     if (a.scale_per_channel) {
-      for (int i = tid; i < GC * D; i += kThreads) q_s[i / D][i % D] *= a.k_scale[kh * D + i % D];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int e = tid + i * kThreads;
+        if (e < GC * D) q_s[e / D][e % D] *= pin.ks[i];
+      }
       __syncthreads();
     } else {
-      sl2 *= a.k_scale[0];
+      sl2 *= pin.ks[0];
     }
   }
 
@@ -965,7 +1108,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   for (int t = 0; t < kStages - 1; ++t) issue_tile(t);
 
   prologue<T, T, GC, FUSED>(a, sq, kh, hc, head0, has_new, sq.past, a.scale_log2, q_s, knew_s,
-                            vnew_s);
+                            vnew_s,
+                            prologue_load<T, T, GC, FUSED>(
+                                a, prologue_global<T, T>(a, sq, kh, head0), has_new, true));
   __syncthreads();
 
   float qr[GC][8];
@@ -1207,8 +1352,29 @@ int decode_cluster_splits(int64_t max_len, int hkv, int group, int nz, bool fuse
   return 1;
 }
 
-cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, int max_splits,
-                          int nz, cudaStream_t s, int cluster) {
+namespace {
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Whether every input the prologue copies with 16-byte cp.async is 16-byte aligned and in
+// device memory (host rows, the q_bcast form, keep plain loads).
+bool prologue_async_ok(const DecodeArgs& a, int mode, bool fused, int nz) {
+  if (a.q_bcast) return false;
+  if (fused && !aligned16(a.rope)) return false;
+  if (a.kv_format == kKvI8 && a.scale_per_channel && !aligned16(a.k_scale)) return false;
+  if (mode == kLayers) {
+    for (int l = 0; l < nz; ++l)
+      if (!aligned16(a.layers[l].qkv) || (a.layers[l].norm_w && !aligned16(a.layers[l].norm_w)))
+        return false;
+    return true;
+  }
+  return aligned16(a.qkv) && (a.ld_qkv % 8) == 0 && (!a.norm_w || aligned16(a.norm_w));
+}
+}  // namespace
+
+cudaError_t launch_decode(const DecodeArgs& args_in, int mode, bool fused, int dtype,
+                          int max_splits, int nz, cudaStream_t s, int cluster) {
+  DecodeArgs a = args_in;
+  a.pro_async = dtype == 0 && prologue_async_ok(a, mode, fused, nz) ? 1 : 0;
   const int group = a.hq / a.hkv;
   const bool cl = cluster > 1;
   if (cl && (cluster > kMaxCluster || cluster != max_splits)) return cudaErrorInvalidValue;
@@ -1217,7 +1383,7 @@ cudaError_t launch_decode(const DecodeArgs& a, int mode, bool fused, int dtype, 
   cudaError_t e = configure(k, cl);
   if (e != cudaSuccess) return e;
   dim3 grid(max_splits, a.hkv * head_chunks(group), nz);
-  void* args[] = {const_cast<DecodeArgs*>(&a)};
+  void* args[] = {&a};
   if (!cl && !a.pdl) return cudaLaunchKernel(k.fn, grid, dim3(kThreads), args, size_t(k.smem), s);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;

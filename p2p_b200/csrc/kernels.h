@@ -87,6 +87,9 @@ struct DecodeArgs {
   int32_t wait_deficit;  // test hook: extra bytes the cluster combine waits for (0 normally)
   int32_t q_bcast;       // cluster form: rank 0 alone reads the qkv rows (host memory) and
                          // hands the rotated q to its peers
+  int32_t pro_async;     // 1: the prologue's inputs (q/k/v heads, norm weights, rope row, key
+                         // scales) are 16-byte aligned and device resident, and go to shared
+                         // memory as the CTA's first cp.async group, ahead of its K/V tiles
   int32_t pdl;           // programmatic dependent launch: 0 off; 1 let the next kernel of the
                          // stream launch once every CTA has started, 2 once it has streamed
                          // its keys (the next kernel still waits for this one to complete
