@@ -259,6 +259,25 @@ def timed_graph(fn, steps, warmup, world, capture_error_mode="global"):
     return start.elapsed_time(end) / steps
 
 
+def stream_reference(ctx, nbytes, steps, warmup, world, copies=12):
+    """The speed of light of "read these bytes in one launch": p2p_debug_stream_read over the
+    same number of bytes, one launch per graph node, rotating over `copies` windows of one
+    buffer (> L2) exactly like the decode legs.  Returns (us per launch, bytes)."""
+    import torch
+    n = (int(nbytes) + 15) // 16 * 16
+    buf = torch.empty((copies * n // 4,), dtype=torch.int32, device="cuda")
+    buf.random_(generator=torch.Generator(device="cuda").manual_seed(7))
+    sink = torch.zeros(1, dtype=torch.int32, device="cuda")
+    views = [buf[i * n // 4:(i + 1) * n // 4] for i in range(copies)]
+
+    def step(i):
+        ctx.debug_stream_read(views[i % copies], sink, n)
+
+    ms = max_over_ranks(timed_graph(step, steps, warmup, world), world)
+    del buf, views
+    return ms * 1e3, n
+
+
 class DecodeWorkload:
     """6 independent LFM2.5-1.2B attention layers at context 4096 (+1), R rotating copies."""
 
@@ -848,12 +867,15 @@ def run_only(ctx, args):
     if args.only == "decode":
         wl = DecodeWorkload(ctx, 0, copies=4, past=args.past)
         ms = timed_graph(wl.step, args.steps, args.warmup, 1)
-        res = {"us_per_step": ms * 1e3, "gbs": wl.bytes_per_step / (ms * 1e-3) / 1e9}
+        res = {"us_per_step": ms * 1e3, "gbs": wl.bytes_per_step / (ms * 1e-3) / 1e9,
+               "stream_same_bytes_us": stream_reference(ctx, wl.bytes_per_step, args.steps,
+                                                        args.warmup, 1, copies=4)[0]}
     elif args.only == "decode1":
         wl = DecodeWorkload(ctx, 0, copies=12, past=args.past)
         ms = timed_graph(wl.step_one_layer, args.steps, args.warmup, 1)
         b = wl.bytes_per_step / N_LAYERS
-        res = {"us_per_step": ms * 1e3, "gbs": b / (ms * 1e-3) / 1e9}
+        res = {"us_per_step": ms * 1e3, "gbs": b / (ms * 1e-3) / 1e9,
+               "stream_same_bytes_us": stream_reference(ctx, b, args.steps, args.warmup, 1)[0]}
     elif args.only == "ragged":
         ms, b, _ = run_ragged(ctx, 0, 1, args.steps, args.warmup, check=False, fmt=args.kv,
                               nseq_total=args.ragged_seqs)
@@ -956,18 +978,24 @@ def main():
     # the headline's output against the oracle (after its timed region); every rank checks
     parity = reduce_parity(wl.check(), world) if not args.quick else None
 
+    # speed of light of the same bytes read by one plain streaming launch, timed the same way
+    sol_us, _ = stream_reference(ctx, wl.bytes_per_step, args.steps, args.warmup, world)
+
     side = {}
     if not args.no_side:
         # the drop-in per-layer call: one p2p_decode_step with one layer (8.4 MB)
         ms1 = max_over_ranks(timed_graph(wl.step_one_layer, args.steps, args.warmup, world),
                              world)
         b1 = wl.bytes_per_step / N_LAYERS
+        sol1_us, _ = stream_reference(ctx, b1, args.steps, args.warmup, world)
         side["decode_one_layer"] = {
             "workload": "one attention layer per call (what engine.js:245-259 dispatches "
                         "between that layer's GEMMs), ctx 4096+1, 32q/8kv, rotating over 72 "
                         "layer caches (605 MB > L2)",
             "gbs_per_gpu": round(b1 / (ms1 * 1e-3) / 1e9, 1), "us_per_step": round(ms1 * 1e3, 3),
-            "hbm_frac_of_measured": round(b1 / (ms1 * 1e-3) / 1e9 / hbm_peak, 4)}
+            "hbm_frac_of_measured": round(b1 / (ms1 * 1e-3) / 1e9 / hbm_peak, 4),
+            "stream_same_bytes_us": round(sol1_us, 3),
+            "frac_of_stream": round(sol1_us / (ms1 * 1e3), 4)}
         for fused in (True, False):
             key = "decode_layers_with_projections" + ("" if fused else "_unfused")
             try:
@@ -1114,7 +1142,11 @@ def main():
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(per_gpu_gbs / hbm_peak, 4), "peak_kind": peak_kind,
                          "frac_of_nominal_8tbs": round(per_gpu_gbs / 8000.0, 4),
-                         "traffic": tr, "kernel": "decode_mma_kernel<G=4,fused,layers,cluster>"},
+                         "traffic": tr, "kernel": "decode_mma_kernel<G=4,fused,layers,cluster>",
+                         "stream_same_bytes_us": round(sol_us, 3),
+                         "frac_of_stream": round(sol_us / (ms_max * 1e3), 4),
+                         "stream_note": "p2p_debug_stream_read: one plain streaming launch "
+                                        "over the same bytes per graph node, same rotation"},
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_sec * 1e6, 2),
                     "host": e2e_note,

@@ -367,6 +367,15 @@ p2p_status p2p_debug_set_alloc_limit(int64_t bytes);
  * 0 restores normal operation.  Exercises the bounded-wait path without any fault. */
 p2p_status p2p_debug_set_wait_deficit(int32_t bytes);
 
+/* Measurement reference, no counterpart in the reference: one launch that reads `bytes`
+ * (a multiple of 16) from the 16-byte aligned device buffer src once, with the plainest
+ * full-bandwidth access pattern (16-byte loads, eight in flight per thread, two 512-thread
+ * CTAs per SM), and XORs every 32-bit word into *xor_out (device memory; the caller zeroes
+ * it).  Timed like a decode step, it is the speed of light of streaming those bytes in one
+ * launch. */
+p2p_status p2p_debug_stream_read(p2p_ctx* ctx, const void* src, int64_t bytes,
+                                 uint32_t* xor_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -150,6 +150,7 @@ PROTOTYPES = {
         _st, [_v, _v, _pp, _v, _i64, _v, _v, _v, _v, _i64, _v, _i32, _i32, _v, _i64, _v]),
     "p2p_debug_set_alloc_limit": (_st, [_i64]),
     "p2p_debug_set_wait_deficit": (_st, [_i32]),
+    "p2p_debug_stream_read": (_st, [_v, _v, _i64, _v, _v]),
 }
 
 

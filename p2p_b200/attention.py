@@ -111,6 +111,15 @@ class Context:
     def sync(self, stream=None):
         self._chk(lib.p2p_sync(self.h, _stream(stream)))
 
+    def debug_stream_read(self, src: torch.Tensor, xor_out: torch.Tensor, nbytes=None,
+                          stream=None):
+        """Measurement reference: one launch streaming `nbytes` (default all) of `src` and
+        XOR-folding its 32-bit words into xor_out[0] (an int32 device tensor, zeroed by the
+        caller)."""
+        n = src.numel() * src.element_size() if nbytes is None else nbytes
+        self._chk(lib.p2p_debug_stream_read(self.h, _ptr(src), n, _ptr(xor_out),
+                                            _stream(stream)))
+
     # -- the shader entry points ----------------------------------------------------------------
     def qk_prep(self, prm: Params, qkv: torch.Tensor, norm_w: Optional[torch.Tensor], rope,
                 q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,

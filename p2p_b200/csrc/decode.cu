@@ -626,8 +626,12 @@ __global__ void __launch_bounds__(kThreads, 3)
   if (refused<MODE>(a, z)) return;  // rows beyond the cache: touch nothing
   const Seq<T, TC> sq = resolve<T, TC, MODE>(a, z);
   const int len = sq.past + 1;  // keys 0..past, key `past` is the new token
-  const int split_len = max(a.min_split, (ceil_div(len, ngrid) + 15) & ~15);
-  const int nsplit = ceil_div(len, split_len);
+  // Splits sized over the cache rows (fused: the new key is computed, not streamed), so that
+  // 4096 rows in 8 splits are 8 whole 64-key tiles each; the last split also takes the rest
+  // (at most one key more than split_len).
+  const int rows = FUSED ? len - 1 : len;
+  const int split_len = max(a.min_split, (ceil_div(max(rows, 1), ngrid) + 15) & ~15);
+  const int nsplit = min(ceil_div(len, split_len), ngrid);
   if (kPg && (split_len >> a.block_shift) + 2 > kPagedTableCap) {
     // a split longer than the block-table copy holds (the host sizes the grid so that this
     // does not happen); the same for every CTA of the sequence, so none of them starts
@@ -637,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   // A cluster CTA past the last split still takes part in the cluster barriers (empty range).
   if (!CL && split >= nsplit) return;
   const int j0 = min(split * split_len, len);
-  const int j1 = min(j0 + split_len, len);
+  const int j1 = split == nsplit - 1 ? len : min(j0 + split_len, len);
   const bool has_new = FUSED && j0 < j1 && j1 == len;
   const int jcopy = has_new ? sq.past : j1;  // rows streamed from the cache
   const int64_t kv_stride = int64_t(a.hkv) * D;
