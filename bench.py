@@ -216,10 +216,28 @@ def reduce_parity(p, world):
 # ---------------------------------------------------------------------------------------------
 # workloads
 
+def warm_up_agreed(fn, warmup, world):
+    """The untimed warm-up calls, then every rank learns whether any rank's failed (one
+    all-reduce): a library error on one rank only becomes the same P2PError on every rank, so
+    no rank is left waiting in a collective the others skipped."""
+    import torch
+    import p2p_b200
+    err = None
+    try:
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+    except p2p_b200.P2PError as e:
+        err = e
+    if world > 1 and max_over_ranks(1.0 if err is not None else 0.0, world) > 0 and err is None:
+        err = p2p_b200.P2PError(-1, "the leg failed on another rank")
+    if err is not None:
+        raise err
+
+
 def timed_loop(fn, steps, warmup, world, stream):
     import torch
-    for i in range(warmup):
-        fn(i)
+    warm_up_agreed(fn, warmup, world)
     barrier(world)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
@@ -237,9 +255,7 @@ def timed_graph(fn, steps, warmup, world, capture_error_mode="global"):
     replay (the K steps back to back on the device, no host launch overhead).  Legs with NCCL
     calls capture in "relaxed" mode (NCCL may enqueue from its own thread)."""
     import torch
-    for i in range(warmup):
-        fn(i)
-    torch.cuda.synchronize()
+    warm_up_agreed(fn, warmup, world)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, capture_error_mode=capture_error_mode):
         for i in range(steps):
@@ -504,7 +520,9 @@ def run_ragged(ctx, rank, world, steps, warmup, check=True, fmt="f16", nseq_tota
         nblk = (rows + RAGGED_BLOCK - 1) // RAGGED_BLOCK
         n_pages = int(nblk.sum())
         perm = np.random.default_rng(5 + rank).permutation(n_pages).astype(np.int32)
-        table = np.full((nseq, int(nblk.max())), -1, np.int32)
+        # as wide as max_past needs (the entry point checks max_past against max_blocks); on
+        # a rank whose longest sequence is shorter the extra entries stay -1 (never read)
+        table = np.full((nseq, max_past // RAGGED_BLOCK + 1), -1, np.int32)
         start = np.concatenate([[0], np.cumsum(nblk)[:-1]])
         for i in range(nseq):
             table[i, :nblk[i]] = perm[start[i]:start[i] + nblk[i]]
