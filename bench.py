@@ -1073,9 +1073,12 @@ def main():
                     "multicast": "flash epilogue stores every row once as NVLink multicast "
                                  "(NVSwitch writes every rank's output), then one ordering "
                                  "all-reduce"}
-            for s_tok in (2048, 16384):
+            for s_tok in (2048, 4096, 8192, 16384):
                 fl = prefill_flops(s_tok)
-                for variant in ("allgather", "scatter", "multicast"):
+                # the crossover sizes (4096, 8192) with the two assemblies that need no multicast
+                variants = (("allgather", "scatter", "multicast") if s_tok in (2048, 16384)
+                            else ("allgather", "scatter"))
+                for variant in variants:
                     key = f"prefill_head_{variant}_s{s_tok}"
                     try:
                         ms, timing, par, same = sharded_prefill_leg(ctx, comm, rank, world,
@@ -1100,11 +1103,12 @@ def main():
                 "tflops": round(vision_flops() / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2),
                 "parity": reduce_parity(v_par, world)}
         if world == 1:
-            for s_tok, steps in ((2048, 20), (16384, 5)):
+            # 4096 and 8192: the one-GPU side of the sharded prefill's crossover
+            for s_tok, steps in ((2048, 20), (4096, 10), (8192, 10), (16384, 5)):
                 key = "prefill" if s_tok == 2048 else f"prefill_s{s_tok}"
                 try:
                     r = run_prefill(ctx, steps=steps, warmup=5 if s_tok == 2048 else 3,
-                                    s=s_tok, copies=4 if s_tok == 2048 else 1)
+                                    s=s_tok, copies=4 if s_tok <= 4096 else 1)
                     fl = prefill_flops(s_tok)
                     pa, pb = r["ms_attn"], r["ms_both"]
                     side[key] = {
