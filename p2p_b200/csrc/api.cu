@@ -446,6 +446,10 @@ p2p_status p2p_sync(p2p_ctx* ctx, void* stream) {
     if (flags & p2p::kErrTimeout)
       return fail(ctx, P2P_ERR_TIMEOUT,
                   "a kernel's bounded wait on another CTA ran out; its output was not written");
+    if (flags & p2p::kErrLayout)
+      return fail(ctx, P2P_ERR_CUDA,
+                  "a kernel's dynamic shared memory did not start on the 1024-byte boundary "
+                  "its tiles need; that work was skipped");
     if (flags & p2p::kErrOutTokFull)
       return fail(ctx, P2P_ERR_INVALID_ARG,
                   "argmax_step: the step index in the meta buffer reached out_tok's capacity; "

@@ -187,6 +187,7 @@ struct FlashArgs {
 constexpr int kErrPosBeyondCache = 1;
 constexpr int kErrTimeout = 2;  // a bounded device-side wait ran out; that work was not written
 constexpr int kErrOutTokFull = 4;  // argmax_step: the step index reached out_tok's capacity
+constexpr int kErrLayout = 8;  // a kernel found its shared memory misplaced; it wrote nothing
 cudaError_t launch_flash(const FlashArgs& a, cudaStream_t s);
 
 }  // namespace p2p

@@ -6,21 +6,23 @@
 // q.k * scale, online softmax (running max / sum), P.V accumulated in f32, out = acc / sum in
 // f16 -- reorganised into 128 x 128 tiles on tcgen05 / TMEM / TMA:
 //
-//   CTA = one (image, q head, pair of 128-row q tiles); 12 warps in three warpgroups.  The
-//   producer warpgroup (warps 8-11) hands registers to the two softmax warpgroups with
-//   setmaxnreg (104 / 192 per thread) so the 128-score rows and their 64 packed P pairs
-//   stay in registers.
-//   warp 8      TMA producer: the two Q tiles once, then K/V tiles of 128 keys (SWIZZLE_128B)
-//               into a 5-stage ring shared by both q tiles; mbarrier complete_tx; single-CTA loads.
-//   warp 9      allocates 512 TMEM columns and issues tcgen05.mma (cta_group::1, f16) from the
-//               converged warp, one elected lane per MMA group:
+//   CTA = one (image, q head, 128-row q tile) with 8 warps, two CTAs per SM (NT = 1, the
+//   default), or one (image, q head, pair of q tiles) with 12 warps, one CTA per SM (NT = 2);
+//   the two independent pipelines of NT = 1 overlap each other better than the two softmax
+//   warpgroups of one NT = 2 CTA.  The producer warpgroup (warps 4NT .. 4NT+3) hands registers
+//   to the softmax warpgroup(s) with setmaxnreg so the 128-score rows and their 64 packed P
+//   pairs stay in registers.
+//   warp 4NT    TMA producer: the Q tile(s) once, then K/V tiles of 128 keys (SWIZZLE_128B)
+//               into a 3-stage (NT = 1) or 5-stage (NT = 2) ring; mbarrier complete_tx.
+//   warp 4NT+1  allocates 256 / 512 TMEM columns and issues tcgen05.mma (cta_group::1, f16)
+//               from the converged warp, one elected lane per MMA group:
 //                 S_w(j)  = Q_w K_j^T -> TMEM S_w   (M128 N128 K64)
 //                 O_w    += P_w(j) V_j -> TMEM O_w  (M128 N64 K128, A = P from TMEM, V an
 //                                                  MN-major shared-memory operand)
 //               S_w(j+1) is issued as soon as softmax warpgroup w has read S_w(j), so the
 //               tensor core computes it while the softmax of tile j runs.
-//   warps 0-3   softmax warpgroup 0 (q tile 0), warps 4-7 warpgroup 1 (q tile 1): one thread
-//               per q row (= TMEM lane).  tcgen05.ld of the S row; mask only on tiles that
+//   warps 0-3   softmax warpgroup 0 (q tile 0; NT = 2: warps 4-7 warpgroup 1, q tile 1): one
+//               thread per q row (= TMEM lane).  tcgen05.ld of the S row; mask only on tiles that
 //               cross the causal diagonal / the key end; row max with 3-input max; exp2 with
 //               the scale folded into one packed FFMA2 and evaluated two at a time, mostly by
 //               MUFU.EX2 on f16x2 and for 5 of every 16 pairs by a cubic on the FMA pipe (the
@@ -36,6 +38,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -47,20 +50,41 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;  // q rows per tile (two tiles per CTA)
+constexpr int BM = 128;  // q rows per tile
 constexpr int BN = 128;  // keys per tile
 constexpr int D = kHeadDim;
-constexpr int kStages = 5;  // K/V ring depth: TMA latency (~2 us under load) spans >1 tile
-// 12 warps (three warpgroups): 0-7 softmax (two warpgroups), 8 TMA, 9 MMA, 10-11 idle.  The
-// block launches with 168 registers per thread (the cap for 384 threads); the producer
-// warpgroup then gives registers back (104 each) and the softmax warpgroups take 192 each:
-// 8 * 32 * 192 + 4 * 32 * 104 = 62464 <= 384 * 168 = 64512, so the increase never waits.
-constexpr int kThreads = 384;
-constexpr int kSoftmaxRegs = 192;
-constexpr int kProducerRegs = 104;
-static_assert(8 * 32 * kSoftmaxRegs + 4 * 32 * kProducerRegs <= kThreads * 168, "register split");
+// Two layouts, NT = q tiles per CTA:
+//  NT = 2: 12 warps (three warpgroups): 0-7 softmax (two warpgroups), 8 TMA, 9 MMA, 10-11
+//    idle; 5-stage K/V ring; 512 TMEM columns; one CTA per SM.  The block launches with 168
+//    registers per thread (the cap for 384 threads); the producer warpgroup then gives
+//    registers back (104 each) and the softmax warpgroups take 192 each:
+//    8 * 32 * 192 + 4 * 32 * 104 = 62464 <= 384 * 168 = 64512, so the increase never waits.
+//  NT = 1: 8 warps: 0-3 softmax, 4 TMA, 5 MMA, 6-7 idle; 3-stage ring; 256 TMEM columns; two
+//    CTAs per SM (112 KB of shared memory each), each with its own pipeline.  Launched with
+//    128 registers per thread: 4 * 32 * 192 + 4 * 32 * 64 = 32768 = 256 * 128.
+template <int NT>
+struct Cfg;
+template <>
+struct Cfg<2> {
+  static constexpr int kStages = 5;  // TMA latency (~2 us under load) spans >1 tile
+  static constexpr int kThreads = 384, kMinBlocks = 1, kLaunchRegs = 168;
+  static constexpr int kSoftmaxRegs = 192, kProducerRegs = 104;
+  static constexpr uint32_t kTmemCols = 512;
+};
+template <>
+struct Cfg<1> {
+  static constexpr int kStages = 3;
+  static constexpr int kThreads = 256, kMinBlocks = 2, kLaunchRegs = 128;
+  static constexpr int kSoftmaxRegs = 192, kProducerRegs = 64;
+  static constexpr uint32_t kTmemCols = 256;
+};
+template <int NT>
+constexpr bool split_fits() {
+  return NT * 4 * 32 * Cfg<NT>::kSoftmaxRegs + 4 * 32 * Cfg<NT>::kProducerRegs <=
+         Cfg<NT>::kThreads * Cfg<NT>::kLaunchRegs;
+}
+static_assert(split_fits<1>() && split_fits<2>(), "register split");
 constexpr uint32_t kTileBytes = BM * D * 2;  // one Q, K or V tile: 16 KB
-constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (factor 256)
 #ifndef P2P_POLY_PAIRS
@@ -74,13 +98,15 @@ __device__ __forceinline__ uint32_t col_s(int w) { return uint32_t(w) * 256u; }
 __device__ __forceinline__ uint32_t col_p(int w) { return uint32_t(w) * 256u + 128u; }
 __device__ __forceinline__ uint32_t col_o(int w) { return uint32_t(w) * 256u + 192u; }
 
-struct __align__(1024) Smem {
-  __half q[2][BM * D];
-  __half k[kStages][BN * D];
-  __half v[kStages][BN * D];
+// The tiles start on a 1024-byte boundary (128-byte swizzle); every tile is 16 KB.
+template <int NT, int ST>
+struct __align__(128) SmemT {
+  __half q[NT][BM * D];
+  __half k[ST][BN * D];
+  __half v[ST][BN * D];
   uint64_t bar_q;
-  uint64_t k_full[kStages], v_full[kStages], kv_empty[kStages];
-  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t k_full[ST], v_full[ST], kv_empty[ST];
+  uint64_t s_full[NT], s_free[NT], p_full[NT], pv_done[NT];
   uint32_t tmem_base;
   volatile int abort_flag;
 };
@@ -99,7 +125,7 @@ struct FlashParams {
   int32_t s_q, s_kv;
   int32_t hq, hkv;
   int32_t causal;
-  int32_t n_qpairs;
+  int32_t n_qpairs;  // work items along the q rows (pairs of q tiles for NT = 2, tiles for 1)
   float scale_log2;
   int32_t wait_deficit;  // test hook (0 normally): the Q-tile wait then runs out
   // Non-causal 1-D grid (lin != 0): CTA i < n_pair covers item i (a pair of q tiles); CTA
@@ -109,6 +135,7 @@ struct FlashParams {
 };
 
 // Bounded wait on an mbarrier phase; false when the limit passed or another role gave up.
+template <class Smem>
 __device__ __forceinline__ bool wait_bar(Smem& s, uint64_t* bar, uint32_t parity,
                                          int32_t* err) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -129,14 +156,24 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <int NT>
+__global__ void __launch_bounds__(Cfg<NT>::kThreads, Cfg<NT>::kMinBlocks)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ FlashParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                     ~uintptr_t(1023));
+  using Smem = SmemT<NT, Cfg<NT>::kStages>;
+  constexpr int kStages = Cfg<NT>::kStages;
+  constexpr int kTmaWarp = 4 * NT, kMmaWarp = 4 * NT + 1;  // the producer warpgroup's roles
+  extern __shared__ uint8_t smem_raw[];  // alignment not assumed: checked below
+  // NT = 2 pads its dynamic shared memory to reach the 1024-byte boundary; NT = 1 has no room
+  // for the pad (two CTAs per SM) and needs the allocation to start there
+  const uintptr_t sbase = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
+  if (NT == 1 && sbase != reinterpret_cast<uintptr_t>(smem_raw)) {
+    if (threadIdx.x == 0) atomicOr(p.err, kErrLayout);
+    return;
+  }
+  Smem& s = *reinterpret_cast<Smem*>(sbase);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Launched behind QK_PREP (programmatic dependent launch): the CTA may be resident before
   // that kernel completes, and reads nothing it writes (q, the cache rows, meta) before this.
@@ -158,14 +195,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     qp = p.causal ? (p.n_qpairs - 1 - int(blockIdx.y)) : int(blockIdx.y);
     h = blockIdx.x;
     b = blockIdx.z;
-    q_row0 = qp * 2 * BM;
+    q_row0 = qp * NT * BM;
   }
   const int kh = h / (p.hq / p.hkv);
   const int pos0 = p.causal ? (p.meta ? int(p.meta[0]) : p.pos0_host) : 0;
   // valid q rows of the two tiles and the keys each needs (causal: 0 .. pos0 + last row)
   const int rows0 = min(BM, p.s_q - q_row0);
   if (rows0 <= 0) return;  // single mode: the second tile of a pair whose q rows end earlier
-  const int rows1 = single ? 0 : max(0, min(BM, p.s_q - q_row0 - BM));
+  const int rows1 = (NT == 1 || single) ? 0 : max(0, min(BM, p.s_q - q_row0 - BM));
   const int64_t kend0 = p.causal ? int64_t(pos0) + q_row0 + rows0 : int64_t(p.s_kv);
   const int64_t kend1 =
       rows1 == 0 ? 0 : (p.causal ? int64_t(pos0) + q_row0 + BM + rows1 : int64_t(p.s_kv));
@@ -187,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.v_full[i], 1);
       mbar_init(&s.kv_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NT; ++i) {
       mbar_init(&s.s_full[i], 1);
       mbar_init(&s.s_free[i], 4);
       mbar_init(&s.p_full[i], 4);
@@ -196,15 +233,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     s.abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 9) tmem_alloc(&s.tmem_base, kTmemCols);
+  if (warp == kMmaWarp) tmem_alloc(&s.tmem_base, Cfg<NT>::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
-  if (warp >= 8) {
-  regs_dec<kProducerRegs>();  // the whole producer warpgroup, before its warps part ways
-  if (warp == 8) {
+  if (warp >= 4 * NT) {
+  regs_dec<Cfg<NT>::kProducerRegs>();  // the whole producer warpgroup, before it splits
+  if (warp == kTmaWarp) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tensormap(&tm_q);
@@ -238,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     // The whole warp runs this loop with warp-uniform descriptors; lane 0 alone polls the
     // mbarriers and broadcasts the outcome, and one elected lane issues each MMA group and
@@ -286,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) {
         tc_fence_after();
         if (n_kv0 > 0) issue_s(0, 0);
-        if (n_kv1 > 0) issue_s(1, 0);
+        if (NT > 1 && n_kv1 > 0) issue_s(NT - 1, 0);
       }
       for (int j = 0; ok && j < n_max; ++j) {
         const int st = j % kStages;
@@ -299,10 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             issue_s(0, st1);
           }
-          if (j + 1 < n_kv1) {
-            if (!wait_warp(&s.s_free[1], j & 1)) break;
+          if (NT > 1 && j + 1 < n_kv1) {
+            if (!wait_warp(&s.s_free[NT - 1], j & 1)) break;
             tc_fence_after();
-            issue_s(1, st1);
+            issue_s(NT - 1, st1);
           }
         }
         if (!wait_warp(&s.v_full[st], (j / kStages) & 1)) break;
@@ -319,10 +356,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           issue_pv(0, st, j > 0);
         }
-        if (j < n_kv1) {
-          if (!wait_warp(&s.p_full[1], j & 1)) break;
+        if (NT > 1 && j < n_kv1) {
+          if (!wait_warp(&s.p_full[NT - 1], j & 1)) break;
           tc_fence_after();
-          issue_pv(1, st, j > 0);
+          issue_pv(NT - 1, st, j > 0);
         }
         if (elect_one()) mma_commit(&s.kv_empty[st]);
         __syncwarp();
@@ -331,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   } else {
     // ------------------------------------------------------------------ softmax warpgroups
-    regs_inc<kSoftmaxRegs>();
+    regs_inc<Cfg<NT>::kSoftmaxRegs>();
     const int w = warp >> 2;           // q tile of this warpgroup
     const int r = threadIdx.x & 127;   // q row within the tile = TMEM lane
     const uint32_t lane_addr = tmem + (uint32_t((warp & 3) * 32) << 16);
@@ -480,9 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, Cfg<NT>::kTmemCols);
   }
 }
 
@@ -516,6 +553,49 @@ bool make_map(CUtensorMap* m, const void* base, int64_t width, int64_t ld, int64
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// One launch of flash_fwd_kernel<NT> (programmatic stream serialization: it may become
+// resident while the previous kernel of the stream finishes; see grid_dependency_wait).
+template <int NT>
+cudaError_t launch_nt(FlashParams& p, CUtensorMap& tq, CUtensorMap& tk, CUtensorMap& tv,
+                      dim3 grid, cudaStream_t stream) {
+  // NT = 2 pads its shared memory to a 1024-byte boundary; NT = 1 must fit twice per SM
+  const size_t smem = sizeof(SmemT<NT, Cfg<NT>::kStages>) + (NT == 2 ? 1024 : 0);
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(flash_fwd_kernel<NT>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(flash_fwd_kernel<NT>,
+                                      cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      int(cudaSharedmemCarveoutMaxShared));
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  void* args[] = {&tq, &tk, &tv, &p};
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(Cfg<NT>::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at{};
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(&flash_fwd_kernel<NT>), args);
+}
+
+// q tiles per CTA: 1 (two independent CTAs per SM; measured faster on every shape: vision
+// 97.7 vs 111.3 us, causal S = 2048 37.0 vs 38.1 us, S = 16384 1423 vs 1518 us), or 2 with
+// P2P_FLASH_TILES=2 for comparison measurements.
+int flash_tiles_per_cta(const FlashArgs&) {
+  static const int forced = [] {
+    const char* e = getenv("P2P_FLASH_TILES");
+    return e ? atoi(e) : 0;
+  }();
+  return forced == 2 ? 2 : 1;
+}
+
 }  // namespace
 
 cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
@@ -546,31 +626,15 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
   p.hq = a.hq;
   p.hkv = a.hkv;
   p.causal = a.causal;
-  p.n_qpairs = (a.s_q + 2 * BM - 1) / (2 * BM);
   p.scale_log2 = a.scale_log2;
   p.wait_deficit = a.wait_deficit;
-  const size_t smem = sizeof(Smem) + 1024;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(flash_fwd_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  });
-  if (attr_err != cudaSuccess) return attr_err;
-  void* args[] = {&tq, &tk, &tv, &p};
-  auto launch = [&](dim3 grid) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute at{};
-    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at.val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = &at;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(&flash_fwd_kernel), args);
-  };
+  const int nt = flash_tiles_per_cta(a);
+  if (nt == 1) {
+    p.n_qpairs = (a.s_q + BM - 1) / BM;  // one q tile per CTA
+    if (p.n_qpairs > 65535) return cudaErrorInvalidValue;
+    return launch_nt<1>(p, tq, tk, tv, dim3(a.hq, p.n_qpairs, a.batch), stream);
+  }
+  p.n_qpairs = (a.s_q + 2 * BM - 1) / (2 * BM);
   // Non-causal (all items equal): when the items do not fill the last wave of one CTA per SM,
   // the last R pairs run as 2R one-tile CTAs at the end of the same grid (the block scheduler
   // hands them out last, to the SMs that free up first).  A one-tile CTA has its softmax
@@ -582,11 +646,11 @@ cudaError_t launch_flash(const FlashArgs& a, cudaStream_t stream) {
     if (tail > 0 && 2 * tail <= a.num_sms && n_items + tail <= INT32_MAX) {
       p.lin = 1;
       p.n_pair = int32_t(n_items - tail);
-      return launch(dim3(unsigned(n_items + tail)));
+      return launch_nt<2>(p, tq, tk, tv, dim3(unsigned(n_items + tail)), stream);
     }
   }
   if (p.n_qpairs > 65535) return cudaErrorInvalidValue;
-  return launch(dim3(a.hq, p.n_qpairs, a.batch));
+  return launch_nt<2>(p, tq, tk, tv, dim3(a.hq, p.n_qpairs, a.batch), stream);
 }
 
 }  // namespace p2p
