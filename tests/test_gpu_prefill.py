@@ -219,3 +219,33 @@ def test_prefill_device_position_beyond_cache_is_refused(ctx):
     ctx.attn(prm, q, kc, vc, out, m_tokens=m, use_meta=True)
     ctx.sync()
     assert bool(torch.isfinite(out.float()).all())
+
+
+@pytest.mark.parametrize("scale_in", [1.0, 0.5])
+def test_prefill_s2048_with_norm_weights_full_oracle(ctx, oracle, scale_in):
+    """Config 3 through the engine's two dispatches (QK_PREP with learned norm weights, then
+    ATTN) at S = 2048, 32 q / 8 kv heads, q/k/v N(0,1) unscaled and x0.5: every output row
+    against the oracle; max-abs also held to the 2e-3 cap on its own."""
+    import p2p_b200
+    hq, hkv, m = 32, 8, 2048
+    rng = np.random.default_rng(20480 + int(10 * scale_in))
+    qkv = (scale_in * rng.standard_normal((m, (hq + 2 * hkv) * D))).astype(np.float16)
+    nw = (1 + 0.2 * rng.standard_normal(2 * D)).astype(np.float16)
+    rope = oracle.rope_table(m)
+    kc_o = np.zeros((m, hkv, D), np.float16)
+    vc_o = np.zeros_like(kc_o)
+    q_o = np.zeros((m, hq * D), np.float16)
+    oracle.qk_prep(hq, hkv, D, qkv, nw, rope, q_o, kc_o, vc_o, 0, m)
+    want = np.zeros((m, hq * D), np.float16)
+    oracle.attn(hq, hkv, D, q_o, kc_o, vc_o, want, 0, m)
+    prm = p2p_b200.Params(hq, hkv)
+    kc = torch.zeros((m, hkv, D), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    q = torch.zeros((m, hq * D), dtype=torch.float16, device="cuda")
+    out = torch.zeros_like(q)
+    ctx.qk_prep(prm, dev(qkv), dev(nw), dev(rope), q, kc, vc, pos0=0, m_tokens=m)
+    ctx.attn(prm, q, kc, vc, out, pos0=0, m_tokens=m)
+    assert np.array_equal(bits(host(q)), bits(q_o))
+    assert np.array_equal(bits(host(kc)), bits(kc_o))
+    max_abs, _ = assert_close(host(out), want, what=f"prefill S=2048 x{scale_in} with norm")
+    assert max_abs <= 2e-3
