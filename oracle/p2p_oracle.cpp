@@ -342,6 +342,39 @@ void p2p_or_gemv_q4(int k, int n_rows, const uint16_t* x, const uint32_t* wq, co
   }
 }
 
+// kernels.js:70-145 (GEMM, the prompt-chunk form of the same MatMulNBits projection):
+// Y[m * y_stride + y_off + n] = f16(sum_k f32(X[m][k]) * W[n][k]) with the dequantised weight
+// W[n][k] = (f32(q) - zp) * scale rounded to f32 first (kernels.js:116-121), and the sum taken
+// over k in increasing order, one product and one addition at a time (kernels.js:125-133: every
+// thread adds its 32 k of a block in order, block after block).
+void p2p_or_gemm_q4(int m_rows, int k, int n_rows, const uint16_t* x, const uint32_t* wq,
+                    const uint16_t* sc, const uint32_t* zp, uint16_t* y, int64_t y_stride,
+                    int64_t y_off) {
+  const int nb = k / 32, zr = (nb + 1) / 2, wpr = k / 8;
+  std::vector<float> wd(size_t(n_rows) * k);
+#pragma omp parallel for schedule(static)
+  for (int n = 0; n < n_rows; ++n)
+    for (int kb = 0; kb < nb; ++kb) {
+      const float s = f16_to_f32(sc[int64_t(n) * nb + kb]);
+      const int64_t zi = int64_t(n) * zr + (kb >> 1);
+      const uint32_t zb = (zp[zi >> 2] >> ((zi & 3) * 8)) & 255u;  // kernels.js:16-19
+      const float z = float((zb >> ((kb & 1) * 4)) & 15u);
+      for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t word = wq[int64_t(n) * wpr + kb * 4 + wi];
+        for (int i = 0; i < 8; ++i)
+          wd[size_t(n) * k + kb * 32 + wi * 8 + i] = (float((word >> (i * 4)) & 15u) - z) * s;
+      }
+    }
+#pragma omp parallel for schedule(static)
+  for (int m = 0; m < m_rows; ++m)
+    for (int n = 0; n < n_rows; ++n) {
+      float c = 0.0f;
+      const float* w = wd.data() + size_t(n) * k;
+      for (int kk = 0; kk < k; ++kk) c += f16_to_f32(x[int64_t(m) * k + kk]) * w[kk];
+      y[int64_t(m) * y_stride + y_off + n] = f32_to_f16(c);
+    }
+}
+
 void p2p_or_quantize_q8(const uint16_t* src, int8_t* dst, int64_t rows, int hkv, int d,
                         const float* scale, int per_channel) {
   const int64_t chan = int64_t(hkv) * d;

@@ -83,6 +83,9 @@ void p2p_or_attn_ragged_h(int hq, int hkv, int d, float scale, const uint16_t* q
  * o_proj projections around the attention path (engine.js:202-204, :224) for one token. */
 void p2p_or_gemv_q4(int k, int n_rows, const uint16_t* x, const uint32_t* wq, const uint16_t* sc,
                     const uint32_t* zp, uint16_t* y, int64_t y_off);
+void p2p_or_gemm_q4(int m_rows, int k, int n_rows, const uint16_t* x, const uint32_t* wq,
+                    const uint16_t* sc, const uint32_t* zp, uint16_t* y, int64_t y_stride,
+                    int64_t y_off);
 /* The int8 KV cache (the reference bundle's GroupQueryAttention int8 cache: quantise
  * clamp(roundeven(x / scale), -128, 127), dequantise f32(q) * scale, scale per tensor or per
  * (kv head, dim) channel): conversion of f16 rows, and ATTN (kernels.js:268-319) per sequence

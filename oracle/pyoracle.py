@@ -60,6 +60,7 @@ def lib():
         L.p2p_or_vision_attn_h.argtypes = [_i, _i, _f, _i, _i, _p, _p, _p, _p, _i64]
         L.p2p_or_quantize_q8.argtypes = [_p, _p, _i64, _i, _i, _p, _i]
         L.p2p_or_gemv_q4.argtypes = [_i, _i, _p, _p, _p, _p, _p, _i64]
+        L.p2p_or_gemm_q4.argtypes = [_i, _i, _i, _p, _p, _p, _p, _p, _i64, _i64]
         L.p2p_or_attn_ragged_q8.argtypes = [_i, _i, _i, _f, _p, _i64, _p, _p, _p, _p, _i, _p, _p,
                                             _i, _p, _i64]
         L.p2p_or_attn_exact.argtypes = [_i, _i, _i, _d, _p, _i64, _p, _p, _p, _i64, _i, _i]
@@ -164,6 +165,35 @@ def ref_gemv(x, wq, sc, zp, y, y_off=0):
     rc = ref().ref_GEMV(_bind(x, wq, sc, zp, y), ovr, (n + 7) // 8, 1, 1)
     if rc:
         raise RuntimeError(f"ref_GEMV failed ({rc})")
+
+
+def gemm_q4(x, wq, sc, zp, y=None, y_stride=None, y_off=0):
+    """kernels.js:70-145: Y[m][y_off + n] = f16(X[m] . W[n]) for an [M][K] f16 block X (rows of
+    y_stride elements in y).  Returns y (float16, [M][y_stride])."""
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    m, k = x.shape
+    n, wpr = wq.shape
+    assert wpr * 8 == k
+    if y_stride is None:
+        y_stride = y_off + n
+    if y is None:
+        y = np.zeros((m, y_stride), np.float16)
+    lib().p2p_or_gemm_q4(m, k, n, _ptr(x), _ptr(np.ascontiguousarray(wq, np.uint32)),
+                         _ptr(np.ascontiguousarray(sc, np.float16)),
+                         _ptr(np.ascontiguousarray(zp, np.uint32)), _ptr(y), y_stride, y_off)
+    return y
+
+
+def ref_gemm(x, wq, sc, zp, y, y_stride, y_off=0):
+    """The reference's own GEMM shader (oracle/_ref), dispatched as engine.js does: (N/64,
+    M/64) workgroups of 256, M from the meta buffer's second word."""
+    m, k = x.shape
+    n = wq.shape[0]
+    mt = np.array([0, m, 0, 0], np.uint32)
+    ovr = (C.c_double * 4)(k, n, y_stride, y_off)
+    rc = ref().ref_GEMM(_bind(x, wq, sc, zp, y, mt), ovr, (n + 63) // 64, (m + 63) // 64, 1)
+    if rc:
+        raise RuntimeError(f"ref_GEMM failed ({rc})")
 
 
 def random_q4(rng, n, k):

@@ -1,5 +1,5 @@
-"""Translate the reference's attention WGSL shaders (and ARGMAX, which advances the meta
-buffer) into C++ for host execution.
+"""Translate the reference's attention WGSL shaders (with ARGMAX, which advances the meta
+buffer, and the MatMulNBits GEMV / GEMM around the path) into C++ for host execution.
 
 TEST INFRASTRUCTURE ONLY.  The reference keeps its GPU code as WGSL template strings inside
 JavaScript modules (src/scripts/lfm-engine/kernels.js, vision-kernels.js) and runs them
@@ -28,6 +28,7 @@ SHADERS = [
     ("src/scripts/lfm-engine/vision-kernels.js", "VISION_ATTN"),
     ("src/scripts/lfm-engine/kernels.js", "ARGMAX"),
     ("src/scripts/lfm-engine/kernels.js", "GEMV"),
+    ("src/scripts/lfm-engine/kernels.js", "GEMM"),
 ]
 
 TYPES = {"f32": "float", "f16": "wgsl::h16", "u32": "uint32_t", "i32": "int32_t"}
@@ -59,6 +60,8 @@ def translate_expr(line: str) -> str:
     line = re.sub(r"\blet\s+(\w+)\s*=", r"const auto \1 =", line)
     line = re.sub(r"\bvar\s+(\w+)\s*:\s*(\w+)\s*=", lambda m: f"{TYPES[m.group(2)]} {m.group(1)} =", line)
     line = re.sub(r"\bvar\s+(\w+)\s*=", r"auto \1 =", line)
+    line = re.sub(r"\barray<vec4<f32>,\s*4>\(", "wgsl::array4v(", line)
+    line = re.sub(r"\bvec4<f32>\(", "wgsl::vec4f(", line)
     line = re.sub(r"\b(f32|f16|u32)\(", r"wgsl::\1(", line)
     line = re.sub(r"\bexp\(", "wgsl::exp_(", line)
     line = re.sub(r"\binverseSqrt\(", "wgsl::inverseSqrt(", line)

@@ -91,6 +91,28 @@ struct uvec3 {
   uint32_t x, y, z;
 };
 
+// vec4<f32> and array<vec4<f32>, 4> (the GEMM's 4x4 accumulators): componentwise, every
+// operation separately rounded.
+struct vec4f {
+  float c[4];
+  explicit vec4f(float v) : c{v, v, v, v} {}
+  vec4f(float a, float b, float d, float e) : c{a, b, d, e} {}
+  float& operator[](uint32_t i) { return c[i]; }
+  float operator[](uint32_t i) const { return c[i]; }
+};
+inline vec4f operator*(float s, const vec4f& v) {
+  return vec4f(s * v.c[0], s * v.c[1], s * v.c[2], s * v.c[3]);
+}
+inline vec4f& operator+=(vec4f& a, const vec4f& b) {
+  for (int i = 0; i < 4; ++i) a.c[i] += b.c[i];
+  return a;
+}
+struct array4v {
+  vec4f v[4];
+  array4v(const vec4f& a, const vec4f& b, const vec4f& d, const vec4f& e) : v{a, b, d, e} {}
+  vec4f& operator[](uint32_t i) { return v[i]; }
+};
+
 // One invocation = one coroutine.
 struct Task {
   struct promise_type {

@@ -66,6 +66,20 @@ def gemv_case(name: str, seed: int, k: int, n: int):
     np.savez_compressed(OUT / f"{name}.npz", x=x, wq=wq, sc=sc, zp=zp, y=y)
 
 
+def gemm_case(name: str, seed: int, m: int, k: int, n: int, y_off: int):
+    """The GEMM shader (kernels.js:70-145): a prompt chunk's 4-bit projection (x [m][k] ->
+    y [m][y_off + n] inside rows of y_off + n + 5), (N/64, M/64) workgroups as engine.js
+    dispatches it."""
+    rng = np.random.default_rng(seed)
+    wq, sc, zp = O.random_q4(rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    stride = y_off + n + 5
+    y = np.zeros((m, stride), np.float16)
+    O.ref_gemm(x, wq, sc, zp, y, stride, y_off)
+    np.savez_compressed(OUT / f"{name}.npz", x=x, wq=wq, sc=sc, zp=zp, y=y,
+                        y_off=np.int32(y_off))
+
+
 def main():
     if not O.ref_available():
         raise SystemExit("oracle/_ref not built: run `make -C oracle` where the reference exists")
@@ -73,6 +87,7 @@ def main():
     decoder_case("decoder_decode_16x8", seed=202, pos0=130, m=1, with_norm_scale=0.1)
     vision_case("vision_s70_h12", seed=303, s_tokens=70)
     gemv_case("gemv_q4_k1024_n96", seed=404, k=1024, n=96)
+    gemm_case("gemm_q4_m70_k256_n96", seed=505, m=70, k=256, n=96, y_off=7)
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

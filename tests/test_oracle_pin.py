@@ -189,6 +189,30 @@ def test_gemv_restatement_matches_reference_shader(oracle, k, n, seed):
     assert np.array_equal(_bits(got), _bits(want))
 
 
+@ref_only
+@pytest.mark.parametrize("m,k,n,seed", [(5, 64, 70, 1), (64, 256, 128, 2), (130, 96, 40, 3),
+                                         (77, 1024, 200, 4)])
+def test_gemm_restatement_matches_reference_shader(oracle, m, k, n, seed):
+    """kernels.js:70-145 (GEMM): the restatement equals the translated shader bit for bit,
+    with partial 64-row / 64-column tiles, an odd block count (K = 96) and the output written
+    at an offset inside wider rows (Y_STRIDE, Y_OFF)."""
+    rng = np.random.default_rng(100 + seed)
+    wq, sc, zp = oracle.random_q4(rng, n, k)
+    x = (2 * rng.standard_normal((m, k))).astype(np.float16)
+    stride, off = n + 9, 3
+    want = np.zeros((m, stride), np.float16)
+    oracle.ref_gemm(x, wq, sc, zp, want, stride, off)
+    got = oracle.gemm_q4(x, wq, sc, zp, y_stride=stride, y_off=off)
+    assert np.array_equal(_bits(got), _bits(want))
+
+
+def test_gemm_restatement_reproduces_golden(oracle, golden_dir):
+    z = np.load(golden_dir / "gemm_q4_m70_k256_n96.npz")
+    got = oracle.gemm_q4(z["x"], z["wq"], z["sc"], z["zp"], y_stride=int(z["y"].shape[1]),
+                         y_off=int(z["y_off"]))
+    assert np.array_equal(_bits(got), _bits(z["y"]))
+
+
 def test_gemv_restatement_reproduces_golden(oracle, golden_dir):
     z = np.load(golden_dir / "gemv_q4_k1024_n96.npz")
     got = oracle.gemv_q4(z["x"], z["wq"], z["sc"], z["zp"])
