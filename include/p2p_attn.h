@@ -325,6 +325,30 @@ p2p_status p2p_qkv_gemv_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
                              void* q_out, void* k_cache, void* v_cache, int64_t kv_cap_tokens,
                              const uint32_t* meta_dev, int32_t pos, void* stream);
 
+/* kernels.js:70-145 (GEMM): the same projection for a prompt chunk of M > 1 tokens,
+ * y[m * ld_y + y_off + n] = f16(x[m] . W[n]) for x [M][ld_x].  The weights are dequantised to
+ * f16 (each value rounded once; the shader keeps f32) into a context workspace and multiplied
+ * on the tensor cores with f32 accumulation, so results agree with the shader to f16 rounding,
+ * not bit for bit.  No k limit; n a multiple of 64; x and y rows 16-byte aligned (ld_x, ld_y
+ * and y_off multiples of 8).  The workspace is shared by the context's calls: calls on
+ * different streams of one context must not overlap. */
+p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int64_t ld_x,
+                       int32_t m_tokens, void* y, int64_t ld_y, int64_t y_off, void* stream);
+
+/* The q/k/v projections of a prompt chunk (three GEMM dispatches, engine.js:202-204) with
+ * QK_PREP (kernels.js:216-266) in the epilogue: from the normed hidden rows x [M][ld_x], the
+ * f16 qkv row of every token is formed on the tensor cores (never written to memory) and its
+ * heads are normed and rotated as QK_PREP does -- rotated q to q_out [M][ld_q], rotated k and
+ * raw v to cache rows pos0 .. pos0+M-1 (pos0 = meta_dev[0] when meta_dev is not NULL).
+ * Given the same f16 projection the QK_PREP part is bit-identical to the shader.  Positions as
+ * in p2p_qk_prep; alignment as in p2p_gemm_q4. */
+p2p_status p2p_qkv_gemm_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const void* x,
+                             int64_t ld_x, const p2p_q4_matrix* wq, const p2p_q4_matrix* wk,
+                             const p2p_q4_matrix* wv, const void* norm_w, const void* rope,
+                             void* q_out, int64_t ld_q, void* k_cache, void* v_cache,
+                             int64_t kv_cap_tokens, const uint32_t* meta_dev, int32_t pos0,
+                             int32_t m_tokens, void* stream);
+
 /* vision-kernels.js:176-258 (VISION_ATTN, dispatched (NUM_HEADS, S) at vision.js:271-276),
  * batched: out[b] = softmax(scale * q[b] k[b]^T) v[b] per head, no mask, tcgen05 kernel.
  * q/k/v/out are [batch][s_tokens][ld] with head h at column h*D. */

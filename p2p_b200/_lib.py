@@ -141,6 +141,10 @@ PROTOTYPES = {
     "p2p_qkv_gemv_prep": (
         _st, [_v, _pp, _v, C.POINTER(Q4Matrix), C.POINTER(Q4Matrix), C.POINTER(Q4Matrix), _v,
               _v, _v, _v, _v, _i64, _v, _i32, _v]),
+    "p2p_gemm_q4": (_st, [_v, C.POINTER(Q4Matrix), _v, _i64, _i32, _v, _i64, _i64, _v]),
+    "p2p_qkv_gemm_prep": (
+        _st, [_v, _pp, _v, _i64, C.POINTER(Q4Matrix), C.POINTER(Q4Matrix), C.POINTER(Q4Matrix),
+              _v, _v, _v, _i64, _v, _v, _i64, _v, _i32, _i32, _v]),
     "p2p_comm_unique_id": (_st, [C.c_char_p]),
     "p2p_comm_create": (_st, [_v, _i32, _i32, C.c_char_p, _i32, C.POINTER(_v)]),
     "p2p_comm_destroy": (_st, [_v]),

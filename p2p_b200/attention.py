@@ -304,6 +304,28 @@ class Context:
             _ptr(k_cache), _ptr(v_cache), k_cache.shape[0], self.meta_ptr if use_meta else None,
             pos, _stream(stream)))
 
+    def gemm_q4(self, w, x: torch.Tensor, y: torch.Tensor, y_off: int = 0,
+                m_tokens: Optional[int] = None, stream=None):
+        """kernels.js:70-145: y[m][y_off + n] = f16(x[m] . W[n]) for a prompt chunk."""
+        mw = self.q4(w)
+        m = x.shape[0] if m_tokens is None else m_tokens
+        self._chk(lib.p2p_gemm_q4(self.h, C.byref(mw), _ptr(x), x.stride(0), m, _ptr(y),
+                                  y.stride(0), y_off, _stream(stream)))
+
+    def qkv_gemm_prep(self, prm: Params, x: torch.Tensor, wq, wk, wv, norm_w, rope,
+                      q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+                      pos0: int = 0, m_tokens: Optional[int] = None, use_meta: bool = False,
+                      stream=None):
+        """q/k/v projections of a prompt chunk with QK_PREP in the epilogue (rotated q to
+        q_out [M][Hq*64], k/v to cache rows pos0..pos0+M-1)."""
+        mq, mk, mv = self.q4(wq), self.q4(wk), self.q4(wv)
+        m = x.shape[0] if m_tokens is None else m_tokens
+        self._chk(lib.p2p_qkv_gemm_prep(
+            self.h, C.byref(prm.c()), _ptr(x), x.stride(0), C.byref(mq), C.byref(mk),
+            C.byref(mv), _ptr(norm_w), rope if isinstance(rope, C.c_void_p) else _ptr(rope),
+            _ptr(q_out), q_out.stride(0), _ptr(k_cache), _ptr(v_cache), k_cache.shape[0],
+            self.meta_ptr if use_meta else None, pos0, m, _stream(stream)))
+
     def attn_prefill_sharded(self, comm, prm: Params, qkv_local: torch.Tensor, norm_w, rope,
                              k_cache: torch.Tensor, v_cache: torch.Tensor, out: torch.Tensor, *,
                              pos0: int = 0, m_tokens: Optional[int] = None,

@@ -41,6 +41,8 @@ struct p2p_ctx {
   size_t partials_bytes = 0;
   int32_t* counters = nullptr;
   size_t counters_bytes = 0;
+  void* w16 = nullptr;  // prompt-chunk projections: the dequantised f16 weights
+  size_t w16_bytes = 0;
   std::map<std::tuple<int, int, double, int>, void*> rope;
   std::map<void*, size_t> shared;  // p2p_shared_alloc buffers and their sizes
   std::string err;
@@ -148,6 +150,22 @@ float eff_scale(const p2p_attn_params* prm) {
   return prm->scale > 0.f ? prm->scale : 1.0f / std::sqrt(float(prm->head_dim));
 }
 float eff_eps(const p2p_attn_params* prm) { return prm->eps > 0.f ? prm->eps : 1e-5f; }
+
+// Grows one library-owned device buffer to at least `need` bytes; rare, so the device is
+// synchronised first (no launch may still use the old buffer).
+p2p_status ensure_buffer(p2p_ctx* ctx, void** ptr, size_t* have, size_t need, const char* what) {
+  if (need <= *have) return P2P_OK;
+  cudaDeviceSynchronize();
+  dev_free(*ptr, *have);
+  *ptr = nullptr;
+  *have = 0;
+  void* p = nullptr;
+  if (dev_alloc(&p, need) != cudaSuccess)
+    return fail(ctx, P2P_ERR_OOM, "%s of %zu bytes", what, need);
+  *ptr = p;
+  *have = need;
+  return P2P_OK;
+}
 
 p2p_status ensure_workspace(p2p_ctx* ctx, size_t pbytes, size_t cbytes, cudaStream_t s) {
   if (pbytes > ctx->partials_bytes) {
@@ -398,6 +416,7 @@ p2p_status p2p_ctx_destroy(p2p_ctx* ctx) {
   if (ctx->host_err) cudaFreeHost(ctx->host_err);
   dev_free(ctx->partials, ctx->partials_bytes);
   dev_free(ctx->counters, ctx->counters_bytes);
+  dev_free(ctx->w16, ctx->w16_bytes);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
   return P2P_OK;
@@ -942,13 +961,12 @@ p2p_status p2p_attn_decode_kv(p2p_ctx* ctx, const p2p_attn_params* prm,
 namespace {
 // Validation of one MatMulNBits matrix argument: rows, k, alignment of its three buffers.
 p2p_status check_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, int32_t n, int32_t k,
-                    const char* what) {
+                    const char* what, int32_t max_k = p2p::kGemvMaxK) {
   if (!w || !w->qweight || !w->scales || !w->zero_points)
     return fail(ctx, P2P_ERR_INVALID_ARG, "%s: NULL matrix or buffer", what);
-  if ((n >= 0 && w->n != n) || w->n <= 0 || w->k != k || k <= 0 || k % 32 ||
-      k > p2p::kGemvMaxK)
+  if ((n >= 0 && w->n != n) || w->n <= 0 || w->k != k || k <= 0 || k % 32 || k > max_k)
     return fail(ctx, P2P_ERR_INVALID_ARG, "%s: n %d (want %d), k %d (want %d; a multiple of "
-                "32, at most %d)", what, w->n, n, w->k, k, p2p::kGemvMaxK);
+                "32, at most %d)", what, w->n, n, w->k, k, max_k);
   if ((reinterpret_cast<uintptr_t>(w->qweight) | reinterpret_cast<uintptr_t>(w->zero_points)) &
           3u ||
       reinterpret_cast<uintptr_t>(w->scales) & 1u)
@@ -983,6 +1001,8 @@ p2p_status p2p_qkv_gemv_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
                              const uint32_t* meta_dev, int32_t pos, void* stream) {
   p2p_status st = check_params(ctx, prm, false);
   if (st != P2P_OK) return st;
+  if (prm->dtype != P2P_F16)
+    return fail(ctx, P2P_ERR_UNSUPPORTED, "qkv_gemv_prep: the projection path is f16");
   const int k = wq ? wq->k : 0;
   const int qn = prm->num_heads * prm->head_dim, kn = prm->num_kv_heads * prm->head_dim;
   if ((st = check_q4(ctx, wq, qn, k, "qkv_gemv_prep (wq)")) != P2P_OK) return st;
@@ -1000,6 +1020,105 @@ p2p_status p2p_qkv_gemv_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
                      eff_eps(prm), ctx->dev_err};
   cudaError_t e = p2p::launch_qkv_prep(a, pick_stream(ctx, stream));
   if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemv_prep launch");
+  return P2P_OK;
+}
+
+p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int64_t ld_x,
+                       int32_t m_tokens, void* y, int64_t ld_y, int64_t y_off, void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  p2p_status st = check_q4(ctx, w, -1, w ? w->k : 0, "gemm_q4", INT32_MAX);
+  if (st != P2P_OK) return st;
+  if (!x || !y || m_tokens < 0 || ld_x < w->k || y_off < 0 || ld_y < y_off + w->n)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "gemm_q4: M %d ld_x %lld ld_y %lld y_off %lld",
+                m_tokens, (long long)ld_x, (long long)ld_y, (long long)y_off);
+  if (w->n % 64 || !aligned16(x) || (ld_x % 8) || !aligned16(y) || (ld_y % 8) || (y_off % 8))
+    return fail(ctx, P2P_ERR_INVALID_ARG,
+                "gemm_q4: n a multiple of 64, 16-byte aligned rows of x and y, y_off % 8 == 0");
+  if (m_tokens == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  st = ensure_buffer(ctx, &ctx->w16, &ctx->w16_bytes, size_t(w->n) * w->k * 2,
+                     "dequantised weights");
+  if (st != P2P_OK) return st;
+  cudaError_t e = p2p::launch_dequant_q4(to_q4(w), w->k, ctx->w16, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_q4 dequant launch");
+  p2p::GemmArgs a{};
+  a.x = x;
+  a.ld_x = ld_x;
+  a.w16 = ctx->w16;
+  a.m = m_tokens;
+  a.n = w->n;
+  a.k = w->k;
+  a.y = y;
+  a.ld_y = ld_y;
+  a.y_off = y_off;
+  a.err = ctx->dev_err;
+  e = p2p::launch_gemm(a, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_q4 launch");
+  return P2P_OK;
+}
+
+p2p_status p2p_qkv_gemm_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const void* x,
+                             int64_t ld_x, const p2p_q4_matrix* wq, const p2p_q4_matrix* wk,
+                             const p2p_q4_matrix* wv, const void* norm_w, const void* rope,
+                             void* q_out, int64_t ld_q, void* k_cache, void* v_cache,
+                             int64_t kv_cap_tokens, const uint32_t* meta_dev, int32_t pos0,
+                             int32_t m_tokens, void* stream) {
+  p2p_status st = check_params(ctx, prm, false);
+  if (st != P2P_OK) return st;
+  if (prm->dtype != P2P_F16)
+    return fail(ctx, P2P_ERR_UNSUPPORTED, "qkv_gemm_prep: the projection path is f16");
+  const int qn = prm->num_heads * prm->head_dim, kn = prm->num_kv_heads * prm->head_dim;
+  const int k = wq ? wq->k : 0;
+  if ((st = check_q4(ctx, wq, qn, k, "qkv_gemm_prep (wq)", INT32_MAX)) != P2P_OK) return st;
+  if ((st = check_q4(ctx, wk, kn, k, "qkv_gemm_prep (wk)", INT32_MAX)) != P2P_OK) return st;
+  if ((st = check_q4(ctx, wv, kn, k, "qkv_gemm_prep (wv)", INT32_MAX)) != P2P_OK) return st;
+  if (!x || !rope || !q_out || !k_cache || !v_cache || m_tokens < 0 || ld_x < k || ld_q < qn ||
+      kv_cap_tokens <= 0 || (!meta_dev && pos0 < 0))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "qkv_gemm_prep: M %d ld_x %lld ld_q %lld pos0 %d",
+                m_tokens, (long long)ld_x, (long long)ld_q, pos0);
+  if (!aligned16(x) || (ld_x % 8) || !aligned16(q_out) || (ld_q % 8) || !aligned16(rope) ||
+      !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "qkv_gemm_prep: 16-byte aligned rows needed");
+  if (!meta_dev && int64_t(pos0) + m_tokens > kv_cap_tokens)
+    return fail(ctx, P2P_ERR_KV_FULL, "qkv_gemm_prep: pos0 %d + M %d > cache rows %lld", pos0,
+                m_tokens, (long long)kv_cap_tokens);
+  if (m_tokens == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  const int n = qn + 2 * kn;
+  st = ensure_buffer(ctx, &ctx->w16, &ctx->w16_bytes, size_t(n) * k * 2, "dequantised weights");
+  if (st != P2P_OK) return st;
+  // one [q rows | k rows | v rows][k] operand: the projection's columns are the qkv row's
+  __half* w16 = static_cast<__half*>(ctx->w16);
+  cudaError_t e = p2p::launch_dequant_q4(to_q4(wq), k, w16, s);
+  if (e == cudaSuccess) e = p2p::launch_dequant_q4(to_q4(wk), k, w16 + int64_t(qn) * k, s);
+  if (e == cudaSuccess)
+    e = p2p::launch_dequant_q4(to_q4(wv), k, w16 + int64_t(qn + kn) * k, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemm_prep dequant launch");
+  p2p::GemmArgs a{};
+  a.x = x;
+  a.ld_x = ld_x;
+  a.w16 = w16;
+  a.m = m_tokens;
+  a.n = n;
+  a.k = k;
+  a.prep = 1;
+  a.hq = prm->num_heads;
+  a.hkv = prm->num_kv_heads;
+  a.norm_w = norm_w;
+  a.rope = rope;
+  a.eps = eff_eps(prm);
+  a.q_out = q_out;
+  a.ld_q = ld_q;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.kv_cap = kv_cap_tokens;
+  a.meta = meta_dev;
+  a.pos0 = pos0;
+  a.err = ctx->dev_err;
+  e = p2p::launch_gemm(a, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemm_prep launch");
   return P2P_OK;
 }
 

@@ -124,6 +124,32 @@ struct Q4Matrix {
   int32_t n;
 };
 constexpr int kGemvMaxK = 4608;  // the GEMV shader's workgroup copy of x (kernels.js:31)
+// Prompt-chunk projection on the tensor cores: y = x . W^T with W the dequantised f16 [n][k];
+// plain (rows into y) or with QK_PREP on each 64-column head (prep != 0: columns [0, 64 hq)
+// are q heads, then hkv k heads, then hkv v heads; q to q_out, k/v to cache rows pos0 + m).
+struct GemmArgs {
+  const void* x;  // f16 [m][ld_x]
+  int64_t ld_x;
+  const void* w16;  // f16 [n][k]
+  int32_t m, n, k;  // n a multiple of 64
+  void* y;          // plain: f16 rows [m][ld_y], outputs at column y_off
+  int64_t ld_y, y_off;
+  int32_t prep;
+  int32_t hq, hkv;
+  const void* norm_w;  // [q(64) | k(64)] or nullptr
+  const void* rope;
+  float eps;
+  void* q_out;
+  int64_t ld_q;
+  void* k_cache;
+  void* v_cache;
+  int64_t kv_cap;
+  const uint32_t* meta;  // nullable -> pos0
+  int32_t pos0;
+  int32_t* err;
+};
+cudaError_t launch_dequant_q4(const Q4Matrix& w, int32_t k, void* dst_f16, cudaStream_t s);
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
 struct GemvArgs {
   Q4Matrix w;
   int32_t k;
