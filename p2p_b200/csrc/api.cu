@@ -1023,6 +1023,15 @@ p2p_status p2p_qkv_gemv_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
   return P2P_OK;
 }
 
+// P2P_GEMM_BN=256|192|128 fixes the GEMM's output tile width (tests compare the widths on one
+// shape); unset or anything else: chosen per shape.
+static int gemm_bn_override() {
+  const char* v = std::getenv("P2P_GEMM_BN");
+  if (!v) return 0;
+  const int bn = std::atoi(v);
+  return (bn == 256 || bn == 192 || bn == 128) ? bn : 0;
+}
+
 p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int64_t ld_x,
                        int32_t m_tokens, void* y, int64_t ld_y, int64_t y_off, void* stream) {
   if (!ctx) return P2P_ERR_INVALID_ARG;
@@ -1053,6 +1062,7 @@ p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int6
   a.ld_y = ld_y;
   a.y_off = y_off;
   a.err = ctx->dev_err;
+  a.bn = gemm_bn_override();
   e = p2p::launch_gemm(a, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_q4 launch");
   return P2P_OK;
@@ -1117,6 +1127,7 @@ p2p_status p2p_qkv_gemm_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
   a.meta = meta_dev;
   a.pos0 = pos0;
   a.err = ctx->dev_err;
+  a.bn = gemm_bn_override();
   e = p2p::launch_gemm(a, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemm_prep launch");
   return P2P_OK;

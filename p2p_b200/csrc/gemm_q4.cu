@@ -7,19 +7,27 @@
 // f32(x) * w over k in f32.  Here:
 //   dequant_q4_kernel  the weights once per call to f16 [n][k] in a workspace (the one
 //                      deviation from the shader: w rounded to f16, relative error <= 2^-12);
-//   gemm_kernel        y = x . W^T on tcgen05: 128 x 256 output tiles, K in 64-wide stages
-//                      through a 4-deep TMA ring (128-byte swizzle, both operands K-major),
-//                      f32 accumulation in 256 TMEM columns, one elected lane issuing the MMAs;
-//                      the epilogue warps (thread = output row = TMEM lane) round to f16 and
-//                      either store the rows, or run QK_PREP on each 64-column head of the row
-//                      (the qkv block never reaches memory): q / k heads normed and rotated
-//                      exactly as the QK_PREP shader does (bit-identical given the same f16
-//                      projection), rotated q to q_out, k and v to the cache rows pos0 + m.
+//   gemm_kernel        y = x . W^T on tcgen05, persistent (one CTA per SM walking 128 x BN
+//                      output tiles, BN = 256, 192 or 128 chosen per shape for the shortest
+//                      makespan over the SMs): K in 64-wide stages through a 4- to 6-deep TMA
+//                      ring (128-byte swizzle, both operands K-major) that runs on across tile
+//                      boundaries, f32 accumulation in two BN-column TMEM buffers so that the
+//                      epilogue of one tile overlaps the MMAs of the next, one elected lane
+//                      issuing the MMAs; eight epilogue warps (two per TMEM lane quarter, heads
+//                      of 64 columns dealt alternately; thread = output row) copy their
+//                      accumulators out, hand the buffer back, round to
+//                      f16 and either store the rows, or run QK_PREP on each 64-column head of
+//                      the row (the qkv block never reaches memory): q / k heads normed and
+//                      rotated exactly as the QK_PREP shader does (bit-identical given the same
+//                      f16 projection), rotated q to q_out, k and v to the cache rows pos0 + m.
 // Every mbarrier wait is bounded (about one second): a wait that gives up sets the device error
-// word, the CTA stops its roles, frees its TMEM and returns.
+// word, every role of the CTA stops, the copies and MMAs in flight are waited for, the TMEM is
+// freed and the CTA returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <climits>
 #include <mutex>
 
 #include "common.cuh"
@@ -33,19 +41,32 @@ namespace {
 using namespace sm100;
 
 constexpr int GBM = 128;  // output rows (tokens) per tile
-constexpr int GBN = 256;  // output columns per tile (four 64-column heads)
 constexpr int GBK = 64;   // k per stage (one 128-byte swizzled row per operand row)
-constexpr int GST = 4;    // ring depth
-constexpr int kGemmThreads = 192;  // warps 0-3 epilogue (TMEM lane quarters), 4 TMA, 5 MMA
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each owning 128 of the 256 columns
+constexpr int kTmaWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
+constexpr int kGemmThreads = 32 * (kEpiWarps + 2);
 constexpr uint32_t kATile = GBM * GBK * 2;  // 16 KB
-constexpr uint32_t kBTile = GBN * GBK * 2;  // 32 KB
-constexpr uint32_t kAccCols = GBN;          // f32 accumulator columns
 constexpr uint64_t kGemmWaitNs = 1000000000ull;
 
+// Output tile width BN (a multiple of the 64-column head): the ring takes as many stages as fit
+// in about 192 KB of shared memory; two BN-column accumulators, TMEM allocated in powers of 2.
+template <int BN>
+struct GemmCfg {
+  static_assert(BN == 256 || BN == 192 || BN == 128, "tile width");
+  static constexpr int kStages = BN == 256 ? 4 : BN == 192 ? 5 : 6;
+  static constexpr uint32_t kBTile = BN * GBK * 2;
+  static constexpr uint32_t kAccCols = BN == 128 ? 256 : 512;
+  static constexpr int kHeads = BN / kHeadDim;
+};
+
+template <int BN>
 struct __align__(1024) GemmSmem {
-  __half a[GST][GBM * GBK];
-  __half b[GST][GBN * GBK];
-  uint64_t full[GST], empty[GST], acc_full;
+  static constexpr int ST = GemmCfg<BN>::kStages;
+  __half a[ST][GBM * GBK];
+  __half b[ST][BN * GBK];
+  uint64_t full[ST], empty[ST];     // TMA -> MMA, MMA -> TMA (per ring stage)
+  uint64_t acc_full[2], acc_empty[2];  // MMA -> epilogue, epilogue -> MMA (per TMEM buffer)
+  uint64_t mma_done;                // every MMA of the CTA has completed (teardown)
   uint32_t tmem_base;
   volatile int abort_flag;
   float nw[2 * kHeadDim];  // fused QK_PREP: [q norm | k norm] as f32
@@ -53,6 +74,7 @@ struct __align__(1024) GemmSmem {
 
 struct GemmParams {
   int32_t m, n, k;
+  int32_t tiles_n, tiles;  // output tiles along n, in all
   __half* y;
   int64_t ld_y, y_off;
   int32_t prep;
@@ -70,19 +92,27 @@ struct GemmParams {
   int32_t* err;
 };
 
-__device__ __forceinline__ bool gemm_wait(GemmSmem& s, uint64_t* bar, uint32_t parity,
-                                          int32_t* err) {
+__device__ __forceinline__ bool gemm_wait(volatile int& abort_flag, uint64_t* bar,
+                                          uint32_t parity, int32_t* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (s.abort_flag) return false;
+    if (abort_flag) return false;
     if (globaltimer_ns() - t0 > kGemmWaitNs) {
-      s.abort_flag = 1;
+      abort_flag = 1;
       atomicOr(err, kErrTimeout);
       return false;
     }
   }
+}
+
+// A wait of a warp: lane 0 polls, the verdict is shared.
+__device__ __forceinline__ bool gemm_wait_warp(volatile int& abort_flag, uint64_t* bar,
+                                               uint32_t parity, int32_t* err, int lane) {
+  bool r = true;
+  if (lane == 0) r = gemm_wait(abort_flag, bar, parity, err);
+  return __shfl_sync(0xffffffffu, r ? 1 : 0, 0) != 0;
 }
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -90,17 +120,19 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
-  GemmSmem& s = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  using Cfg = GemmCfg<BN>;
+  constexpr int GST = Cfg::kStages;
+  GemmSmem<BN>& s = *reinterpret_cast<GemmSmem<BN>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Launched behind the previous kernel of the stream (programmatic dependent launch): nothing
-  // it writes (x, the caches) is read or written before that kernel has completed.
+  // it writes (x, the weights, the caches) is read or written before that kernel has completed.
   grid_dependency_wait();
-  const int n0 = int(blockIdx.x) * GBN, m0 = int(blockIdx.y) * GBM;
   const int nk = (p.k + GBK - 1) / GBK;
 
   if (threadIdx.x == 0) {
@@ -108,102 +140,147 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
-    mbar_init(&s.acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], kEpiWarps);
+    }
+    mbar_init(&s.mma_done, 1);
     s.abort_flag = 0;
     fence_barrier_init();
   }
   if (p.prep && threadIdx.x < 2 * kHeadDim)
     s.nw[threadIdx.x] = p.norm_w ? to_f32(p.norm_w[threadIdx.x]) : 0.f;
-  if (warp == 5) tmem_alloc(&s.tmem_base, kAccCols);
+  if (warp == kMmaWarp) tmem_alloc(&s.tmem_base, Cfg::kAccCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
-  if (warp == 4) {
+  if (warp == kTmaWarp) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tensormap(&tm_a);
       prefetch_tensormap(&tm_b);
-      int issued = 0;
-      for (int kt = 0; kt < nk; ++kt) {
-        const int st = kt % GST;
-        if (kt >= GST && !gemm_wait(s, &s.empty[st], ((kt / GST) - 1) & 1, p.err)) break;
-        mbar_arrive_expect_tx(&s.full[st], kATile + kBTile);
-        tma_load_2d(s.a[st], &tm_a, kt * GBK, m0, &s.full[st]);
-        tma_load_2d(s.b[st], &tm_b, kt * GBK, n0, &s.full[st]);
-        issued = kt + 1;
+      uint32_t g = 0;  // ring slot counter, continuous across tiles
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        const int m0 = (t / p.tiles_n) * GBM, n0 = (t % p.tiles_n) * BN;
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const uint32_t st = g % GST;
+          if (g >= GST && !gemm_wait(s.abort_flag, &s.empty[st], ((g / GST) - 1) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.full[st], kATile + Cfg::kBTile);
+          tma_load_2d(s.a[st], &tm_a, kt * GBK, m0, &s.full[st]);
+          tma_load_2d(s.b[st], &tm_b, kt * GBK, n0, &s.full[st]);
+        }
       }
-      if (s.abort_flag) {  // let the copies already in flight land before the CTA exits
-        for (int kt = max(0, issued - GST); kt < issued; ++kt) {
+      if (!ok) {  // let the copies already in flight land before the CTA exits
+        for (uint32_t h = g > GST ? g - GST : 0; h < g; ++h) {
           const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(&s.full[kt % GST], (kt / GST) & 1) &&
+          while (!mbar_try_wait(&s.full[h % GST], (h / GST) & 1) &&
                  globaltimer_ns() - t0 < kGemmWaitNs) {
           }
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = idesc_f16_f32(GBM, GBN, 0, 0);
-    static_assert(sizeof(s.a[0]) == 16384 && sizeof(s.b[0]) == 32768, "tile sizes");
+    constexpr uint32_t idesc = idesc_f16_f32(GBM, BN, 0, 0);
+    static_assert(sizeof(s.a[0]) == kATile && sizeof(s.b[0]) == Cfg::kBTile, "tile sizes");
     const uint64_t adesc0 = smem_desc_sw128(smem_u32(s.a[0]), 16, 1024);
     const uint64_t bdesc0 = smem_desc_sw128(smem_u32(s.b[0]), 16, 1024);
-    bool ok = true;
-    for (int kt = 0; kt < nk && ok; ++kt) {
-      const int st = kt % GST;
-      bool r = true;
-      if (lane == 0) r = gemm_wait(s, &s.full[st], (kt / GST) & 1, p.err);
-      ok = __shfl_sync(0xffffffffu, r ? 1 : 0, 0) != 0;
-      if (!ok) break;
+    bool ok = true, issued = false;
+    uint32_t g = 0;
+    int i = 0;  // tiles of this CTA
+    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++i) {
+      const int b = i & 1, u = i >> 1;  // accumulator buffer, its use count
+      if (u > 0 && !(ok = gemm_wait_warp(s.abort_flag, &s.acc_empty[b], (u - 1) & 1, p.err, lane))) break;
       tc_fence_after();
-      if (elect_one()) {
-        // a K16 step is +32 bytes (2 address units) inside the 128-byte swizzled rows; a
-        // stage is 1024 (A) / 2048 (B) address units further
-        const uint64_t ad = adesc0 + uint64_t(st) * 1024, bd = bdesc0 + uint64_t(st) * 2048;
+      const uint32_t acc = tmem + uint32_t(b * BN);
+      for (int kt = 0; kt < nk; ++kt, ++g) {
+        const uint32_t st = g % GST;
+        if (!(ok = gemm_wait_warp(s.abort_flag, &s.full[st], (g / GST) & 1, p.err, lane))) break;
+        tc_fence_after();
+        if (elect_one()) {
+          // a K16 step is +32 bytes (2 address units) inside the 128-byte swizzled rows; a
+          // stage is one tile (bytes / 16 address units) further
+          const uint64_t ad = adesc0 + uint64_t(st) * (kATile >> 4),
+                         bd = bdesc0 + uint64_t(st) * (Cfg::kBTile >> 4);
 #pragma unroll
-        for (int kk = 0; kk < GBK / 16; ++kk)
-          mma_f16_ss(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&s.empty[st]);
+          for (int kk = 0; kk < GBK / 16; ++kk)
+            mma_f16_ss(acc, ad + 2 * kk, bd + 2 * kk, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&s.empty[st]);
+        }
+        issued = true;
+        __syncwarp();
+      }
+      if (ok && elect_one()) mma_commit(&s.acc_full[b]);
+      __syncwarp();
+    }
+    // teardown: no MMA of this CTA may still be running when its TMEM is freed
+    if (issued) {
+      if (elect_one()) mma_commit(&s.mma_done);
+      __syncwarp();
+      if (lane == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&s.mma_done, 0) && globaltimer_ns() - t0 < kGemmWaitNs) {
+        }
       }
       __syncwarp();
     }
-    if (ok && elect_one()) mma_commit(&s.acc_full);
-    __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int row = warp * 32 + lane;  // = TMEM lane
-    const int m = m0 + row;
-    const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);
-    bool ok = gemm_wait(s, &s.acc_full, 0, p.err);
-    ok = __all_sync(0xffffffffu, ok);
-    int64_t pos = 0;
-    bool row_ok = m < p.m;
-    if (p.prep && row_ok) {
-      pos = int64_t(p.meta ? int(p.meta[0]) : p.pos0) + m;
-      if (pos >= p.kv_cap) {  // the cache cannot hold this row: touch nothing, report it
-        atomicOr(p.err, kErrPosBeyondCache);
-        row_ok = false;
-      }
-    }
-    if (ok) {
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;  // = TMEM lane
+    const uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
+    const int64_t kv_stride = int64_t(p.hkv) * kHeadDim;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++i) {
+      const int b = i & 1, u = i >> 1;
+      const int m0 = (t / p.tiles_n) * GBM, n0 = (t % p.tiles_n) * BN;
+      __syncwarp();  // lanes that skipped the previous tile's rows rejoin before the TMEM loads
+      if (!gemm_wait_warp(s.abort_flag, &s.acc_full[b], u & 1, p.err, lane)) break;
       tc_fence_after();
-      const int64_t kv_stride = int64_t(p.hkv) * kHeadDim;
-      for (int hc = 0; hc < GBN / kHeadDim; ++hc) {
-        const int n = n0 + hc * kHeadDim;
-        if (n >= p.n) break;  // the same for every thread of the CTA
+      // this warp's heads (half, half + 2) out of TMEM as f16 rows, then the buffer goes back
+      // to the MMA
+      Row64<__half> x[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int hc = half + 2 * j;
+        if (hc >= Cfg::kHeads) break;
         uint32_t v[2][32];
-        tmem_ld32(lane_addr + hc * kHeadDim, v[0]);
-        tmem_ld32(lane_addr + hc * kHeadDim + 32, v[1]);
+        const uint32_t a = lane_addr + uint32_t(b * BN + hc * kHeadDim);
+        tmem_ld32(a, v[0]);
+        tmem_ld32(a + 32, v[1]);
         tmem_ld_wait();
-        if (!row_ok) continue;
-        // the f16 projection row (what the GEMM shader stores)
-        Row64<__half> x;
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          x.w[e] = pack2(__uint_as_float(v[0][2 * e]), __uint_as_float(v[0][2 * e + 1]));
-          x.w[16 + e] = pack2(__uint_as_float(v[1][2 * e]), __uint_as_float(v[1][2 * e + 1]));
+          x[j].w[e] = pack2(__uint_as_float(v[0][2 * e]), __uint_as_float(v[0][2 * e + 1]));
+          x[j].w[16 + e] =
+              pack2(__uint_as_float(v[1][2 * e]), __uint_as_float(v[1][2 * e + 1]));
         }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[b]);
+
+      const int m = m0 + row;
+      if (m >= p.m) continue;
+      int64_t pos = 0;
+      if (p.prep) {
+        pos = int64_t(p.meta ? int(p.meta[0]) : p.pos0) + m;
+        if (pos >= p.kv_cap) {  // the cache cannot hold this row: touch nothing, report it
+          atomicOr(p.err, kErrPosBeyondCache);
+          continue;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int hc = half + 2 * j;
+        const int n = n0 + hc * kHeadDim;
+        if (hc >= Cfg::kHeads || n >= p.n) break;
         __half* dst;
         const int unit = n / kHeadDim;
         if (!p.prep) {
@@ -214,43 +291,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const bool isq = unit < p.hq;
           __half* out = isq ? p.q_out + int64_t(m) * p.ld_q + int64_t(unit) * kHeadDim
                             : p.k_cache + pos * kv_stride + int64_t(unit - p.hq) * kHeadDim;
-          rotate_row<__half>(x, p.norm_w ? s.nw + (isq ? 0 : kHeadDim) : nullptr, p.eps,
+          rotate_row<__half>(x[j], p.norm_w ? s.nw + (isq ? 0 : kHeadDim) : nullptr, p.eps,
                              p.rope + pos * kHeadDim,
                              [&](int kc, const float(&vals)[8]) { store8(out + 8 * kc, vals); });
           continue;
         }
         uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          d4[i] = make_uint4(x.w[4 * i], x.w[4 * i + 1], x.w[4 * i + 2], x.w[4 * i + 3]);
+        for (int q = 0; q < 8; ++q)
+          d4[q] = make_uint4(x[j].w[4 * q], x[j].w[4 * q + 1], x[j].w[4 * q + 2],
+                             x[j].w[4 * q + 3]);
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, kAccCols);
+    tmem_dealloc(tmem, Cfg::kAccCols);
   }
 }
 
-// Dequantised weights: dst[n][k] = f16((f32(q) - zp) * scale), one 8-value word per thread.
-__global__ void dequant_q4_kernel(const Q4Matrix w, int32_t k, __half* dst) {
-  const int wpr = k >> 3, nb = k >> 5, zr = (nb + 1) >> 1;
-  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= int64_t(w.n) * wpr) return;
-  const int64_t n = idx / wpr;
-  const int wi = int(idx % wpr), blk = wi >> 2;
-  const uint32_t word = w.qweight[idx];
-  const float sc = __half2float(w.scales[n * nb + blk]);
-  const uint32_t zb =
-      reinterpret_cast<const unsigned char*>(w.zero_points)[n * zr + (blk >> 1)];
-  const float z = float((zb >> ((blk & 1) * 4)) & 15u);
-  float vals[8];
+// Dequantised weights: dst[n][k] = f16((f32(q) - zp) * scale), one 32-value block (four words,
+// one scale, one zero point) per thread and step of a grid-stride loop over the matrix.
+// (A qweight base that is only 4-byte aligned is read word by word.)
+template <bool kVec>
+__global__ void __launch_bounds__(256) dequant_q4_kernel(const Q4Matrix w, int32_t k, __half* dst) {
+  const int nb = k >> 5, zr = (nb + 1) >> 1;
+  const int64_t total = int64_t(w.n) * nb;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t n = idx / nb;
+    const int blk = int(idx - n * nb);
+    uint4 words;
+    if constexpr (kVec) {
+      words = reinterpret_cast<const uint4*>(w.qweight)[idx];
+    } else {
+      const uint32_t* q = w.qweight + idx * 4;
+      words = make_uint4(q[0], q[1], q[2], q[3]);
+    }
+    const float sc = __half2float(w.scales[idx]);
+    const uint32_t zb =
+        reinterpret_cast<const unsigned char*>(w.zero_points)[n * zr + (blk >> 1)];
+    const float z = float((zb >> ((blk & 1) * 4)) & 15u);
+    const uint32_t wv[4] = {words.x, words.y, words.z, words.w};
+    __half* out = dst + idx * 32;  // = n * k + blk * 32
 #pragma unroll
-  for (int i = 0; i < 8; ++i) vals[i] = (float((word >> (4 * i)) & 15u) - z) * sc;
-  store8(dst + n * k + wi * 8, vals);
+    for (int j = 0; j < 4; ++j) {
+      float vals[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) vals[i] = (float((wv[j] >> (4 * i)) & 15u) - z) * sc;
+      store8(out + 8 * j, vals);
+    }
+  }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -285,27 +379,40 @@ bool map_k_major(CUtensorMap* m, const void* base, int64_t width, int64_t ld, in
 }  // namespace
 
 cudaError_t launch_dequant_q4(const Q4Matrix& w, int32_t k, void* dst, cudaStream_t s) {
-  const int64_t words = int64_t(w.n) * (k / 8);
-  if (words <= 0) return cudaSuccess;
+  const int64_t blocks = int64_t(w.n) * (k / 32);
+  if (blocks <= 0) return cudaSuccess;
+  if ((k % 32) || (reinterpret_cast<uintptr_t>(dst) & 15)) return cudaErrorInvalidValue;
   const int threads = 256;
-  dequant_q4_kernel<<<unsigned((words + threads - 1) / threads), threads, 0, s>>>(
-      w, k, static_cast<__half*>(dst));
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  // eight resident CTAs of 256 per SM; each thread walks its blocks with a stride of the grid
+  const unsigned grid =
+      unsigned(std::min<int64_t>((blocks + threads - 1) / threads, int64_t(std::max(sms, 1)) * 8));
+  if (reinterpret_cast<uintptr_t>(w.qweight) & 15)
+    dequant_q4_kernel<false><<<grid, threads, 0, s>>>(w, k, static_cast<__half*>(dst));
+  else
+    dequant_q4_kernel<true><<<grid, threads, 0, s>>>(w, k, static_cast<__half*>(dst));
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
-  if (a.m <= 0 || a.n <= 0) return cudaSuccess;
-  if (a.k <= 0 || (a.k % 8) || (a.ld_x % 8) || (reinterpret_cast<uintptr_t>(a.x) & 15) ||
-      (reinterpret_cast<uintptr_t>(a.w16) & 15) || (a.n % kHeadDim))
-    return cudaErrorInvalidValue;
+namespace {
+
+template <int BN>
+cudaError_t launch_gemm_bn(const GemmArgs& a, int sms, cudaStream_t stream) {
   CUtensorMap ta, tb;
   if (!map_k_major(&ta, a.x, a.k, a.ld_x, a.m, GBM) ||
-      !map_k_major(&tb, a.w16, a.k, a.k, a.n, GBN))
+      !map_k_major(&tb, a.w16, a.k, a.k, a.n, BN))
     return cudaErrorInvalidValue;
+  const int64_t tiles_n = (a.n + BN - 1) / BN, tiles = tiles_n * ((a.m + GBM - 1) / GBM);
+  if (tiles > INT32_MAX) return cudaErrorInvalidValue;
   GemmParams p{};
   p.m = a.m;
   p.n = a.n;
   p.k = a.k;
+  p.tiles_n = int32_t(tiles_n);
+  p.tiles = int32_t(tiles);
   p.y = static_cast<__half*>(a.y);
   p.ld_y = a.ld_y;
   p.y_off = a.y_off;
@@ -323,16 +430,16 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.meta = a.meta;
   p.pos0 = a.pos0;
   p.err = a.err;
-  const size_t smem = sizeof(GemmSmem) + 1024;
+  const size_t smem = sizeof(GemmSmem<BN>) + 1024;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(smem));
+    attr_err = cudaFuncSetAttribute(gemm_kernel<BN>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   });
   if (attr_err != cudaSuccess) return attr_err;
-  const dim3 grid(unsigned((a.n + GBN - 1) / GBN), unsigned((a.m + GBM - 1) / GBM));
-  if (grid.y > 65535) return cudaErrorInvalidValue;
+  // persistent: one CTA per SM (the shared ring admits no second), tiles strided over them
+  const dim3 grid(unsigned(std::min<int64_t>(tiles, sms)));
   void* args[] = {&ta, &tb, &p};
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
@@ -344,7 +451,49 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   at.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(&gemm_kernel), args);
+  return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(&gemm_kernel<BN>), args);
+}
+
+}  // namespace
+
+int gemm_tile_width(int64_t m, int64_t n, int sms) {
+  // The makespan of a persistent launch is the busiest SM's tiles: ceil(tiles / SMs) x BN
+  // columns of 128 rows.  Narrower tiles move more operand bytes per FLOP ((128 + BN) /
+  // (128 BN): +11 % at 192, +33 % at 128), weighed here as +15 % / +30 % of time (measured at
+  // 2048 x 2048 x 2048, 2048 / 8192 x 3072 x 2048 and 512 x 3072 x 2048 this picks the fastest
+  // width).
+  const int widths[3] = {256, 192, 128};
+  const double weight[3] = {1.0, 1.15, 1.3};
+  int best = 256;
+  double best_cost = 0;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t tiles = ((n + widths[i] - 1) / widths[i]) * ((m + GBM - 1) / GBM);
+    const int64_t rounds = (tiles + sms - 1) / sms;
+    const double cost = double(rounds) * widths[i] * weight[i];
+    if (i == 0 || cost < best_cost) {
+      best = widths[i];
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
+  if (a.m <= 0 || a.n <= 0) return cudaSuccess;
+  if (a.k <= 0 || (a.k % 8) || (a.ld_x % 8) || (reinterpret_cast<uintptr_t>(a.x) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.w16) & 15) || (a.n % kHeadDim))
+    return cudaErrorInvalidValue;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  sms = std::max(sms, 1);
+  switch (a.bn ? a.bn : gemm_tile_width(a.m, a.n, sms)) {
+    case 256: return launch_gemm_bn<256>(a, sms, stream);
+    case 192: return launch_gemm_bn<192>(a, sms, stream);
+    case 128: return launch_gemm_bn<128>(a, sms, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace p2p

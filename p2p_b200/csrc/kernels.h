@@ -147,7 +147,10 @@ struct GemmArgs {
   const uint32_t* meta;  // nullable -> pos0
   int32_t pos0;
   int32_t* err;
+  int32_t bn;  // output tile width 256 / 192 / 128; 0 = gemm_tile_width()
 };
+// The tile width with the shortest makespan of m x n over `sms` persistent CTAs.
+int gemm_tile_width(int64_t m, int64_t n, int sms);
 cudaError_t launch_dequant_q4(const Q4Matrix& w, int32_t k, void* dst_f16, cudaStream_t s);
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
 struct GemvArgs {

@@ -268,3 +268,24 @@ def test_gemm_in_a_graph(ctx, oracle):
         torch.cuda.synchronize()
         assert_gemm_close(host(y), oracle.gemm_q4(x, *w), gemm_tolerance(x, w), f"replay {it}")
     del graph
+
+
+@pytest.mark.parametrize("m,k,n", [(2048, 256, 3072), (300, 512, 2048), (70, 96, 192)])
+def test_gemm_tile_widths_agree(ctx, oracle, monkeypatch, m, k, n):
+    """The output tile width (256, 192 or 128 columns, chosen per shape) changes only which CTA
+    computes an element, not its K order: every width gives the same bits, within the bound."""
+    rng = np.random.default_rng(m + 3 * n)
+    w = oracle.random_q4(rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    g_w, g_x = dev_q4(w), dev(x)
+    outs = {}
+    for bn in ("256", "192", "128"):
+        monkeypatch.setenv("P2P_GEMM_BN", bn)
+        y = torch.zeros((m, n), dtype=torch.float16, device="cuda")
+        ctx.gemm_q4(g_w, g_x, y)
+        ctx.sync()
+        outs[bn] = host(y)
+    monkeypatch.delenv("P2P_GEMM_BN")
+    assert np.array_equal(bits(outs["256"]), bits(outs["192"]))
+    assert np.array_equal(bits(outs["256"]), bits(outs["128"]))
+    assert_gemm_close(outs["256"], oracle.gemm_q4(x, *w), gemm_tolerance(x, w), "widths")
