@@ -434,6 +434,91 @@ def run_decode_block(ctx, wl, steps, warmup, fused=True, sets=4):
     return ms, N_LAYERS * per_layer
 
 
+def gemm_flops(m, n, k):
+    return 2.0 * m * n * k
+
+
+def run_prefill_projections(ctx, steps, warmup, s=2048, sets=12, check=True):
+    """The 4-bit projections around the attention of an s-token prompt chunk of one LFM2.5-1.2B
+    layer (hidden 2048, 32q/8kv): the q/k/v projections with QK_PREP in the GEMM's epilogue
+    (p2p_qkv_gemm_prep: the qkv block never reaches memory), the reference's order (three GEMMs
+    into the qkv block, then QK_PREP; engine.js:202-204, :221) and the o_proj GEMM
+    (engine.js:224).  Hidden rows and weights rotate over `sets` copies (12 x 12.4 MB > L2).
+    Every call dequantises its weights to f16 first (inside the timed region)."""
+    import numpy as np
+    import torch
+    import p2p_b200
+    k = HQ * D
+    g = torch.Generator(device="cuda").manual_seed(77)
+    weights = [tuple(q4_weights(g, n, k) for n in (HQ * D, HKV * D, HKV * D, k))
+               for _ in range(sets)]
+    xs = [torch.randn((s, k), generator=g, device="cuda").half() for _ in range(sets)]
+    nw = (1 + 0.1 * torch.randn((2 * D,), generator=g, device="cuda")).half()
+    rope = ctx.rope_table(s, D, 1e6)
+    prm = p2p_b200.Params(HQ, HKV)
+    q = torch.zeros((s, HQ * D), device="cuda", dtype=torch.float16)
+    kc = torch.zeros((s, HKV, D), device="cuda", dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    q_u, kc_u, vc_u = torch.zeros_like(q), torch.zeros_like(kc), torch.zeros_like(vc)
+    qkv = torch.zeros((s, (HQ + 2 * HKV) * D), device="cuda", dtype=torch.float16)
+    y = torch.zeros((s, k), device="cuda", dtype=torch.float16)
+
+    def fused(i):
+        wq, wk, wv, _ = weights[i % sets]
+        ctx.qkv_gemm_prep(prm, xs[i % sets], wq, wk, wv, nw, rope, q, kc, vc, pos0=0)
+
+    def unfused(i):
+        wq, wk, wv, _ = weights[i % sets]
+        x = xs[i % sets]
+        ctx.gemm_q4(wq, x, qkv, y_off=0)
+        ctx.gemm_q4(wk, x, qkv, y_off=HQ * D)
+        ctx.gemm_q4(wv, x, qkv, y_off=(HQ + HKV) * D)
+        ctx.qk_prep(prm, qkv, nw, rope, q_u, kc_u, vc_u, pos0=0)
+
+    def oproj(i):
+        ctx.gemm_q4(weights[i % sets][3], xs[(i + 1) % sets], y)
+
+    res = {"ms_fused": timed_graph(fused, steps, warmup, 1),
+           "ms_unfused": timed_graph(unfused, steps, warmup, 1),
+           "ms_oproj": timed_graph(oproj, steps, warmup, 1)}
+    if check:
+        from oracle import pyoracle as O
+        fused(0)
+        unfused(0)
+        torch.cuda.synchronize()
+        same = all(torch.equal(a.view(torch.int16), b.view(torch.int16))
+                   for a, b in ((q, q_u), (kc, kc_u), (vc, vc_u)))
+        # GEMM rows against the oracle's restatement of the GEMM shader, within the bound of
+        # the f16 weight rounding: |err| <= 2^-10 sum_k |x_k w_k| + 1 f16 ulp
+        rows = sample_rows(s)
+        wq, wk, wv, _ = weights[0]
+        x_h = xs[0][rows].cpu().numpy()
+        want = np.zeros((len(rows), (HQ + 2 * HKV) * D), np.float16)
+        bound = np.zeros(want.shape, np.float64)
+        off = 0
+        for w in (wq, wk, wv):
+            wq_h = w[0].cpu().numpy().view(np.uint32)
+            sc_h = w[1].cpu().numpy()
+            zp_h = w[2].cpu().numpy().view(np.uint32)
+            n = wq_h.shape[0]
+            O.gemm_q4(x_h, wq_h, sc_h, zp_h, y=want, y_stride=want.shape[1], y_off=off)
+            wd = O.dequant_q4(wq_h, sc_h, zp_h).astype(np.float64)
+            bound[:, off:off + n] = 2.0 ** -10 * (np.abs(x_h.astype(np.float64)) @ np.abs(wd).T)
+            off += n
+        got = qkv[rows].cpu().numpy().astype(np.float64)
+        ulp = np.spacing(np.abs(want.astype(np.float16))).astype(np.float64)
+        ratio = np.abs(got - want.astype(np.float64)) / (bound + ulp)
+        res["parity"] = {
+            "fused_equals_unfused_bits": bool(same),
+            "gemm_rows_max_err_over_bound": float(f"{float(ratio.max()):.3e}"),
+            "ok": bool(same and ratio.max() <= 1.0 and np.isfinite(got).all()),
+            "checked": f"{len(rows)} qkv rows x 3072 against the oracle's GEMM (bound 2^-10 "
+                       "sum|x w| + 1 ulp); fused q / k / v cache rows bit-equal to GEMM x3 + "
+                       "QK_PREP on the GPU"}
+    del weights, xs
+    return res
+
+
 def e2e_decode(wl, steps, warmup):
     """The user-facing per-token call with host buffers: p2p_decode_step whose 6 qkv rows and 6
     output rows live in page-locked host memory, so the kernel itself reads the step's inputs
@@ -910,6 +995,13 @@ def run_only(ctx, args):
         fl = prefill_flops(args.prefill_s)
         res = {"us_attn": r["ms_attn"] * 1e3, "tflops_attn": fl / (r["ms_attn"] * 1e-3) / 1e12,
                "us_prep_plus_attn": r["ms_both"] * 1e3}
+    elif args.only == "projections":
+        r = run_prefill_projections(ctx, args.steps, args.warmup, s=args.prefill_s,
+                                    check=args.check)
+        res = {"us_qkv_fused": r["ms_fused"] * 1e3, "us_qkv_unfused": r["ms_unfused"] * 1e3,
+               "us_oproj": r["ms_oproj"] * 1e3,
+               "tflops_qkv_fused": gemm_flops(args.prefill_s, (HQ + 2 * HKV) * D, HQ * D)
+               / (r["ms_fused"] * 1e-3) / 1e12, **({"parity": r["parity"]} if args.check else {})}
     else:
         va, _ = run_vision(ctx, args.steps, args.warmup, check=False)
         res = {"us": va * 1e3, "tflops": vision_flops() / (va * 1e-3) / 1e12}
@@ -924,10 +1016,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip prefill/vision/ragged legs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", choices=["decode", "decode1", "ragged", "prefill", "vision", "block"],
+    ap.add_argument("--only", choices=["decode", "decode1", "ragged", "prefill", "vision", "block",
+                                       "projections"],
                     help="run one leg on one GPU and print its timing (profiling commands)")
     ap.add_argument("--past", type=int, default=PAST, help="decode context for --only decode")
     ap.add_argument("--prefill-s", type=int, default=2048, help="prompt length for --only prefill")
+    ap.add_argument("--check", action="store_true",
+                    help="with --only projections: also run the leg's output checks")
     ap.add_argument("--kv", default="f16", choices=["f16", "int8", "paged"],
                     help="KV-cache format for --only ragged")
     ap.add_argument("--ragged-seqs", type=int, default=256,
@@ -1123,6 +1218,27 @@ def main():
                         "parity": reduce_parity(r["parity"], 1)}
                 except p2p_b200.P2PError as e:
                     side[key] = {"error": str(e)}
+            try:
+                r = run_prefill_projections(ctx, steps=20, warmup=5)
+                fl_qkv = gemm_flops(2048, (HQ + 2 * HKV) * D, HQ * D)
+                fl_o = gemm_flops(2048, HQ * D, HQ * D)
+                pf, pu, po = r["ms_fused"], r["ms_unfused"], r["ms_oproj"]
+                side["prefill_projections"] = {
+                    "workload": "4-bit q/k/v projections + QK_PREP and o_proj of a 2048-token "
+                                "prompt chunk, one LFM2.5-1.2B layer (hidden 2048, 32q/8kv); "
+                                "weights dequantised to f16 in every call; 12 rotating sets "
+                                "(150 MB > L2)",
+                    "us_qkv_fused": round(pf * 1e3, 2),
+                    "us_qkv_unfused": round(pu * 1e3, 2),
+                    "us_oproj": round(po * 1e3, 2),
+                    "tflops_qkv_fused": round(fl_qkv / (pf * 1e-3) / 1e12, 1),
+                    "tflops_oproj": round(fl_o / (po * 1e-3) / 1e12, 1),
+                    "tensor_frac_of_measured_qkv": round(
+                        fl_qkv / (pf * 1e-3) / 1e12 / tensor_peak, 4),
+                    "hbm_bytes_saved": 2048 * (HQ + 2 * HKV) * D * 2 * 2,
+                    "parity": r["parity"]}
+            except p2p_b200.P2PError as e:
+                side["prefill_projections"] = {"error": str(e)}
             try:
                 va, v_par = run_vision(ctx, steps=20, warmup=5)
                 fl = vision_flops()

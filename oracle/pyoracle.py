@@ -184,6 +184,23 @@ def gemm_q4(x, wq, sc, zp, y=None, y_stride=None, y_off=0):
     return y
 
 
+def dequant_q4(wq, sc, zp):
+    """W[n][k] = (q - zp) * scale in f32, the block rule of kernels.js:22-68 / :70-145 (value
+    8w+i of a row is nibble i of word w; zero point of block b is nibble b&1 of byte b>>1 of the
+    row's ceil(K/64) bytes).  For error bounds; the GEMV / GEMM restatements do not use it."""
+    wq = np.ascontiguousarray(wq, np.uint32)
+    n, wpr = wq.shape
+    k = wpr * 8
+    q = (wq[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 15
+    q = q.reshape(n, k).astype(np.float32)
+    nb, zr = k // 32, (k // 32 + 1) // 2
+    zb = np.ascontiguousarray(zp).view(np.uint8)[: n * zr].reshape(n, zr)
+    blk = np.arange(nb)
+    z = ((zb[:, blk // 2] >> ((blk & 1) * 4)) & 15).astype(np.float32)
+    s = np.asarray(sc).astype(np.float32)
+    return (q - np.repeat(z, 32, axis=1)) * np.repeat(s, 32, axis=1)
+
+
 def ref_gemm(x, wq, sc, zp, y, y_stride, y_off=0):
     """The reference's own GEMM shader (oracle/_ref), dispatched as engine.js does: (N/64,
     M/64) workgroups of 256, M from the meta buffer's second word."""

@@ -49,23 +49,10 @@ def dev_q4(m):
     return dev(wq.view(np.int32)), dev(sc), dev(zp.view(np.int32))
 
 
-def dequant(wq, sc, zp):
-    """W[n][k] = (q - zp) * scale in f32 (kernels.js:70-145's block rule), for the error bound."""
-    n, wpr = wq.shape
-    k = wpr * 8
-    q = (wq[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 15
-    q = q.reshape(n, k).astype(np.float32)
-    nb, zr = k // 32, (k // 32 + 1) // 2
-    zb = zp.view(np.uint8)[: n * zr].reshape(n, zr)
-    blk = np.arange(nb)
-    z = ((zb[:, blk // 2] >> ((blk & 1) * 4)) & 15).astype(np.float32)
-    s = sc.astype(np.float32)
-    return (q - np.repeat(z, 32, axis=1)) * np.repeat(s, 32, axis=1)
-
-
 def gemm_tolerance(x, m):
     """2^-10 * sum_k |x_k w_k| + 1 f16 ulp of the reference result, per output element."""
-    w = dequant(*m).astype(np.float64)
+    from oracle import pyoracle
+    w = pyoracle.dequant_q4(*m).astype(np.float64)
     return 2.0 ** -10 * (np.abs(x.astype(np.float64)) @ np.abs(w).T)
 
 
