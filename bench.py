@@ -1218,27 +1218,31 @@ def main():
                         "parity": reduce_parity(r["parity"], 1)}
                 except p2p_b200.P2PError as e:
                     side[key] = {"error": str(e)}
-            try:
-                r = run_prefill_projections(ctx, steps=20, warmup=5)
-                fl_qkv = gemm_flops(2048, (HQ + 2 * HKV) * D, HQ * D)
-                fl_o = gemm_flops(2048, HQ * D, HQ * D)
-                pf, pu, po = r["ms_fused"], r["ms_unfused"], r["ms_oproj"]
-                side["prefill_projections"] = {
-                    "workload": "4-bit q/k/v projections + QK_PREP and o_proj of a 2048-token "
-                                "prompt chunk, one LFM2.5-1.2B layer (hidden 2048, 32q/8kv); "
-                                "weights dequantised to f16 in every call; 12 rotating sets "
-                                "(150 MB > L2)",
-                    "us_qkv_fused": round(pf * 1e3, 2),
-                    "us_qkv_unfused": round(pu * 1e3, 2),
-                    "us_oproj": round(po * 1e3, 2),
-                    "tflops_qkv_fused": round(fl_qkv / (pf * 1e-3) / 1e12, 1),
-                    "tflops_oproj": round(fl_o / (po * 1e-3) / 1e12, 1),
-                    "tensor_frac_of_measured_qkv": round(
-                        fl_qkv / (pf * 1e-3) / 1e12 / tensor_peak, 4),
-                    "hbm_bytes_saved": 2048 * (HQ + 2 * HKV) * D * 2 * 2,
-                    "parity": r["parity"]}
-            except p2p_b200.P2PError as e:
-                side["prefill_projections"] = {"error": str(e)}
+            # 2048: the whole prompt as one chunk; 256: the reference engine's chunk
+            # (engine.js:80, :384-401)
+            for s_tok in (2048, 256):
+                key = "prefill_projections" + ("" if s_tok == 2048 else f"_chunk{s_tok}")
+                try:
+                    r = run_prefill_projections(ctx, steps=20, warmup=5, s=s_tok)
+                    fl_qkv = gemm_flops(s_tok, (HQ + 2 * HKV) * D, HQ * D)
+                    fl_o = gemm_flops(s_tok, HQ * D, HQ * D)
+                    pf, pu, po = r["ms_fused"], r["ms_unfused"], r["ms_oproj"]
+                    side[key] = {
+                        "workload": f"4-bit q/k/v projections + QK_PREP and o_proj of a "
+                                    f"{s_tok}-token prompt chunk, one LFM2.5-1.2B layer (hidden "
+                                    "2048, 32q/8kv); weights dequantised to f16 in every call; "
+                                    "12 rotating sets of hidden rows and weights",
+                        "us_qkv_fused": round(pf * 1e3, 2),
+                        "us_qkv_unfused": round(pu * 1e3, 2),
+                        "us_oproj": round(po * 1e3, 2),
+                        "tflops_qkv_fused": round(fl_qkv / (pf * 1e-3) / 1e12, 1),
+                        "tflops_oproj": round(fl_o / (po * 1e-3) / 1e12, 1),
+                        "tensor_frac_of_measured_qkv": round(
+                            fl_qkv / (pf * 1e-3) / 1e12 / tensor_peak, 4),
+                        "hbm_bytes_saved": s_tok * (HQ + 2 * HKV) * D * 2 * 2,
+                        "parity": r["parity"]}
+                except p2p_b200.P2PError as e:
+                    side[key] = {"error": str(e)}
             try:
                 va, v_par = run_vision(ctx, steps=20, warmup=5)
                 fl = vision_flops()

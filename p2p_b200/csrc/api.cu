@@ -1023,13 +1023,19 @@ p2p_status p2p_qkv_gemv_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
   return P2P_OK;
 }
 
-// P2P_GEMM_BN=256|192|128 fixes the GEMM's output tile width (tests compare the widths on one
-// shape); unset or anything else: chosen per shape.
+// P2P_GEMM_BN=256|192|128 fixes the GEMM's output tile width and P2P_GEMM_PAIR=0|1 its form
+// (one CTA or a 2-CTA pair per tile; tests compare them on one shape); unset or anything
+// else: chosen per shape.
 static int gemm_bn_override() {
   const char* v = std::getenv("P2P_GEMM_BN");
   if (!v) return 0;
   const int bn = std::atoi(v);
   return (bn == 256 || bn == 192 || bn == 128) ? bn : 0;
+}
+static int gemm_pair_override() {
+  const char* v = std::getenv("P2P_GEMM_PAIR");
+  if (!v || (std::strcmp(v, "0") && std::strcmp(v, "1"))) return -1;
+  return std::atoi(v);
 }
 
 p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int64_t ld_x,
@@ -1063,6 +1069,7 @@ p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int6
   a.y_off = y_off;
   a.err = ctx->dev_err;
   a.bn = gemm_bn_override();
+  a.pair = gemm_pair_override();
   e = p2p::launch_gemm(a, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_q4 launch");
   return P2P_OK;
@@ -1128,6 +1135,7 @@ p2p_status p2p_qkv_gemm_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
   a.pos0 = pos0;
   a.err = ctx->dev_err;
   a.bn = gemm_bn_override();
+  a.pair = gemm_pair_override();
   e = p2p::launch_gemm(a, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemm_prep launch");
   return P2P_OK;

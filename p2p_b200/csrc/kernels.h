@@ -147,10 +147,16 @@ struct GemmArgs {
   const uint32_t* meta;  // nullable -> pos0
   int32_t pos0;
   int32_t* err;
-  int32_t bn;  // output tile width 256 / 192 / 128; 0 = gemm_tile_width()
+  int32_t bn;    // output tile width 256 / 192 / 128; 0 = chosen by gemm_tiling()
+  int32_t pair;  // 1: 2-CTA tiles (tcgen05 cta_group::2), 0: one CTA per tile, -1: chosen
 };
-// The tile width with the shortest makespan of m x n over `sms` persistent CTAs.
-int gemm_tile_width(int64_t m, int64_t n, int sms);
+struct GemmTiling {
+  int bn;
+  bool pair;
+};
+// The tiling with the shortest estimated makespan of m x n over `sms` persistent CTAs
+// (force_bn 0 / force_pair -1: free).
+GemmTiling gemm_tiling(int64_t m, int64_t n, int sms, int force_bn, int force_pair);
 cudaError_t launch_dequant_q4(const Q4Matrix& w, int32_t k, void* dst_f16, cudaStream_t s);
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
 struct GemvArgs {

@@ -257,22 +257,56 @@ def test_gemm_in_a_graph(ctx, oracle):
     del graph
 
 
+FORMS = [(bn, pair) for pair in ("0", "1") for bn in ("256", "192", "128")]
+
+
 @pytest.mark.parametrize("m,k,n", [(2048, 256, 3072), (300, 512, 2048), (70, 96, 192)])
-def test_gemm_tile_widths_agree(ctx, oracle, monkeypatch, m, k, n):
-    """The output tile width (256, 192 or 128 columns, chosen per shape) changes only which CTA
-    computes an element, not its K order: every width gives the same bits, within the bound."""
+def test_gemm_tile_forms_agree(ctx, oracle, monkeypatch, m, k, n):
+    """The output tile (128 x 256 / 192 / 128 on one CTA, or 256 x 256 / 192 / 128 on a pair of
+    CTAs sharing one tcgen05.mma.cta_group::2 stream, chosen per shape) changes only which SM
+    computes an element, not its K order: every form gives the same bits, within the bound."""
     rng = np.random.default_rng(m + 3 * n)
     w = oracle.random_q4(rng, n, k)
     x = rng.standard_normal((m, k)).astype(np.float16)
     g_w, g_x = dev_q4(w), dev(x)
     outs = {}
-    for bn in ("256", "192", "128"):
+    for bn, pair in FORMS:
         monkeypatch.setenv("P2P_GEMM_BN", bn)
+        monkeypatch.setenv("P2P_GEMM_PAIR", pair)
         y = torch.zeros((m, n), dtype=torch.float16, device="cuda")
         ctx.gemm_q4(g_w, g_x, y)
         ctx.sync()
-        outs[bn] = host(y)
+        outs[(bn, pair)] = host(y)
     monkeypatch.delenv("P2P_GEMM_BN")
-    assert np.array_equal(bits(outs["256"]), bits(outs["192"]))
-    assert np.array_equal(bits(outs["256"]), bits(outs["128"]))
-    assert_gemm_close(outs["256"], oracle.gemm_q4(x, *w), gemm_tolerance(x, w), "widths")
+    monkeypatch.delenv("P2P_GEMM_PAIR")
+    ref = outs[("256", "0")]
+    assert_gemm_close(ref, oracle.gemm_q4(x, *w), gemm_tolerance(x, w), "forms")
+    for form, got in outs.items():
+        assert np.array_equal(bits(got), bits(ref)), f"tile form {form}"
+
+
+@pytest.mark.parametrize("pair", ["0", "1"])
+def test_qkv_gemm_prep_forms_bit_exact(ctx, oracle, monkeypatch, pair):
+    """The fused q/k/v + QK_PREP on either tile form equals the unfused GEMMs + QK_PREP."""
+    import p2p_b200
+    monkeypatch.setenv("P2P_GEMM_PAIR", pair)
+    hq, hkv, k, m, pos0, cap = 32, 8, 1024, 700, 37, 800
+    rng = np.random.default_rng(41)
+    mq, mk, mv, x, nw, rope, kc, vc = qkv_case(oracle, rng, hq, hkv, k, m, cap, True)
+    prm = p2p_b200.Params(hq, hkv)
+    wq, wk, wv = dev_q4(mq), dev_q4(mk), dev_q4(mv)
+    g_x, g_nw, g_rope = dev(x), dev(nw), dev(rope)
+    qkv = torch.zeros((m, (hq + 2 * hkv) * D), dtype=torch.float16, device="cuda")
+    ctx.gemm_q4(wq, g_x, qkv, y_off=0)
+    ctx.gemm_q4(wk, g_x, qkv, y_off=hq * D)
+    ctx.gemm_q4(wv, g_x, qkv, y_off=(hq + hkv) * D)
+    q_u = torch.zeros((m, hq * D), dtype=torch.float16, device="cuda")
+    kc_u, vc_u = dev(kc), dev(vc)
+    ctx.qk_prep(prm, qkv, g_nw, g_rope, q_u, kc_u, vc_u, pos0=pos0)
+    q_f = torch.zeros_like(q_u)
+    kc_f, vc_f = dev(kc), dev(vc)
+    ctx.qkv_gemm_prep(prm, g_x, wq, wk, wv, g_nw, g_rope, q_f, kc_f, vc_f, pos0=pos0)
+    ctx.sync()
+    assert np.array_equal(bits(host(q_f)), bits(host(q_u)))
+    assert np.array_equal(bits(host(kc_f)), bits(host(kc_u)))
+    assert np.array_equal(bits(host(vc_f)), bits(host(vc_u)))
