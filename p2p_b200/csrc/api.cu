@@ -1055,7 +1055,8 @@ p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int6
   st = ensure_buffer(ctx, &ctx->w16, &ctx->w16_bytes, size_t(w->n) * w->k * 2,
                      "dequantised weights");
   if (st != P2P_OK) return st;
-  cudaError_t e = p2p::launch_dequant_q4(to_q4(w), w->k, ctx->w16, s);
+  const p2p::Q4Matrix wm = to_q4(w);
+  cudaError_t e = p2p::launch_dequant_q4(&wm, 1, w->k, ctx->w16, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_q4 dequant launch");
   p2p::GemmArgs a{};
   a.x = x;
@@ -1106,12 +1107,11 @@ p2p_status p2p_qkv_gemm_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
   const int n = qn + 2 * kn;
   st = ensure_buffer(ctx, &ctx->w16, &ctx->w16_bytes, size_t(n) * k * 2, "dequantised weights");
   if (st != P2P_OK) return st;
-  // one [q rows | k rows | v rows][k] operand: the projection's columns are the qkv row's
+  // one [q rows | k rows | v rows][k] operand (one launch): the projection's columns are the
+  // qkv row's
   __half* w16 = static_cast<__half*>(ctx->w16);
-  cudaError_t e = p2p::launch_dequant_q4(to_q4(wq), k, w16, s);
-  if (e == cudaSuccess) e = p2p::launch_dequant_q4(to_q4(wk), k, w16 + int64_t(qn) * k, s);
-  if (e == cudaSuccess)
-    e = p2p::launch_dequant_q4(to_q4(wv), k, w16 + int64_t(qn + kn) * k, s);
+  const p2p::Q4Matrix ws[3] = {to_q4(wq), to_q4(wk), to_q4(wv)};
+  cudaError_t e = p2p::launch_dequant_q4(ws, 3, k, w16, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemm_prep dequant launch");
   p2p::GemmArgs a{};
   a.x = x;

@@ -485,23 +485,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// Dequantised weights: dst[n][k] = f16((f32(q) - zp) * scale), one 8-value word per thread and
-// step of a grid-stride loop, so that a warp stores 512 contiguous bytes per instruction.
-__global__ void __launch_bounds__(256) dequant_q4_kernel(const Q4Matrix w, int32_t k, __half* dst) {
+// Dequantised weights of up to three matrices stacked along n (the q, k and v projections in
+// one launch): dst[n][k] = f16((f32(q) - zp) * scale), one 8-value word per thread and step of
+// a grid-stride loop, so that a warp stores 512 contiguous bytes per instruction.  Every
+// matrix has the same k, so word idx of the stack is element 8 idx of dst.
+struct Q4Stack {
+  Q4Matrix w[3];
+  int64_t end[3];  // cumulative words
+  int count;
+};
+
+__global__ void __launch_bounds__(256)
+    dequant_q4_kernel(const __grid_constant__ Q4Stack st, int32_t k, __half* dst) {
   const int wpr = k >> 3, nb = k >> 5, zr = (nb + 1) >> 1;
-  const int64_t total = int64_t(w.n) * wpr;
-  const unsigned char* zp = reinterpret_cast<const unsigned char*>(w.zero_points);
+  const int64_t total = st.end[st.count - 1];
   for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t n = idx / wpr;
-    const int wi = int(idx - n * wpr), blk = wi >> 2;
-    const uint32_t word = w.qweight[idx];
+    const int j = idx < st.end[0] ? 0 : idx < st.end[1] ? 1 : 2;
+    const Q4Matrix& w = st.w[j];
+    const int64_t local = j ? idx - st.end[j - 1] : idx;
+    const int64_t n = local / wpr;
+    const int wi = int(local - n * wpr), blk = wi >> 2;
+    const uint32_t word = w.qweight[local];
     const float sc = __half2float(w.scales[n * nb + blk]);
+    const unsigned char* zp = reinterpret_cast<const unsigned char*>(w.zero_points);
     const float z = float((zp[n * zr + (blk >> 1)] >> ((blk & 1) * 4)) & 15u);
     float vals[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) vals[i] = (float((word >> (4 * i)) & 15u) - z) * sc;
-    store8(dst + idx * 8, vals);  // = n * k + wi * 8
+    store8(dst + idx * 8, vals);
   }
 }
 
@@ -536,10 +548,20 @@ bool map_k_major(CUtensorMap* m, const void* base, int64_t width, int64_t ld, in
 
 }  // namespace
 
-cudaError_t launch_dequant_q4(const Q4Matrix& w, int32_t k, void* dst, cudaStream_t s) {
-  const int64_t words = int64_t(w.n) * (k / 8);
+cudaError_t launch_dequant_q4(const Q4Matrix* ws, int count, int32_t k, void* dst,
+                              cudaStream_t s) {
+  if (count < 1 || count > 3 || (k % 32) || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return cudaErrorInvalidValue;
+  Q4Stack st{};
+  int64_t words = 0;
+  for (int i = 0; i < count; ++i) {
+    st.w[i] = ws[i];
+    words += int64_t(ws[i].n) * (k / 8);
+    st.end[i] = words;
+  }
+  for (int i = count; i < 3; ++i) st.end[i] = words;
+  st.count = count;
   if (words <= 0) return cudaSuccess;
-  if ((k % 32) || (reinterpret_cast<uintptr_t>(dst) & 15)) return cudaErrorInvalidValue;
   const int threads = 256;
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -548,7 +570,7 @@ cudaError_t launch_dequant_q4(const Q4Matrix& w, int32_t k, void* dst, cudaStrea
   // eight resident CTAs of 256 per SM (measured best of 4 / 8 / 16 / 64 per SM)
   const unsigned grid =
       unsigned(std::min<int64_t>((words + threads - 1) / threads, int64_t(std::max(sms, 1)) * 8));
-  dequant_q4_kernel<<<grid, threads, 0, s>>>(w, k, static_cast<__half*>(dst));
+  dequant_q4_kernel<<<grid, threads, 0, s>>>(st, k, static_cast<__half*>(dst));
   return cudaGetLastError();
 }
 

@@ -157,7 +157,9 @@ struct GemmTiling {
 // The tiling with the shortest estimated makespan of m x n over `sms` persistent CTAs
 // (force_bn 0 / force_pair -1: free).
 GemmTiling gemm_tiling(int64_t m, int64_t n, int sms, int force_bn, int force_pair);
-cudaError_t launch_dequant_q4(const Q4Matrix& w, int32_t k, void* dst_f16, cudaStream_t s);
+// f16 copies of `count` (1-3) 4-bit matrices with the same k, stacked along n in dst_f16.
+cudaError_t launch_dequant_q4(const Q4Matrix* ws, int count, int32_t k, void* dst_f16,
+                              cudaStream_t s);
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
 struct GemvArgs {
   Q4Matrix w;
