@@ -349,6 +349,28 @@ p2p_status p2p_qkv_gemm_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
                              int64_t kv_cap_tokens, const uint32_t* meta_dev, int32_t pos0,
                              int32_t m_tokens, void* stream);
 
+/* Resident f16 weights.  The engine builds every 4-bit matrix once (engine.js:100, `proj`) and
+ * the GEMM entry points above dequantise it again on every call.  A B200 holds the f16 copy of
+ * all of a small model's projections many times over, so the copy can be made once, where the
+ * engine uploads its weights, and reused by every prompt chunk:
+ *   p2p_q4_to_f16       dst [n][k] f16 = (q - zp) * scale, rounded once (the same values the
+ *                       4-bit GEMM entry points compute per call); dst 16-byte aligned.
+ *   p2p_gemm_f16w       p2p_gemm_q4 on such a copy (w16 [n][k], k a multiple of 8);
+ *   p2p_qkv_gemm_prep_f16w  p2p_qkv_gemm_prep on the q, k and v copies stacked along n:
+ *                       w16_qkv [q rows | k rows | v rows][k].
+ * Given the same copy, the outputs equal the 4-bit entry points' bit for bit.  These two use no
+ * context workspace, so calls on different streams may overlap. */
+p2p_status p2p_q4_to_f16(p2p_ctx* ctx, const p2p_q4_matrix* w, void* dst, void* stream);
+p2p_status p2p_gemm_f16w(p2p_ctx* ctx, const void* w16, int32_t n, int32_t k, const void* x,
+                         int64_t ld_x, int32_t m_tokens, void* y, int64_t ld_y, int64_t y_off,
+                         void* stream);
+p2p_status p2p_qkv_gemm_prep_f16w(p2p_ctx* ctx, const p2p_attn_params* prm, const void* x,
+                                  int64_t ld_x, const void* w16_qkv, int32_t k,
+                                  const void* norm_w, const void* rope, void* q_out,
+                                  int64_t ld_q, void* k_cache, void* v_cache,
+                                  int64_t kv_cap_tokens, const uint32_t* meta_dev, int32_t pos0,
+                                  int32_t m_tokens, void* stream);
+
 /* vision-kernels.js:176-258 (VISION_ATTN, dispatched (NUM_HEADS, S) at vision.js:271-276),
  * batched: out[b] = softmax(scale * q[b] k[b]^T) v[b] per head, no mask, tcgen05 kernel.
  * q/k/v/out are [batch][s_tokens][ld] with head h at column h*D. */

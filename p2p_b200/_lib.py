@@ -142,6 +142,10 @@ PROTOTYPES = {
         _st, [_v, _pp, _v, C.POINTER(Q4Matrix), C.POINTER(Q4Matrix), C.POINTER(Q4Matrix), _v,
               _v, _v, _v, _v, _i64, _v, _i32, _v]),
     "p2p_gemm_q4": (_st, [_v, C.POINTER(Q4Matrix), _v, _i64, _i32, _v, _i64, _i64, _v]),
+    "p2p_q4_to_f16": (_st, [_v, C.POINTER(Q4Matrix), _v, _v]),
+    "p2p_gemm_f16w": (_st, [_v, _v, _i32, _i32, _v, _i64, _i32, _v, _i64, _i64, _v]),
+    "p2p_qkv_gemm_prep_f16w": (
+        _st, [_v, _pp, _v, _i64, _v, _i32, _v, _v, _v, _i64, _v, _v, _i64, _v, _i32, _i32, _v]),
     "p2p_qkv_gemm_prep": (
         _st, [_v, _pp, _v, _i64, C.POINTER(Q4Matrix), C.POINTER(Q4Matrix), C.POINTER(Q4Matrix),
               _v, _v, _v, _i64, _v, _v, _i64, _v, _i32, _i32, _v]),

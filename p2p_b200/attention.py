@@ -326,6 +326,35 @@ class Context:
             _ptr(q_out), q_out.stride(0), _ptr(k_cache), _ptr(v_cache), k_cache.shape[0],
             self.meta_ptr if use_meta else None, pos0, m, _stream(stream)))
 
+    def q4_to_f16(self, w, dst: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """The resident f16 copy [n][k] of a 4-bit matrix (made once, reused by every call of
+        gemm_f16w / qkv_gemm_prep_f16w)."""
+        mw = self.q4(w)
+        if dst is None:
+            dst = torch.empty((mw.n, mw.k), dtype=torch.float16, device="cuda")
+        self._chk(lib.p2p_q4_to_f16(self.h, C.byref(mw), _ptr(dst), _stream(stream)))
+        return dst
+
+    def gemm_f16w(self, w16: torch.Tensor, x: torch.Tensor, y: torch.Tensor, y_off: int = 0,
+                  m_tokens: Optional[int] = None, stream=None):
+        """gemm_q4 on resident f16 weights w16 [n][k]."""
+        m = x.shape[0] if m_tokens is None else m_tokens
+        self._chk(lib.p2p_gemm_f16w(self.h, _ptr(w16), w16.shape[0], w16.shape[1], _ptr(x),
+                                    x.stride(0), m, _ptr(y), y.stride(0), y_off,
+                                    _stream(stream)))
+
+    def qkv_gemm_prep_f16w(self, prm: Params, x: torch.Tensor, w16_qkv: torch.Tensor, norm_w,
+                           rope, q_out: torch.Tensor, k_cache: torch.Tensor,
+                           v_cache: torch.Tensor, *, pos0: int = 0,
+                           m_tokens: Optional[int] = None, use_meta: bool = False, stream=None):
+        """qkv_gemm_prep on resident f16 weights stacked [q rows | k rows | v rows][k]."""
+        m = x.shape[0] if m_tokens is None else m_tokens
+        self._chk(lib.p2p_qkv_gemm_prep_f16w(
+            self.h, C.byref(prm.c()), _ptr(x), x.stride(0), _ptr(w16_qkv), w16_qkv.shape[1],
+            _ptr(norm_w), rope if isinstance(rope, C.c_void_p) else _ptr(rope), _ptr(q_out),
+            q_out.stride(0), _ptr(k_cache), _ptr(v_cache), k_cache.shape[0],
+            self.meta_ptr if use_meta else None, pos0, m, _stream(stream)))
+
     def attn_prefill_sharded(self, comm, prm: Params, qkv_local: torch.Tensor, norm_w, rope,
                              k_cache: torch.Tensor, v_cache: torch.Tensor, out: torch.Tensor, *,
                              pos0: int = 0, m_tokens: Optional[int] = None,

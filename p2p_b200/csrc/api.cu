@@ -1038,17 +1038,114 @@ static int gemm_pair_override() {
   return std::atoi(v);
 }
 
+// ---- prompt-chunk GEMM (kernels.js:70-145) -------------------------------------------------
+// Shared by the 4-bit entry points (dequantise into the context's workspace first) and the
+// f16-weight ones (weights made once by p2p_q4_to_f16).
+static p2p_status gemm_check(p2p_ctx* ctx, int32_t n, int32_t k, const void* x, int64_t ld_x,
+                             int32_t m_tokens, const void* y, int64_t ld_y, int64_t y_off,
+                             const char* what) {
+  if (!x || !y || m_tokens < 0 || ld_x < k || y_off < 0 || ld_y < y_off + n)
+    return fail(ctx, P2P_ERR_INVALID_ARG, "%s: M %d ld_x %lld ld_y %lld y_off %lld", what,
+                m_tokens, (long long)ld_x, (long long)ld_y, (long long)y_off);
+  if (n % 64 || !aligned16(x) || (ld_x % 8) || !aligned16(y) || (ld_y % 8) || (y_off % 8))
+    return fail(ctx, P2P_ERR_INVALID_ARG,
+                "%s: n a multiple of 64, 16-byte aligned rows of x and y, y_off %% 8 == 0", what);
+  return P2P_OK;
+}
+
+static p2p_status gemm_run(p2p_ctx* ctx, const void* w16, int32_t n, int32_t k, const void* x,
+                           int64_t ld_x, int32_t m_tokens, void* y, int64_t ld_y, int64_t y_off,
+                           cudaStream_t s, const char* what) {
+  p2p::GemmArgs a{};
+  a.x = x;
+  a.ld_x = ld_x;
+  a.w16 = w16;
+  a.m = m_tokens;
+  a.n = n;
+  a.k = k;
+  a.y = y;
+  a.ld_y = ld_y;
+  a.y_off = y_off;
+  a.err = ctx->dev_err;
+  a.bn = gemm_bn_override();
+  a.pair = gemm_pair_override();
+  const cudaError_t e = p2p::launch_gemm(a, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  return P2P_OK;
+}
+
+struct QkvPrepIo {
+  const void* x;
+  int64_t ld_x;
+  const void* norm_w;
+  const void* rope;
+  void* q_out;
+  int64_t ld_q;
+  void* k_cache;
+  void* v_cache;
+  int64_t kv_cap;
+  const uint32_t* meta;
+  int32_t pos0, m;
+};
+
+static p2p_status qkv_check(p2p_ctx* ctx, const p2p_attn_params* prm, int32_t k,
+                            const QkvPrepIo& io, const char* what) {
+  p2p_status st = check_params(ctx, prm, false);
+  if (st != P2P_OK) return st;
+  if (prm->dtype != P2P_F16)
+    return fail(ctx, P2P_ERR_UNSUPPORTED, "%s: the projection path is f16", what);
+  const int qn = prm->num_heads * prm->head_dim;
+  if (!io.x || !io.rope || !io.q_out || !io.k_cache || !io.v_cache || io.m < 0 ||
+      io.ld_x < k || io.ld_q < qn || io.kv_cap <= 0 || (!io.meta && io.pos0 < 0))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "%s: M %d ld_x %lld ld_q %lld pos0 %d", what, io.m,
+                (long long)io.ld_x, (long long)io.ld_q, io.pos0);
+  if (!aligned16(io.x) || (io.ld_x % 8) || !aligned16(io.q_out) || (io.ld_q % 8) ||
+      !aligned16(io.rope) || !aligned16(io.k_cache) || !aligned16(io.v_cache))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "%s: 16-byte aligned rows needed", what);
+  if (!io.meta && int64_t(io.pos0) + io.m > io.kv_cap)
+    return fail(ctx, P2P_ERR_KV_FULL, "%s: pos0 %d + M %d > cache rows %lld", what, io.pos0,
+                io.m, (long long)io.kv_cap);
+  return P2P_OK;
+}
+
+static p2p_status qkv_run(p2p_ctx* ctx, const p2p_attn_params* prm, const void* w16, int32_t k,
+                          const QkvPrepIo& io, cudaStream_t s, const char* what) {
+  p2p::GemmArgs a{};
+  a.x = io.x;
+  a.ld_x = io.ld_x;
+  a.w16 = w16;
+  a.m = io.m;
+  a.n = (prm->num_heads + 2 * prm->num_kv_heads) * prm->head_dim;
+  a.k = k;
+  a.prep = 1;
+  a.hq = prm->num_heads;
+  a.hkv = prm->num_kv_heads;
+  a.norm_w = io.norm_w;
+  a.rope = io.rope;
+  a.eps = eff_eps(prm);
+  a.q_out = io.q_out;
+  a.ld_q = io.ld_q;
+  a.k_cache = io.k_cache;
+  a.v_cache = io.v_cache;
+  a.kv_cap = io.kv_cap;
+  a.meta = io.meta;
+  a.pos0 = io.pos0;
+  a.err = ctx->dev_err;
+  a.bn = gemm_bn_override();
+  a.pair = gemm_pair_override();
+  const cudaError_t e = p2p::launch_gemm(a, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  return P2P_OK;
+}
+
 p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int64_t ld_x,
                        int32_t m_tokens, void* y, int64_t ld_y, int64_t y_off, void* stream) {
   if (!ctx) return P2P_ERR_INVALID_ARG;
   p2p_status st = check_q4(ctx, w, -1, w ? w->k : 0, "gemm_q4", INT32_MAX);
   if (st != P2P_OK) return st;
-  if (!x || !y || m_tokens < 0 || ld_x < w->k || y_off < 0 || ld_y < y_off + w->n)
-    return fail(ctx, P2P_ERR_INVALID_ARG, "gemm_q4: M %d ld_x %lld ld_y %lld y_off %lld",
-                m_tokens, (long long)ld_x, (long long)ld_y, (long long)y_off);
-  if (w->n % 64 || !aligned16(x) || (ld_x % 8) || !aligned16(y) || (ld_y % 8) || (y_off % 8))
-    return fail(ctx, P2P_ERR_INVALID_ARG,
-                "gemm_q4: n a multiple of 64, 16-byte aligned rows of x and y, y_off % 8 == 0");
+  if ((st = gemm_check(ctx, w->n, w->k, x, ld_x, m_tokens, y, ld_y, y_off, "gemm_q4")) !=
+      P2P_OK)
+    return st;
   if (m_tokens == 0) return P2P_OK;
   DeviceGuard g(ctx->device);
   cudaStream_t s = pick_stream(ctx, stream);
@@ -1058,22 +1155,8 @@ p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int6
   const p2p::Q4Matrix wm = to_q4(w);
   cudaError_t e = p2p::launch_dequant_q4(&wm, 1, w->k, ctx->w16, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_q4 dequant launch");
-  p2p::GemmArgs a{};
-  a.x = x;
-  a.ld_x = ld_x;
-  a.w16 = ctx->w16;
-  a.m = m_tokens;
-  a.n = w->n;
-  a.k = w->k;
-  a.y = y;
-  a.ld_y = ld_y;
-  a.y_off = y_off;
-  a.err = ctx->dev_err;
-  a.bn = gemm_bn_override();
-  a.pair = gemm_pair_override();
-  e = p2p::launch_gemm(a, s);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_q4 launch");
-  return P2P_OK;
+  return gemm_run(ctx, ctx->w16, w->n, w->k, x, ld_x, m_tokens, y, ld_y, y_off, s,
+                  "gemm_q4 launch");
 }
 
 p2p_status p2p_qkv_gemm_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const void* x,
@@ -1082,63 +1165,80 @@ p2p_status p2p_qkv_gemm_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
                              void* q_out, int64_t ld_q, void* k_cache, void* v_cache,
                              int64_t kv_cap_tokens, const uint32_t* meta_dev, int32_t pos0,
                              int32_t m_tokens, void* stream) {
-  p2p_status st = check_params(ctx, prm, false);
-  if (st != P2P_OK) return st;
-  if (prm->dtype != P2P_F16)
-    return fail(ctx, P2P_ERR_UNSUPPORTED, "qkv_gemm_prep: the projection path is f16");
-  const int qn = prm->num_heads * prm->head_dim, kn = prm->num_kv_heads * prm->head_dim;
+  const QkvPrepIo io{x,       ld_x,    norm_w,        rope,     q_out, ld_q,
+                     k_cache, v_cache, kv_cap_tokens, meta_dev, pos0,  m_tokens};
   const int k = wq ? wq->k : 0;
+  p2p_status st = qkv_check(ctx, prm, k, io, "qkv_gemm_prep");
+  if (st != P2P_OK) return st;
+  const int qn = prm->num_heads * prm->head_dim, kn = prm->num_kv_heads * prm->head_dim;
   if ((st = check_q4(ctx, wq, qn, k, "qkv_gemm_prep (wq)", INT32_MAX)) != P2P_OK) return st;
   if ((st = check_q4(ctx, wk, kn, k, "qkv_gemm_prep (wk)", INT32_MAX)) != P2P_OK) return st;
   if ((st = check_q4(ctx, wv, kn, k, "qkv_gemm_prep (wv)", INT32_MAX)) != P2P_OK) return st;
-  if (!x || !rope || !q_out || !k_cache || !v_cache || m_tokens < 0 || ld_x < k || ld_q < qn ||
-      kv_cap_tokens <= 0 || (!meta_dev && pos0 < 0))
-    return fail(ctx, P2P_ERR_INVALID_ARG, "qkv_gemm_prep: M %d ld_x %lld ld_q %lld pos0 %d",
-                m_tokens, (long long)ld_x, (long long)ld_q, pos0);
-  if (!aligned16(x) || (ld_x % 8) || !aligned16(q_out) || (ld_q % 8) || !aligned16(rope) ||
-      !aligned16(k_cache) || !aligned16(v_cache))
-    return fail(ctx, P2P_ERR_INVALID_ARG, "qkv_gemm_prep: 16-byte aligned rows needed");
-  if (!meta_dev && int64_t(pos0) + m_tokens > kv_cap_tokens)
-    return fail(ctx, P2P_ERR_KV_FULL, "qkv_gemm_prep: pos0 %d + M %d > cache rows %lld", pos0,
-                m_tokens, (long long)kv_cap_tokens);
   if (m_tokens == 0) return P2P_OK;
   DeviceGuard g(ctx->device);
   cudaStream_t s = pick_stream(ctx, stream);
-  const int n = qn + 2 * kn;
-  st = ensure_buffer(ctx, &ctx->w16, &ctx->w16_bytes, size_t(n) * k * 2, "dequantised weights");
+  st = ensure_buffer(ctx, &ctx->w16, &ctx->w16_bytes, size_t(qn + 2 * kn) * k * 2,
+                     "dequantised weights");
   if (st != P2P_OK) return st;
   // one [q rows | k rows | v rows][k] operand (one launch): the projection's columns are the
   // qkv row's
-  __half* w16 = static_cast<__half*>(ctx->w16);
   const p2p::Q4Matrix ws[3] = {to_q4(wq), to_q4(wk), to_q4(wv)};
-  cudaError_t e = p2p::launch_dequant_q4(ws, 3, k, w16, s);
+  cudaError_t e = p2p::launch_dequant_q4(ws, 3, k, ctx->w16, s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemm_prep dequant launch");
-  p2p::GemmArgs a{};
-  a.x = x;
-  a.ld_x = ld_x;
-  a.w16 = w16;
-  a.m = m_tokens;
-  a.n = n;
-  a.k = k;
-  a.prep = 1;
-  a.hq = prm->num_heads;
-  a.hkv = prm->num_kv_heads;
-  a.norm_w = norm_w;
-  a.rope = rope;
-  a.eps = eff_eps(prm);
-  a.q_out = q_out;
-  a.ld_q = ld_q;
-  a.k_cache = k_cache;
-  a.v_cache = v_cache;
-  a.kv_cap = kv_cap_tokens;
-  a.meta = meta_dev;
-  a.pos0 = pos0;
-  a.err = ctx->dev_err;
-  a.bn = gemm_bn_override();
-  a.pair = gemm_pair_override();
-  e = p2p::launch_gemm(a, s);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "qkv_gemm_prep launch");
+  return qkv_run(ctx, prm, ctx->w16, k, io, s, "qkv_gemm_prep launch");
+}
+
+p2p_status p2p_q4_to_f16(p2p_ctx* ctx, const p2p_q4_matrix* w, void* dst, void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  p2p_status st = check_q4(ctx, w, -1, w ? w->k : 0, "q4_to_f16", INT32_MAX);
+  if (st != P2P_OK) return st;
+  if (!dst || !aligned16(dst))
+    return fail(ctx, P2P_ERR_INVALID_ARG, "q4_to_f16: dst must be a 16-byte aligned buffer");
+  DeviceGuard g(ctx->device);
+  const p2p::Q4Matrix wm = to_q4(w);
+  const cudaError_t e = p2p::launch_dequant_q4(&wm, 1, w->k, dst, pick_stream(ctx, stream));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "q4_to_f16 launch");
   return P2P_OK;
+}
+
+static p2p_status check_w16(p2p_ctx* ctx, const void* w16, int32_t n, int32_t k,
+                            const char* what) {
+  if (!w16 || !aligned16(w16) || n <= 0 || k <= 0 || (k % 8))
+    return fail(ctx, P2P_ERR_INVALID_ARG,
+                "%s: f16 weights [n][k], 16-byte aligned, k a multiple of 8 (n %d k %d)", what,
+                n, k);
+  return P2P_OK;
+}
+
+p2p_status p2p_gemm_f16w(p2p_ctx* ctx, const void* w16, int32_t n, int32_t k, const void* x,
+                         int64_t ld_x, int32_t m_tokens, void* y, int64_t ld_y, int64_t y_off,
+                         void* stream) {
+  if (!ctx) return P2P_ERR_INVALID_ARG;
+  p2p_status st = check_w16(ctx, w16, n, k, "gemm_f16w");
+  if (st != P2P_OK) return st;
+  if ((st = gemm_check(ctx, n, k, x, ld_x, m_tokens, y, ld_y, y_off, "gemm_f16w")) != P2P_OK)
+    return st;
+  if (m_tokens == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  return gemm_run(ctx, w16, n, k, x, ld_x, m_tokens, y, ld_y, y_off, pick_stream(ctx, stream),
+                  "gemm_f16w launch");
+}
+
+p2p_status p2p_qkv_gemm_prep_f16w(p2p_ctx* ctx, const p2p_attn_params* prm, const void* x,
+                                  int64_t ld_x, const void* w16_qkv, int32_t k,
+                                  const void* norm_w, const void* rope, void* q_out,
+                                  int64_t ld_q, void* k_cache, void* v_cache,
+                                  int64_t kv_cap_tokens, const uint32_t* meta_dev, int32_t pos0,
+                                  int32_t m_tokens, void* stream) {
+  const QkvPrepIo io{x,       ld_x,    norm_w,        rope,     q_out, ld_q,
+                     k_cache, v_cache, kv_cap_tokens, meta_dev, pos0,  m_tokens};
+  p2p_status st = qkv_check(ctx, prm, k, io, "qkv_gemm_prep_f16w");
+  if (st != P2P_OK) return st;
+  const int n = (prm->num_heads + 2 * prm->num_kv_heads) * prm->head_dim;
+  if ((st = check_w16(ctx, w16_qkv, n, k, "qkv_gemm_prep_f16w")) != P2P_OK) return st;
+  if (m_tokens == 0) return P2P_OK;
+  DeviceGuard g(ctx->device);
+  return qkv_run(ctx, prm, w16_qkv, k, io, pick_stream(ctx, stream), "qkv_gemm_prep_f16w launch");
 }
 
 p2p_status p2p_kv_quantize_q8(p2p_ctx* ctx, const void* src, void* dst, int64_t rows,

@@ -310,3 +310,44 @@ def test_qkv_gemm_prep_forms_bit_exact(ctx, oracle, monkeypatch, pair):
     assert np.array_equal(bits(host(q_f)), bits(host(q_u)))
     assert np.array_equal(bits(host(kc_f)), bits(host(kc_u)))
     assert np.array_equal(bits(host(vc_f)), bits(host(vc_u)))
+
+
+def test_q4_to_f16_exact(ctx, oracle):
+    """The resident f16 copy is (q - zp) * scale in f32, rounded once to f16 (RNE)."""
+    rng = np.random.default_rng(12)
+    w = oracle.random_q4(rng, 192, 96)
+    got = host(ctx.q4_to_f16(dev_q4(w)))
+    want = oracle.dequant_q4(*w).astype(np.float16)
+    assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("m", [256, 2048])
+def test_f16_weight_entry_points_equal_q4(ctx, oracle, m):
+    """gemm_f16w / qkv_gemm_prep_f16w on the resident copies give the 4-bit entry points'
+    outputs bit for bit (the same dequantised values, the same GEMM)."""
+    import p2p_b200
+    hq, hkv, k, pos0, cap = 32, 8, 2048, 3, m + 16
+    rng = np.random.default_rng(m)
+    mq, mk, mv, x, nw, rope, kc, vc = qkv_case(oracle, rng, hq, hkv, k, m, cap, True)
+    mo = oracle.random_q4(rng, k, hq * D)
+    prm = p2p_b200.Params(hq, hkv)
+    wq, wk, wv, wo = dev_q4(mq), dev_q4(mk), dev_q4(mv), dev_q4(mo)
+    g_x, g_nw, g_rope = dev(x), dev(nw), dev(rope)
+    w16_qkv = torch.cat([ctx.q4_to_f16(w) for w in (wq, wk, wv)])
+    w16_o = ctx.q4_to_f16(wo)
+    outs = []
+    for resident in (False, True):
+        q = torch.zeros((m, hq * D), dtype=torch.float16, device="cuda")
+        kc_g, vc_g = dev(kc), dev(vc)
+        y = torch.zeros((m, k), dtype=torch.float16, device="cuda")
+        if resident:
+            ctx.qkv_gemm_prep_f16w(prm, g_x, w16_qkv, g_nw, g_rope, q, kc_g, vc_g, pos0=pos0)
+            ctx.gemm_f16w(w16_o, q, y)
+        else:
+            ctx.qkv_gemm_prep(prm, g_x, wq, wk, wv, g_nw, g_rope, q, kc_g, vc_g, pos0=pos0)
+            ctx.gemm_q4(wo, q, y)
+        ctx.sync()
+        outs.append([host(t) for t in (q, kc_g, vc_g, y)])
+    for a, b in zip(*outs):
+        assert np.array_equal(bits(a), bits(b))
+    assert np.isfinite(outs[1][3].astype(np.float32)).all()
