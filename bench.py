@@ -564,16 +564,20 @@ def e2e_decode(wl, steps, warmup):
     return dt, h_in.numel() * 2, h_out.numel() * 2
 
 
-def e2e_native(device, steps, warmup, world):
+def e2e_native(device, steps, warmup, world, graph=True):
     """The same per-token call from a plain C host (p2p_b200/host/p2p_decode_loop: the C ABI
     alone, no Python or torch, as a native engine binding calls it), one process per GPU, all
-    ranks at once; returns (seconds per step, h2d bytes, d2h bytes, finite)."""
+    ranks at once.  graph: the binding records each cache copy's p2p_decode_step once as a
+    CUDA graph and replays it per token (the kernel reads the token's qkv rows from and writes
+    its outputs to page-locked host memory on every replay); otherwise it calls the C ABI per
+    token.  Returns (seconds per step, h2d bytes, d2h bytes, finite)."""
     exe = ROOT / "p2p_b200" / "host" / "p2p_decode_loop"
     if not exe.exists():
         raise RuntimeError(f"{exe} is missing: build with python p2p_b200/build.py")
     barrier(world)
     r = subprocess.run([str(exe), "--device", str(device), "--steps", str(steps),
-                        "--warmup", str(warmup), "--copies", "12", "--past", str(PAST)],
+                        "--warmup", str(warmup), "--copies", "12", "--past", str(PAST),
+                        "--graph", "1" if graph else "0"],
                        capture_output=True, text=True, timeout=600)
     barrier(world)
     if r.returncode != 0:
@@ -1091,20 +1095,26 @@ def main():
     value_gbs = total_bytes / (ms_max * 1e-3) / 1e9
     per_gpu_gbs = wl.bytes_per_step / (ms_max * 1e-3) / 1e9
 
-    e2e_note = "plain C host over the C ABI (p2p_b200/host/p2p_decode_loop), wall clock"
+    e2e_note = ("plain C host over the C ABI (p2p_b200/host/p2p_decode_loop), wall clock; "
+                "each cache copy's p2p_decode_step recorded once as a CUDA graph and replayed "
+                "per token, the kernel reading and writing the host rows")
+    direct_sec = float("nan")
     if args.quick:
         e2e_sec, h2d, d2h, py_sec = float("nan"), 0, 0, float("nan")
     else:
         try:
             e2e_sec, h2d, d2h, finite = e2e_native(local, max(50, args.steps), args.warmup,
                                                    world)
-            if not finite:
+            direct_sec, _, _, finite_d = e2e_native(local, max(50, args.steps), args.warmup,
+                                                    world, graph=False)
+            if not (finite and finite_d):
                 e2e_note += "; NON-FINITE OUTPUT"
         except (RuntimeError, subprocess.TimeoutExpired, ValueError) as e:
             e2e_sec, h2d, d2h = float("nan"), 0, 0
             e2e_note = f"native host program failed: {str(e)[:160]}"
         py_sec, _, _ = e2e_decode(wl, max(20, args.steps // 2), args.warmup)
     e2e_sec = max_over_ranks(e2e_sec, world)
+    direct_sec = max_over_ranks(direct_sec, world)
     py_sec = max_over_ranks(py_sec, world)
     e2e_gbs = total_bytes / e2e_sec / 1e9
 
@@ -1319,6 +1329,7 @@ def main():
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_sec * 1e6, 2),
                     "host": e2e_note,
+                    "c_abi_call_per_token_us_per_step": round(direct_sec * 1e6, 2),
                     "python_ctypes_us_per_step": round(py_sec * 1e6, 2)},
             "gpu_launches": args.steps,
             "parity": parity,

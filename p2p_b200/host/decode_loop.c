@@ -8,6 +8,15 @@
  * synchronization per token.
  *
  *   p2p_decode_loop [--device N] [--steps K] [--warmup W] [--copies C] [--past P]
+ *                   [--sched auto|spin|yield|block] [--graph 0|1] [--rows host|device]
+ *
+ * --sched sets how the host thread waits for the GPU (cudaSetDeviceFlags before the context
+ * exists: spin keeps the core polling, the lowest latency for a serving thread that owns a
+ * core); --graph 1 records each copy's step once as a CUDA graph and replays it per token
+ * instead of launching through the C ABI each time (what a binding does once the shapes are
+ * fixed; the kernel still reads and writes the host rows on every replay); --rows device keeps
+ * the rows in device memory and moves them with one copy in (36 KB) and one copy out (24 KB)
+ * per token on the same stream instead of the kernel crossing the host link itself.
  *
  * Prints one JSON line: microseconds per step (wall clock around K steps), the host bytes in
  * and out per step, and whether every output was finite.  The KV caches (C copies of the six
@@ -86,14 +95,29 @@ static double now_s(void) {
   } while (0)
 
 int main(int argc, char** argv) {
-  int device = 0, steps = 200, warmup = 20, copies = 12, past = 4096;
+  int device = 0, steps = 200, warmup = 20, copies = 12, past = 4096, use_graph = 0;
+  const char* sched = "auto";
+  const char* rows = "host";
   for (int i = 1; i + 1 < argc; i += 2) {
     if (!strcmp(argv[i], "--device")) device = atoi(argv[i + 1]);
     else if (!strcmp(argv[i], "--steps")) steps = atoi(argv[i + 1]);
     else if (!strcmp(argv[i], "--warmup")) warmup = atoi(argv[i + 1]);
     else if (!strcmp(argv[i], "--copies")) copies = atoi(argv[i + 1]);
     else if (!strcmp(argv[i], "--past")) past = atoi(argv[i + 1]);
+    else if (!strcmp(argv[i], "--sched")) sched = argv[i + 1];
+    else if (!strcmp(argv[i], "--graph")) use_graph = atoi(argv[i + 1]);
+    else if (!strcmp(argv[i], "--rows")) rows = argv[i + 1];
   }
+  unsigned flags = cudaDeviceScheduleAuto;
+  if (!strcmp(sched, "spin")) flags = cudaDeviceScheduleSpin;
+  else if (!strcmp(sched, "yield")) flags = cudaDeviceScheduleYield;
+  else if (!strcmp(sched, "block")) flags = cudaDeviceScheduleBlockingSync;
+  else if (strcmp(sched, "auto")) {
+    fprintf(stderr, "bad --sched\n");
+    return 2;
+  }
+  CHECK_CUDA(cudaSetDevice(device));
+  CHECK_CUDA(cudaSetDeviceFlags(flags));
   if (steps < 1 || warmup < 0 || copies < 1 || past < 0) {
     fprintf(stderr, "bad arguments\n");
     return 2;
@@ -138,26 +162,67 @@ int main(int argc, char** argv) {
   CHECK_CUDA(cudaHostAlloc((void**)&qkv_h, LAYERS * qkv_w * 2, cudaHostAllocDefault));
   CHECK_CUDA(cudaHostAlloc((void**)&out_h, LAYERS * out_w * 2, cudaHostAllocDefault));
   for (size_t i = 0; i < LAYERS * qkv_w; ++i) qkv_h[i] = normal_half();
+  const int dev_rows = !strcmp(rows, "device");
+  if (!dev_rows && strcmp(rows, "host")) {
+    fprintf(stderr, "bad --rows\n");
+    return 2;
+  }
+  uint16_t *qkv_d = NULL, *out_d = NULL;
+  if (dev_rows) {
+    CHECK_CUDA(cudaMalloc((void**)&qkv_d, LAYERS * qkv_w * 2));
+    CHECK_CUDA(cudaMalloc((void**)&out_d, LAYERS * out_w * 2));
+  }
+  uint16_t* qkv_k = dev_rows ? qkv_d : qkv_h; /* the rows the kernel reads and writes */
+  uint16_t* out_k = dev_rows ? out_d : out_h;
 
   p2p_decode_layer* layers = (p2p_decode_layer*)malloc(sizeof(p2p_decode_layer) * copies * LAYERS);
   for (int c = 0; c < copies; ++c)
     for (int l = 0; l < LAYERS; ++l) {
       p2p_decode_layer* L = &layers[c * LAYERS + l];
-      L->qkv = qkv_h + l * qkv_w;
+      L->qkv = qkv_k + l * qkv_w;
       L->norm_w = (const uint16_t*)nw_d + l * 2 * D;
       L->k_cache = p2p_kv_k(kv[c], l);
       L->v_cache = p2p_kv_v(kv[c], l);
-      L->out = out_h + l * out_w;
+      L->out = out_k + l * out_w;
     }
   CHECK_P2P(p2p_meta_write(ctx, (uint32_t)past, 1, 0, stream));
   CHECK_P2P(p2p_sync(ctx, stream));
+
+#define STEP(c)                                                                            \
+  do {                                                                                     \
+    if (dev_rows)                                                                          \
+      CHECK_CUDA(cudaMemcpyAsync(qkv_d, qkv_h, LAYERS * qkv_w * 2, cudaMemcpyHostToDevice, \
+                                 (cudaStream_t)stream));                                   \
+    CHECK_P2P(p2p_decode_step(ctx, &prm, LAYERS, &layers[(c) * LAYERS], rope, cap, meta, 0, \
+                              stream));                                                    \
+    if (dev_rows)                                                                          \
+      CHECK_CUDA(cudaMemcpyAsync(out_h, out_d, LAYERS * out_w * 2, cudaMemcpyDeviceToHost, \
+                                 (cudaStream_t)stream));                                   \
+  } while (0)
+  /* warm-up of the plain call (workspace, kernel attributes) before any capture */
+  STEP(0);
+  CHECK_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  cudaGraphExec_t* execs = NULL;
+  if (use_graph) {
+    execs = (cudaGraphExec_t*)calloc((size_t)copies, sizeof(cudaGraphExec_t));
+    for (int c = 0; c < copies; ++c) {
+      cudaGraph_t g;
+      CHECK_CUDA(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal));
+      STEP(c);
+      CHECK_CUDA(cudaStreamEndCapture((cudaStream_t)stream, &g));
+      CHECK_CUDA(cudaGraphInstantiate(&execs[c], g, 0));
+      CHECK_CUDA(cudaGraphDestroy(g));
+    }
+  }
 
   double t0 = 0.0;
   for (int i = 0; i < warmup + steps; ++i) {
     if (i == warmup) t0 = now_s();
     /* the per-token call: the kernel reads qkv rows from and writes out rows to host memory */
-    CHECK_P2P(p2p_decode_step(ctx, &prm, LAYERS, &layers[(i % copies) * LAYERS], rope, cap,
-                              meta, 0, stream));
+    if (use_graph)
+      CHECK_CUDA(cudaGraphLaunch(execs[i % copies], (cudaStream_t)stream));
+    else
+      STEP(i % copies);
     CHECK_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
   }
   const double dt = (now_s() - t0) / steps;
@@ -165,7 +230,16 @@ int main(int argc, char** argv) {
   int finite = 1;
   for (size_t i = 0; i < LAYERS * out_w; ++i) finite &= finite_half(out_h[i]);
 
-  printf("{\"us_per_step\": %.3f, \"h2d_bytes_per_step\": %zu, \"d2h_bytes_per_step\": %zu, "
+  if (execs) {
+    for (int c = 0; c < copies; ++c) cudaGraphExecDestroy(execs[c]);
+    free(execs);
+  }
+  if (dev_rows) {
+    cudaFree(qkv_d);
+    cudaFree(out_d);
+  }
+  printf("{\"sched\": \"%s\", \"graph\": %d, \"rows\": \"%s\", ", sched, use_graph, rows);
+  printf("\"us_per_step\": %.3f, \"h2d_bytes_per_step\": %zu, \"d2h_bytes_per_step\": %zu, "
          "\"steps\": %d, \"warmup\": %d, \"copies\": %d, \"past\": %d, \"outputs_finite\": %s}\n",
          dt * 1e6, (size_t)LAYERS * qkv_w * 2, (size_t)LAYERS * out_w * 2, steps, warmup,
          copies, past, finite ? "true" : "false");
