@@ -490,11 +490,29 @@ def run_prefill_projections(ctx, steps, warmup, s=2048, sets=12, check=True):
     def oproj_resident(i):
         ctx.gemm_f16w(resident[i % sets][1], xs[(i + 1) % sets], y)
 
+    def gemm_only_resident(i):  # the same projection without the QK_PREP epilogue
+        ctx.gemm_f16w(resident[i % sets][0], xs[i % sets], qkv)
+
+    att = torch.zeros((s, HQ * D), device="cuda", dtype=torch.float16)
+
+    def layer_resident(i):  # the prompt chunk's whole attention layer, fused
+        fused_resident(i)
+        ctx.attn(prm, q_r, kc_r, vc_r, att, pos0=0, m_tokens=s)
+        ctx.gemm_f16w(resident[i % sets][1], att, y)
+
+    def layer_reference_order(i):  # three GEMMs, QK_PREP, attention, o_proj (engine.js:202-224)
+        unfused(i)
+        ctx.attn(prm, q_u, kc_u, vc_u, att, pos0=0, m_tokens=s)
+        ctx.gemm_q4(weights[i % sets][3], att, y)
+
     res = {"ms_fused": timed_graph(fused, steps, warmup, 1),
            "ms_unfused": timed_graph(unfused, steps, warmup, 1),
            "ms_oproj": timed_graph(oproj, steps, warmup, 1),
            "ms_fused_resident": timed_graph(fused_resident, steps, warmup, 1),
-           "ms_oproj_resident": timed_graph(oproj_resident, steps, warmup, 1)}
+           "ms_oproj_resident": timed_graph(oproj_resident, steps, warmup, 1),
+           "ms_gemm_only_resident": timed_graph(gemm_only_resident, steps, warmup, 1),
+           "ms_layer_resident": timed_graph(layer_resident, steps, warmup, 1),
+           "ms_layer_reference_order": timed_graph(layer_reference_order, steps, warmup, 1)}
     if check:
         from oracle import pyoracle as O
         fused(0)
@@ -1024,6 +1042,9 @@ def run_only(ctx, args):
                "us_oproj": r["ms_oproj"] * 1e3,
                "us_qkv_fused_resident_f16": r["ms_fused_resident"] * 1e3,
                "us_oproj_resident_f16": r["ms_oproj_resident"] * 1e3,
+               "us_qkv_gemm_only_resident_f16": r["ms_gemm_only_resident"] * 1e3,
+               "us_attention_layer_resident_f16": r["ms_layer_resident"] * 1e3,
+               "us_attention_layer_reference_order": r["ms_layer_reference_order"] * 1e3,
                "tflops_qkv_fused": gemm_flops(args.prefill_s, (HQ + 2 * HKV) * D, HQ * D)
                / (r["ms_fused"] * 1e-3) / 1e12, **({"parity": r["parity"]} if args.check else {})}
     else:
@@ -1268,6 +1289,12 @@ def main():
                         "us_oproj": round(po * 1e3, 2),
                         "us_qkv_fused_resident_f16": round(r["ms_fused_resident"] * 1e3, 2),
                         "us_oproj_resident_f16": round(r["ms_oproj_resident"] * 1e3, 2),
+                        "us_qkv_gemm_only_resident_f16": round(
+                            r["ms_gemm_only_resident"] * 1e3, 2),
+                        "us_attention_layer_resident_f16": round(
+                            r["ms_layer_resident"] * 1e3, 2),
+                        "us_attention_layer_reference_order": round(
+                            r["ms_layer_reference_order"] * 1e3, 2),
                         "tflops_qkv_fused": round(fl_qkv / (pf * 1e-3) / 1e12, 1),
                         "tflops_qkv_fused_resident_f16": round(
                             fl_qkv / (r["ms_fused_resident"] * 1e-3) / 1e12, 1),
