@@ -351,3 +351,24 @@ def test_f16_weight_entry_points_equal_q4(ctx, oracle, m):
     for a, b in zip(*outs):
         assert np.array_equal(bits(a), bits(b))
     assert np.isfinite(outs[1][3].astype(np.float32)).all()
+
+
+def test_f16_weight_entry_points_refuse_bad_buffers(ctx, oracle):
+    """Refusals on the host, before any launch: a k that is not a multiple of 8 (the weight
+    rows would not start on 16-byte boundaries), a misaligned weight pointer and a misaligned
+    f16 copy destination; the output is left untouched."""
+    import ctypes as C
+    import p2p_b200
+    lib, bad = p2p_b200.lib, p2p_b200.P2P_ERR_INVALID_ARG
+    rng = np.random.default_rng(5)
+    x = torch.zeros((64, 2048), dtype=torch.float16, device="cuda")
+    y = torch.ones((64, 256), dtype=torch.float16, device="cuda")
+    w16 = torch.zeros((256 * 2048 + 8,), dtype=torch.float16, device="cuda")
+    assert lib.p2p_gemm_f16w(ctx.h, w16.data_ptr(), 256, 2044, x.data_ptr(), 2048, 64,
+                             y.data_ptr(), 256, 0, None) == bad
+    assert lib.p2p_gemm_f16w(ctx.h, w16.data_ptr() + 2, 256, 2048, x.data_ptr(), 2048, 64,
+                             y.data_ptr(), 256, 0, None) == bad
+    mw = ctx.q4(dev_q4(oracle.random_q4(rng, 64, 256)))
+    assert lib.p2p_q4_to_f16(ctx.h, C.byref(mw), w16.data_ptr() + 2, None) == bad
+    ctx.sync()
+    assert float(y.float().min()) == 1.0  # nothing ran
