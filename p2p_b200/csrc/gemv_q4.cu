@@ -123,11 +123,9 @@ __global__ void __cluster_dims__(kUnitCtas, 1, 1) __launch_bounds__(kThreads)
   grid_dependency_wait();
   const int unit = blockIdx.x / kUnitCtas;
   const int part = blockIdx.x % kUnitCtas;  // rank in the cluster
+  // The position (meta) is needed only once the rows are computed: its load overlaps the
+  // weight loads instead of preceding them.
   const int pos = a.meta ? int(a.meta[0]) : a.pos_host;
-  if (pos < 0 || int64_t(pos) >= a.kv_cap) {  // the same for every CTA: nothing is written
-    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
-    return;
-  }
   stage_x(static_cast<const __half*>(a.x), a.k, xs);
   __syncthreads();
   launch_dependents();
@@ -139,6 +137,24 @@ __global__ void __cluster_dims__(kUnitCtas, 1, 1) __launch_bounds__(kThreads)
   // written into the cluster leader's y_s
   const int row = part * kWarps + warp;
   const float v = row_dot(w, head * D + row, a.k, xs, lane);
+  if (pos < 0 || int64_t(pos) >= a.kv_cap) {  // the same for every CTA: nothing is written
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
+    return;
+  }
+  // the leader's epilogue warp fetches the position's rope row and the norm weights while the
+  // cluster gathers the rows
+  const bool epi = part == 0 && warp == 0 && kind != 2;
+  const __half* nw = static_cast<const __half*>(a.norm_w);
+  float cs = 0.f, sn = 0.f, w0 = 0.f, w1 = 0.f;
+  if (epi) {
+    const __half* rope = static_cast<const __half*>(a.rope) + int64_t(pos) * D;
+    cs = __half2float(rope[lane]);
+    sn = __half2float(rope[32 + lane]);
+    if (nw) {
+      w0 = __half2float(nw[(kind == 1 ? D : 0) + lane]);
+      w1 = __half2float(nw[(kind == 1 ? D : 0) + lane + 32]);
+    }
+  }
   cluster_sync_all();  // every CTA of the cluster is running: its shared memory is mapped
   if (lane == 0) {
     float* dst = map_cluster_rank(&y_s[row], 0);
@@ -153,12 +169,9 @@ __global__ void __cluster_dims__(kUnitCtas, 1, 1) __launch_bounds__(kThreads)
     vc[lane + 32] = __float2half_rn(y_s[lane + 32]);
     return;
   }
-  const __half* rope = static_cast<const __half*>(a.rope) + int64_t(pos) * D;
-  const float cs = __half2float(rope[lane]), sn = __half2float(rope[32 + lane]);
-  const __half* nw = static_cast<const __half*>(a.norm_w);
   float r0, r1;  // QK_PREP q / k unit (kernels.js:244-264)
-  norm_rope_head<__half>(y_s[lane], y_s[lane + 32], nw ? nw + (kind == 1 ? D : 0) : nullptr,
-                         nw != nullptr, a.eps, cs, sn, r0, r1);
+  norm_rope_vals<__half>(y_s[lane], y_s[lane + 32], w0, w1, nw != nullptr, a.eps, cs, sn, r0,
+                         r1);
   __half* dst = kind == 0 ? static_cast<__half*>(a.q_out) + int64_t(head) * D
                           : static_cast<__half*>(a.k_cache) + crow;
   dst[lane] = __float2half_rn(r0);
