@@ -613,11 +613,10 @@ cudaError_t launch_gemm_bn(const GemmArgs& a, int sms, cudaStream_t stream) {
   p.tiles_n = int32_t(tiles_n);
   p.tiles = int32_t(tiles);
   const size_t smem = sizeof(GemmSmem<BN, false>) + 1024;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(gemm_kernel<BN>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  static PerDeviceOnce attrs;
+  const cudaError_t attr_err = per_device_once(attrs, [&](int&) {
+    return cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(smem));
   });
   if (attr_err != cudaSuccess) return attr_err;
   // persistent: one CTA per SM (the shared ring admits no second), tiles strided over them
@@ -666,15 +665,15 @@ cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream) {
   cfg.numAttrs = 1;
   // persistent: as many pairs as can be resident at once (the SM pairs of the TPCs), tiles
   // strided over them
-  static std::once_flag once;
-  static cudaError_t setup_err = cudaSuccess;
-  static int max_pairs = 0;
-  std::call_once(once, [&] {
-    setup_err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (setup_err != cudaSuccess) return;
+  static PerDeviceOnce setup;
+  int max_pairs = 0;
+  const cudaError_t setup_err = per_device_once(setup, [&](int& pairs) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem));
+    if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(2);
-    setup_err = cudaOccupancyMaxActiveClusters(&max_pairs, fn, &cfg);
-  });
+    return cudaOccupancyMaxActiveClusters(&pairs, fn, &cfg);
+  }, &max_pairs);
   if (setup_err != cudaSuccess) return setup_err;
   if (max_pairs <= 0) return cudaErrorInvalidConfiguration;
   cfg.gridDim = dim3(unsigned(2 * std::min<int64_t>(tiles, max_pairs)));

@@ -1,11 +1,38 @@
 // kernels.h -- host-side launchers of the sm_100a kernels (internal to libp2pattn.so).
 #pragma once
 
+#include <mutex>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace p2p {
+
+// Kernel attributes (dynamic shared-memory size, carveout) belong to each device's context: a
+// launcher sets them once per device, with that device current.  `setup(value)` runs on the
+// first call for the current device; its status (and an int it may record, such as a count of
+// resident clusters) is returned on every later call for that device.
+constexpr int kMaxDevicesPerProcess = 64;
+struct PerDeviceOnce {
+  std::mutex mu;
+  bool done[kMaxDevicesPerProcess] = {};
+  cudaError_t err[kMaxDevicesPerProcess] = {};
+  int value[kMaxDevicesPerProcess] = {};
+};
+template <class F>
+cudaError_t per_device_once(PerDeviceOnce& st, F&& setup, int* value = nullptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevicesPerProcess) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(st.mu);
+  if (!st.done[dev]) {
+    st.err[dev] = setup(st.value[dev]);
+    st.done[dev] = true;
+  }
+  if (value) *value = st.value[dev];
+  return st.err[dev];
+}
 
 // ---- qk_prep.cu -----------------------------------------------------------------------------
 struct QkPrepArgs {

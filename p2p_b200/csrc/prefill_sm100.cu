@@ -560,15 +560,15 @@ cudaError_t launch_nt(FlashParams& p, CUtensorMap& tq, CUtensorMap& tk, CUtensor
                       dim3 grid, cudaStream_t stream) {
   // NT = 2 pads its shared memory to a 1024-byte boundary; NT = 1 must fit twice per SM
   const size_t smem = sizeof(SmemT<NT, Cfg<NT>::kStages>) + (NT == 2 ? 1024 : 0);
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(flash_fwd_kernel<NT>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(flash_fwd_kernel<NT>,
-                                      cudaFuncAttributePreferredSharedMemoryCarveout,
-                                      int(cudaSharedmemCarveoutMaxShared));
+  static PerDeviceOnce attrs;
+  const cudaError_t attr_err = per_device_once(attrs, [&](int&) {
+    cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(flash_fwd_kernel<NT>,
+                               cudaFuncAttributePreferredSharedMemoryCarveout,
+                               int(cudaSharedmemCarveoutMaxShared));
+    return e;
   });
   if (attr_err != cudaSuccess) return attr_err;
   void* args[] = {&tq, &tk, &tv, &p};

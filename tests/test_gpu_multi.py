@@ -5,6 +5,10 @@ Two NCCL ranks, one process per GPU, rendezvous on 127.0.0.1:
     the library, through the C ABI) vs the oracle on the full heads, and
     the same with the flash kernel scattering its rows into every rank's output (CUDA IPC);
   * ragged decode split by sequence (LPT by tokens, no collective) vs the oracle.
+
+And one process driving two GPUs through two contexts: the kernels whose launch sets
+per-device attributes (flash attention, the prompt-chunk GEMM in both tile forms) give the same
+bits on the second device as on the first.
 """
 import os
 import socket
@@ -146,3 +150,41 @@ def test_two_gpu_prefill_heads_and_ragged_sequences():
         assert p.exitcode == 0
     for rank, ok in results.items():
         assert all(ok.values()), (rank, ok)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_two_devices_in_one_process(oracle):
+    import p2p_b200
+    rng = np.random.default_rng(8)
+    hq, hkv, s_tok, k, n = 32, 8, 512, 1024, 3072
+    q = (0.5 * rng.standard_normal((s_tok, hq * D))).astype(np.float16)
+    kc = (0.5 * rng.standard_normal((s_tok, hkv, D))).astype(np.float16)
+    vc = rng.standard_normal((s_tok, hkv, D)).astype(np.float16)
+    wq, sc, zp = oracle.random_q4(rng, n, k)
+    x = rng.standard_normal((s_tok, k)).astype(np.float16)
+    outs = []
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            ctx = p2p_b200.Context(dev)
+            try:
+                t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(f"cuda:{dev}")
+                out = torch.zeros((s_tok, hq * D), dtype=torch.float16, device=f"cuda:{dev}")
+                ctx.attn(p2p_b200.Params(hq, hkv), t(q), t(kc), t(vc), out, pos0=0,
+                         m_tokens=s_tok)
+                w = (t(wq.view(np.int32)), t(sc), t(zp.view(np.int32)))
+                ys = []
+                for pair in ("0", "1"):  # single-CTA and 2-CTA tiles
+                    os.environ["P2P_GEMM_PAIR"] = pair
+                    y = torch.zeros((s_tok, n), dtype=torch.float16, device=f"cuda:{dev}")
+                    ctx.gemm_q4(w, t(x), y)
+                    ys.append(y)
+                os.environ.pop("P2P_GEMM_PAIR", None)
+                ctx.sync()
+                outs.append([o.cpu().numpy().view(np.uint16) for o in [out] + ys])
+            finally:
+                os.environ.pop("P2P_GEMM_PAIR", None)
+                ctx.close()
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
+    assert np.isfinite(outs[0][0].view(np.float16).astype(np.float32)).all()
