@@ -331,7 +331,8 @@ p2p_status p2p_qkv_gemv_prep(p2p_ctx* ctx, const p2p_attn_params* prm, const voi
  * on the tensor cores with f32 accumulation, so results agree with the shader to f16 rounding,
  * not bit for bit.  No k limit; n a multiple of 64; x and y rows 16-byte aligned (ld_x, ld_y
  * and y_off multiples of 8).  The workspace is shared by the context's calls: calls on
- * different streams of one context must not overlap. */
+ * different streams of one context must not overlap.  It grows (synchronising the device) on
+ * the first call with a larger matrix: make that call before capturing a CUDA graph. */
 p2p_status p2p_gemm_q4(p2p_ctx* ctx, const p2p_q4_matrix* w, const void* x, int64_t ld_x,
                        int32_t m_tokens, void* y, int64_t ld_y, int64_t y_off, void* stream);
 
