@@ -32,18 +32,56 @@ namespace {
 constexpr int kThreads = 512;  // 16 warps
 constexpr int kWarps = kThreads / 32;
 
-// Barrier over the CTAs of the thread-block cluster (release / acquire of shared memory).
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
+// Arrive on the cluster barrier now (relaxed: the leader's barrier init is released by its own
+// fence) and wait for every CTA's arrival later, just before the first remote store.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
-// Generic address of `p` (a shared-memory variable) in the cluster CTA of rank `rank`.
-template <class T>
-__device__ __forceinline__ T* map_cluster_rank(T* p, unsigned rank) {
-  T* r;
-  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(p), "r"(rank));
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t smem_u32addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32addr(p)),
+               "r"(rank));
   return r;
 }
+// One f32 into a cluster CTA's shared memory, counted (4 bytes) on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_f32(uint32_t dst, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(
+                   dst),
+               "f"(v), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void rows_bar_init(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32addr(bar)));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_u32addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool rows_bar_try_wait(uint64_t* bar) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32addr(bar))
+      : "memory");
+  return ok != 0;
+}
+constexpr uint64_t kRowsWaitNs = 1000000000ull;
+__device__ __forceinline__ uint64_t globaltimer_ns_() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 
 // One output row as the shader's 32-lane subgroup computes it (kernels.js:44-66); the row's
 // value ends in lane 0.  The words of a lane are fetched 8 at a time (all loads of a batch in
@@ -111,7 +149,8 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const __grid_constant
 }
 
 // One head unit per cluster of kUnitCtas CTAs: CTA r computes rows 16r..16r+15 of the head
-// (one per warp) and stores them in the first CTA's shared memory, which runs the epilogue.
+// (one per warp) and pushes them into the first CTA's shared memory (st.async, counted on its
+// mbarrier), whose epilogue warp alone waits for them; the other CTAs never wait on a peer.
 constexpr int kUnitCtas = 4;
 
 __global__ void __cluster_dims__(kUnitCtas, 1, 1) __launch_bounds__(kThreads)
@@ -120,9 +159,12 @@ __global__ void __cluster_dims__(kUnitCtas, 1, 1) __launch_bounds__(kThreads)
   static_assert(D == kUnitCtas * kWarps, "one row per warp");
   __shared__ __align__(16) __half xs[kGemvMaxK];
   __shared__ float y_s[D];
+  __shared__ uint64_t rows_bar;
   grid_dependency_wait();
   const int unit = blockIdx.x / kUnitCtas;
   const int part = blockIdx.x % kUnitCtas;  // rank in the cluster
+  if (part == 0 && threadIdx.x == 0) rows_bar_init(&rows_bar, uint32_t(D * sizeof(float)));
+  cluster_arrive_relaxed();
   // The position (meta) is needed only once the rows are computed: its load overlaps the
   // weight loads instead of preceding them.
   const int pos = a.meta ? int(a.meta[0]) : a.pos_host;
@@ -137,13 +179,18 @@ __global__ void __cluster_dims__(kUnitCtas, 1, 1) __launch_bounds__(kThreads)
   // written into the cluster leader's y_s
   const int row = part * kWarps + warp;
   const float v = row_dot(w, head * D + row, a.k, xs, lane);
+  cluster_wait();  // every CTA has arrived: the leader's rows_bar is initialised
   if (pos < 0 || int64_t(pos) >= a.kv_cap) {  // the same for every CTA: nothing is written
     if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.err, kErrPosBeyondCache);
     return;
   }
+  if (lane == 0)
+    st_async_f32(cluster_addr(&y_s[row], 0), __half2float(__float2half_rn(v)),
+                 cluster_addr(&rows_bar, 0));
+  if (part != 0 || warp != 0) return;
   // the leader's epilogue warp fetches the position's rope row and the norm weights while the
   // cluster gathers the rows
-  const bool epi = part == 0 && warp == 0 && kind != 2;
+  const bool epi = kind != 2;  // (only the leader's warp 0 reaches here)
   const __half* nw = static_cast<const __half*>(a.norm_w);
   float cs = 0.f, sn = 0.f, w0 = 0.f, w1 = 0.f;
   if (epi) {
@@ -155,13 +202,18 @@ __global__ void __cluster_dims__(kUnitCtas, 1, 1) __launch_bounds__(kThreads)
       w1 = __half2float(nw[(kind == 1 ? D : 0) + lane + 32]);
     }
   }
-  cluster_sync_all();  // every CTA of the cluster is running: its shared memory is mapped
-  if (lane == 0) {
-    float* dst = map_cluster_rank(&y_s[row], 0);
-    *dst = __half2float(__float2half_rn(v));
+  // the 64 rows of the unit: every lane waits (its own acquire orders its reads of y_s), bounded;
+  // a peer that never delivers is reported and nothing is written
+  bool got = rows_bar_try_wait(&rows_bar);
+  if (!got) {
+    const uint64_t t0 = globaltimer_ns_();
+    while (!(got = rows_bar_try_wait(&rows_bar)) && globaltimer_ns_() - t0 < kRowsWaitNs) {
+    }
   }
-  cluster_sync_all();  // the leader's y_s is complete
-  if (part != 0 || warp != 0) return;
+  if (!__all_sync(0xffffffffu, got)) {
+    if (lane == 0) atomicOr(a.err, kErrTimeout);
+    return;
+  }
   const int64_t crow = (int64_t(pos) * a.hkv + head) * D;  // cache row `pos`, kv head `head`
   if (kind == 2) {  // QK_PREP v unit (kernels.js:237-241): raw copy
     __half* vc = static_cast<__half*>(a.v_cache) + crow;
