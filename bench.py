@@ -438,6 +438,36 @@ def gemm_flops(m, n, k):
     return 2.0 * m * n * k
 
 
+def run_qkv_gemm_calls(ctx, s, calls, resident):
+    """`calls` direct calls of one LFM2.5-1.2B layer's fused q/k/v projection + QK_PREP over an
+    s-token chunk (4-bit weights dequantised per call, or resident f16 copies): the command the
+    profiler wraps for the GEMM kernels."""
+    import torch
+    import p2p_b200
+    k = HQ * D
+    g = torch.Generator(device="cuda").manual_seed(77)
+    ws = [q4_weights(g, n, k) for n in (HQ * D, HKV * D, HKV * D)]
+    w16 = torch.cat([ctx.q4_to_f16(w) for w in ws]) if resident else None
+    x = torch.randn((s, k), generator=g, device="cuda").half()
+    nw = torch.ones((2 * D,), device="cuda", dtype=torch.float16)
+    rope = ctx.rope_table(s, D, 1e6)
+    prm = p2p_b200.Params(HQ, HKV)
+    q = torch.zeros((s, HQ * D), device="cuda", dtype=torch.float16)
+    kc = torch.zeros((s, HKV, D), device="cuda", dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(calls):
+        if resident:
+            ctx.qkv_gemm_prep_f16w(prm, x, w16, nw, rope, q, kc, vc, pos0=0)
+        else:
+            ctx.qkv_gemm_prep(prm, x, *ws, nw, rope, q, kc, vc, pos0=0)
+    end.record()
+    ctx.sync()
+    return {"chunk": s, "calls": calls, "resident_f16": bool(resident),
+            "us_per_call_direct_launch": start.elapsed_time(end) * 1e3 / max(calls, 1)}
+
+
 def run_prefill_projections(ctx, steps, warmup, s=2048, sets=12, check=True):
     """The 4-bit projections around the attention of an s-token prompt chunk of one LFM2.5-1.2B
     layer (hidden 2048, 32q/8kv): the q/k/v projections with QK_PREP in the GEMM's epilogue
@@ -1035,6 +1065,8 @@ def run_only(ctx, args):
         fl = prefill_flops(args.prefill_s)
         res = {"us_attn": r["ms_attn"] * 1e3, "tflops_attn": fl / (r["ms_attn"] * 1e-3) / 1e12,
                "us_prep_plus_attn": r["ms_both"] * 1e3}
+    elif args.only == "qkvgemm":
+        res = run_qkv_gemm_calls(ctx, args.prefill_s, args.steps, args.resident)
     elif args.only == "projections":
         r = run_prefill_projections(ctx, args.steps, args.warmup, s=args.prefill_s,
                                     check=args.check)
@@ -1062,10 +1094,12 @@ def main():
     ap.add_argument("--no-side", action="store_true", help="skip prefill/vision/ragged legs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--only", choices=["decode", "decode1", "ragged", "prefill", "vision", "block",
-                                       "projections"],
+                                       "projections", "qkvgemm"],
                     help="run one leg on one GPU and print its timing (profiling commands)")
     ap.add_argument("--past", type=int, default=PAST, help="decode context for --only decode")
     ap.add_argument("--prefill-s", type=int, default=2048, help="prompt length for --only prefill")
+    ap.add_argument("--resident", action="store_true",
+                    help="with --only qkvgemm: resident f16 weights instead of 4-bit per call")
     ap.add_argument("--check", action="store_true",
                     help="with --only projections: also run the leg's output checks")
     ap.add_argument("--kv", default="f16", choices=["f16", "int8", "paged"],
